@@ -1,0 +1,442 @@
+#!/usr/bin/env python
+"""Throughput of the speculative-decoding step on B200.
+
+Workload (the configuration the headline metric -- accepted tok/s per B200
+at gamma=4 -- is quoted on): a Llama-style 1.1B bf16 target (d_model 2048,
+22 layers, 32 query / 4 KV heads, SwiGLU 5632, vocab 32000, RoPE 1e4) with
+a 2-layer draft of the same width, random-init weights (std 0.02); 256
+requests per GPU with contexts uniform in [512, 2048] (token ids uniform
+over the vocabulary, K/V pools filled with synthetic values), paged block
+16, gamma = 4, temperature 0.8, top-p 0.9.  One step = one speculative
+round over all requests (4 draft passes, one 5-token verify pass, fused
+accept/resample, rollback).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+For N > 1 run under torchrun (one process per GPU); each rank serves its own
+256 requests (weak scaling), there is no collective in the decode loop, and
+the end-of-run counters are reduced over NCCL (SUM of tokens, MAX of time).
+
+Reported: ``value`` = emitted tokens of all ranks / max over ranks of the
+summed device time of the rounds' kernels (metadata already on the device);
+``e2e`` = the same tokens / the time of the public ``SpeculativeDecoder.step``
+calls including host bookkeeping, the pinned host->device metadata copy and
+the device->host copy of the accepted tokens.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "accepted tok/s per B200 (spec γ=4)"
+WORKLOAD = "llama-1.1b-bf16 target + 2-layer draft, 256 req/GPU, ctx U[512,2048], gamma 4, T 0.8, top-p 0.9"
+
+TARGET = dict(vocab_size=32000, n_layers=22, d_model=2048, n_heads=32, n_kv_heads=4, d_ff=5632,
+              rope_theta=10000.0)
+DRAFT = dict(TARGET, n_layers=2)
+GAMMA = 4
+BLOCK = 16
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--requests", type=int, default=256, help="requests per GPU")
+    ap.add_argument("--ctx-min", type=int, default=512)
+    ap.add_argument("--ctx-max", type=int, default=2048)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-requests", type=int, default=2, help="CPU sample: requests per round")
+    ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
+    return ap.parse_args()
+
+
+def model_cfgs(small: bool):
+    from microserve_b200.config import ModelConfig
+
+    t, d = dict(TARGET), dict(DRAFT)
+    if small:
+        t.update(n_layers=2)
+        d.update(n_layers=1)
+    msl = 4096
+    return (ModelConfig(**t, max_seq_len=msl, dtype="bfloat16"),
+            ModelConfig(**d, max_seq_len=msl, dtype="bfloat16"))
+
+
+def contexts(n: int, lo: int, hi: int, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+
+
+# -- clocks during the timed region ------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int) -> None:
+        self.gpu = gpu_index
+        self.proc: subprocess.Popen | None = None
+        self.path = Path(tempfile.mkstemp(suffix=".csv")[1])
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict[str, object] | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = [r.split(",") for r in self.path.read_text().splitlines() if r.strip()]
+        self.path.unlink(missing_ok=True)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": max(smax), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# -- GPU arm -----------------------------------------------------------------------
+def gemm_flops_per_round(shape: dict[str, int], tcfg, dcfg) -> float:
+    """2*M*N*K over every GEMM launch of one round (the algorithmic FLOPs)."""
+
+    def per_pass(cfg, m: int, rows: int) -> float:
+        d, hq, hkv, dh, ff = cfg.d_model, cfg.n_heads, cfg.kv_heads, cfg.d_head, cfg.ffn_hidden
+        # qkv, o_proj, gate+up, down
+        layer = 2 * m * (d * (hq + 2 * hkv) * dh + hq * dh * d + d * 2 * ff + ff * d)
+        return cfg.n_layers * layer + 2 * rows * d * cfg.vocab_size
+
+    B, G = shape["B"], shape["gamma"]
+    draft = per_pass(dcfg, shape["T0"], B) + (G - 1) * per_pass(dcfg, B, B)
+    return draft + per_pass(tcfg, shape["Tv"], B * (G + 1))
+
+
+def run_gpu(args: argparse.Namespace) -> None:
+    import torch
+
+    from microserve_b200 import _lib, distributed
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import CacheConfig, SamplingConfig
+    from microserve_b200.model import Transformer
+    from microserve_b200.scheduler import Request
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    info = distributed.init("nccl", timeout_s=300.0) if args.gpus > 1 else distributed.rank_info()
+    dev = torch.device("cuda", info.local_rank)
+    torch.cuda.set_device(dev)
+    _lib.load()
+    tcfg, dcfg = model_cfgs(args.small)
+    target = Transformer(tcfg, dev, seed=args.seed)
+    draft = Transformer(dcfg, dev, seed=args.seed + 1)
+
+    B = args.requests
+    rng_seed = args.seed * 1000 + info.rank
+    ctx = contexts(B, args.ctx_min, args.ctx_max, rng_seed)
+    rounds_total = args.warmup + args.steps
+    per_req_blocks = (ctx + rounds_total * (GAMMA + 1) + 2 * BLOCK) // BLOCK + 1
+    nblocks = int(per_req_blocks.sum()) + 64
+    ccfg = CacheConfig(BLOCK, nblocks, "bfloat16")
+    tcache = PagedKVCache(tcfg, ccfg, dev)
+    dec = SpeculativeDecoder(target, draft, ccfg, gamma=GAMMA, device=dev)
+    # interleave block allocation across requests (non-contiguous tables)
+    tok_rng = np.random.default_rng(rng_seed + 7)
+    sc = SamplingConfig(temperature=0.8, top_p=0.9, max_new_tokens=1 << 30)
+    reqs, gens = [], {}
+    for i in range(B):
+        prompt = tok_rng.integers(0, tcfg.vocab_size, int(ctx[i])).tolist()
+        r = Request(i, prompt, sc)
+        r.num_computed = len(prompt) - 1
+        reqs.append(r)
+        gens[i] = torch.Generator().manual_seed(rng_seed * 100003 + i)
+    remaining = (ctx - 1).copy()
+    while remaining.max() > 0:
+        step = np.minimum(remaining, BLOCK)
+        live = [i for i in range(B) if step[i] > 0]
+        tcache.append_many(live, step[live])
+        dec.draft_cache.append_many(live, step[live])
+        remaining -= step
+    g = torch.Generator(device=dev).manual_seed(rng_seed)
+    for pool in (tcache.pool, dec.draft_cache.pool):
+        for lyr in range(pool.shape[1]):
+            pool[:, lyr].normal_(generator=g)
+    torch.cuda.synchronize()
+
+    def one_round() -> int:
+        out = dec.step(reqs, tcache, gens)
+        n = 0
+        for r, toks in zip(reqs, out, strict=True):
+            r.output_ids.extend(toks)
+            n += len(toks)
+        return n
+
+    for _ in range(args.warmup):
+        one_round()
+    acc0, prop0 = dec.num_accepted, dec.num_proposed
+    dec.round_events = []
+    launches0 = _lib.launch_count()
+    clocks = ClockSampler(info.local_rank) if info.rank == 0 else None
+    distributed.barrier()
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.start()
+    _lib.call("ms_profile_start", 1)  # GEMM: the dominant kernel class
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    emitted = 0
+    flops = 0.0
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        emitted += one_round()
+        flops += gemm_flops_per_round(dec.last_round_shape, tcfg, dcfg)
+        h2d += dec.last_h2d_bytes
+        d2h += dec.last_d2h_bytes
+    end.record()
+    torch.cuda.synchronize()
+    gemm_ms = _c_double()
+    gemm_n = _c_int64()
+    _lib.call("ms_profile_stop", _byref(gemm_ms), _byref(gemm_n))
+    distributed.barrier()
+    clk = clocks.stop() if clocks else None
+    e2e_ms = start.elapsed_time(end)
+    dev_ms = sum(a.elapsed_time(b) for a, b in dec.round_events)
+    launches = _lib.launch_count() - launches0
+    counters = {"emitted": emitted, "accepted": dec.num_accepted - acc0,
+                "proposed": dec.num_proposed - prop0}
+    tot, dev_ms_max = distributed.reduce_stats(counters, dev_ms / 1e3)
+    _, e2e_s_max = distributed.reduce_stats({}, e2e_ms / 1e3)
+    if info.rank != 0:
+        distributed.shutdown()
+        return
+
+    peaks = _peaks()
+    achieved = flops / (gemm_ms.value / 1e3) / 1e12 if gemm_ms.value > 0 else 0.0
+    line = {
+        "metric": METRIC,
+        "value": tot["emitted"] / dev_ms_max,
+        "unit": "tok/s",
+        "n_gpus": info.world_size,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms_max * 1e3 / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random-init weights, uniform token ids, synthetic K/V contexts)",
+        "config": {
+            "workload": WORKLOAD if not args.small else WORKLOAD + " [small: 2+1 layers]",
+            "requests_per_gpu": B, "gamma": GAMMA, "block_size": BLOCK,
+            "ctx_range": [args.ctx_min, args.ctx_max],
+            "target": TARGET if not args.small else dict(TARGET, n_layers=2),
+            "draft_layers": dcfg.n_layers, "temperature": 0.8, "top_p": 0.9,
+            "l2": "inputs larger than L2 (2.1 GB target weights + ~7 GB of K/V read per round)",
+            "parallelism": f"request-sharded x{info.world_size}, no decode-loop collective",
+        },
+        "acceptance_rate": tot["accepted"] / max(1, tot["proposed"]),
+        "emitted_tokens": tot["emitted"],
+        "verify_step_us": None,
+        "e2e": {
+            "value": tot["emitted"] / e2e_s_max,
+            "unit": "tok/s",
+            "h2d_bytes_per_step": h2d // args.steps,
+            "d2h_bytes_per_step": d2h // args.steps,
+            "ms_per_step": e2e_s_max * 1e3 / args.steps,
+        },
+        "gpu_launches": int(launches),
+        "roofline": {
+            "kernel": "GEMM (all projection and lm_head launches)",
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peaks["bf16_sustained"],
+            "unit": "TFLOP/s",
+            "frac": achieved / peaks["bf16_sustained"],
+            "peak_source": peaks["source"],
+            "traffic": None,
+            "launches": int(gemm_n.value),
+            "device_ms": gemm_ms.value,
+        },
+        "clocks": clk,
+    }
+    if not args.no_cpu_baseline and info.world_size == 1:
+        line["cpu_baseline"] = cpu_baseline(args, rounds=args.cpu_rounds)
+    print(json.dumps(line), flush=True)
+    distributed.shutdown()
+
+
+def _c_double():
+    import ctypes
+
+    return ctypes.c_double(0.0)
+
+
+def _c_int64():
+    import ctypes
+
+    return ctypes.c_int64(0)
+
+
+def _byref(x):
+    import ctypes
+
+    return ctypes.byref(x)
+
+
+def _peaks() -> dict[str, object]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"],
+                "bf16_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+# -- CPU side (the oracle restatement of the reference path) ----------------------------
+def cpu_workload(args: argparse.Namespace, n_req: int, seed: int):
+    """Host-generated random weights of the same architecture and a sample of
+    requests with synthetic K/V histories (float32, the reference's dtype)."""
+    from oracle.model import Dims, OracleModel, SeqKV
+    from oracle.spec import OracleRequest
+
+    rng = np.random.default_rng(seed)
+
+    def state(cfg: dict) -> dict[str, np.ndarray]:
+        d, hq, hkv, ff, L = cfg["d_model"], cfg["n_heads"], cfg["n_kv_heads"], cfg["d_ff"], cfg["n_layers"]
+        dh = d // hq
+        res = 0.02 / np.sqrt(2 * L)
+        n = lambda *s, std=0.02: rng.standard_normal(s, dtype=np.float32) * np.float32(std)  # noqa: E731
+        st = {"embed.weight": n(cfg["vocab_size"], d), "norm.weight": np.ones(d, np.float32)}
+        for i in range(L):
+            p = f"blocks.{i}."
+            st[p + "attn.q_proj.weight"] = n(hq * dh, d)
+            st[p + "attn.k_proj.weight"] = n(hkv * dh, d)
+            st[p + "attn.v_proj.weight"] = n(hkv * dh, d)
+            st[p + "attn.o_proj.weight"] = n(d, hq * dh, std=res)
+            st[p + "ffn.gate_proj.weight"] = n(ff, d)
+            st[p + "ffn.up_proj.weight"] = n(ff, d)
+            st[p + "ffn.down_proj.weight"] = n(d, ff, std=res)
+            st[p + "attn_norm.weight"] = np.ones(d, np.float32)
+            st[p + "ffn_norm.weight"] = np.ones(d, np.float32)
+        return st
+
+    t = dict(TARGET)
+    dr = dict(DRAFT)
+    if args.small:
+        t.update(n_layers=2)
+        dr.update(n_layers=1)
+    dims = lambda c: Dims(c["vocab_size"], c["d_model"], c["n_layers"], c["n_heads"],  # noqa: E731
+                          c["n_kv_heads"], c["d_ff"], 4096, c["rope_theta"])
+    target = OracleModel(dims(t), state(t))
+    draft = OracleModel(dims(dr), state(dr))
+    ctx = contexts(n_req, args.ctx_min, args.ctx_max, seed + 1)
+    reqs = []
+    for i in range(n_req):
+        prompt = rng.integers(0, t["vocab_size"], int(ctx[i])).tolist()
+        r = OracleRequest(i, prompt, 0.8, None, 0.9, seed=seed * 7 + i)
+        dh = t["d_model"] // t["n_heads"]
+        for kv, cfg in ((r.target_kv, t), (r.draft_kv, dr)):
+            shape = (int(ctx[i]) - 1, cfg["n_kv_heads"], dh)
+            kv.k = [rng.standard_normal(shape, dtype=np.float32) for _ in range(cfg["n_layers"])]
+            kv.v = [rng.standard_normal(shape, dtype=np.float32) for _ in range(cfg["n_layers"])]
+        reqs.append(r)
+    _ = SeqKV
+    return target, draft, reqs
+
+
+def cpu_rounds(target, draft, reqs, rounds: int) -> tuple[int, float]:
+    from oracle.spec import spec_round
+
+    emitted = 0
+    t0 = time.perf_counter()
+    for _ in range(rounds):
+        tr = spec_round(target, draft, GAMMA, reqs)
+        for r, toks in zip(reqs, tr.emitted, strict=True):
+            r.output_ids.extend(toks)
+            emitted += len(toks)
+    return emitted, time.perf_counter() - t0
+
+
+def cpu_baseline(args: argparse.Namespace, rounds: int) -> dict[str, object]:
+    target, draft, reqs = cpu_workload(args, args.cpu_requests, args.seed + 99)
+    emitted, secs = cpu_rounds(target, draft, reqs, rounds)
+    return {
+        "value": emitted / secs,
+        "unit": "tok/s",
+        "cores": os.cpu_count(),
+        "kind": "port",
+        "sample": f"{args.cpu_requests} requests x {rounds} rounds of the same workload, "
+                  f"numpy float32 oracle (multithreaded BLAS), {secs:.1f} s",
+    }
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    """The reference's CPU path (its numpy restatement) on this host's cores."""
+    info_rank = int(os.environ.get("RANK", "0"))
+    if info_rank != 0:
+        return
+    target, draft, reqs = cpu_workload(args, args.cpu_requests, args.seed + 99)
+    from oracle.spec import spec_round
+
+    for _ in range(args.warmup):
+        spec_round(target, draft, GAMMA, reqs)
+    emitted, secs = cpu_rounds(target, draft, reqs, args.steps)
+    value = emitted / secs
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "sample_requests_per_step": args.cpu_requests},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"{args.cpu_requests} requests per step, numpy float32 "
+                                   "restatement of the reference path"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,303 @@
+// Per-token kernels of the paged forward: embedding + RMSNorm, RMSNorm,
+// RoPE with the K/V cache write, and the cache write/gather used by the
+// PagedKVCache API.
+//
+// Pool layout per layer: [num_blocks][n_kv_heads][block_size][d_head], so one
+// (block, kv head) tile of block_size x d_head is contiguous in HBM.
+#include "common.cuh"
+#include "model_kernels.cuh"
+
+namespace ms {
+namespace {
+
+// One warp per row.  y = x * (1/sqrt(mean(x^2) + eps)) * w, float32 math
+// (reference model.py:77-79).
+template <typename TY>
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               TY* __restrict__ y, const int32_t* __restrict__ row_idx, int n_rows,
+                               int dim, float eps) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_rows) return;
+  const int src = row_idx ? row_idx[warp] : warp;
+  const float* xr = x + (int64_t)src * dim;
+  float ss = 0.f;
+  for (int i = lane; i < dim; i += 32) {
+    const float v = xr[i];
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = 1.f / sqrtf(ss / (float)dim + eps);
+  TY* yr = y + (int64_t)warp * dim;
+  for (int i = lane; i < dim; i += 32) yr[i] = from_f<TY>(xr[i] * r * w[i]);
+}
+
+// x[t] = embed[ids[t]] (float32 residual stream), y[t] = rmsnorm(x[t]) * w.
+template <typename TW>
+__global__ void embed_rmsnorm_kernel(const TW* __restrict__ embed, const int32_t* __restrict__ ids,
+                                     int n_tokens, int vocab, int dim, const float* __restrict__ w,
+                                     float eps, float* __restrict__ x, TW* __restrict__ y,
+                                     int* __restrict__ err) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= n_tokens) return;
+  int id = ids[warp];
+  if (id < 0 || id >= vocab) {
+    if (lane == 0) raise_device_error(err, kErrToken);
+    id = 0;
+  }
+  const TW* er = embed + (int64_t)id * dim;
+  float* xr = x + (int64_t)warp * dim;
+  float ss = 0.f;
+  for (int i = lane; i < dim; i += 32) {
+    const float v = to_f(er[i]);
+    xr[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  const float r = 1.f / sqrtf(ss / (float)dim + eps);
+  TW* yr = y + (int64_t)warp * dim;
+  for (int i = lane; i < dim; i += 32) yr[i] = from_f<TW>(to_f(er[i]) * r * w[i]);
+}
+
+__device__ __forceinline__ int64_t pool_offset(int slot, int g, int d, int bs, int hkv, int dh,
+                                               int num_blocks, bool& ok) {
+  const int blk = slot / bs, off = slot - blk * bs;
+  ok = slot >= 0 && blk < num_blocks;
+  return (((int64_t)blk * hkv + g) * bs + off) * dh + d;
+}
+
+// One CTA per token: rotate q and k heads in place (half-split rotation,
+// reference model.py:104-113) and scatter k, v into the layer's pools.
+template <typename T>
+__global__ void rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ positions,
+                               const int32_t* __restrict__ slots, const float* __restrict__ cos_t,
+                               const float* __restrict__ sin_t, int max_pos, int hq, int hkv,
+                               int dh, int bs, int num_blocks, T* __restrict__ kpool,
+                               T* __restrict__ vpool, int* __restrict__ err) {
+  const int t = blockIdx.x;
+  const int width = (hq + 2 * hkv) * dh;
+  T* row = qkv + (int64_t)t * width;
+  int pos = positions[t];
+  if (pos < 0 || pos >= max_pos) {
+    if (threadIdx.x == 0) raise_device_error(err, kErrPosition);
+    pos = 0;
+  }
+  const int slot = slots[t];
+  const int half = dh / 2;
+  const float* c = cos_t + (int64_t)pos * half;
+  const float* s = sin_t + (int64_t)pos * half;
+  // rotations: q heads then k heads
+  const int n_rot = (hq + hkv) * half;
+  for (int idx = threadIdx.x; idx < n_rot; idx += blockDim.x) {
+    const int h = idx / half, i = idx - h * half;
+    T* hp = row + h * dh;
+    const float x1 = to_f(hp[i]), x2 = to_f(hp[i + half]);
+    const float r1 = x1 * c[i] - x2 * s[i];
+    const float r2 = x2 * c[i] + x1 * s[i];
+    if (h < hq) {
+      hp[i] = from_f<T>(r1);
+      hp[i + half] = from_f<T>(r2);
+    } else {
+      const int g = h - hq;
+      bool ok;
+      const int64_t o1 = pool_offset(slot, g, i, bs, hkv, dh, num_blocks, ok);
+      if (!ok) {
+        raise_device_error(err, kErrSlot);
+        continue;
+      }
+      kpool[o1] = from_f<T>(r1);
+      kpool[o1 + half] = from_f<T>(r2);
+    }
+  }
+  const int n_v = hkv * dh;
+  const T* vrow = row + (hq + hkv) * dh;
+  for (int idx = threadIdx.x; idx < n_v; idx += blockDim.x) {
+    const int g = idx / dh, d = idx - g * dh;
+    bool ok;
+    const int64_t o = pool_offset(slot, g, d, bs, hkv, dh, num_blocks, ok);
+    if (!ok) {
+      raise_device_error(err, kErrSlot);
+      continue;
+    }
+    vpool[o] = vrow[idx];
+  }
+}
+
+template <typename T>
+__global__ void kv_write_kernel(const int32_t* __restrict__ slots, int n_tokens,
+                                const float* __restrict__ keys, const float* __restrict__ values,
+                                int hkv, int dh, int bs, int num_blocks, T* __restrict__ kpool,
+                                T* __restrict__ vpool, int* __restrict__ err) {
+  const int t = blockIdx.x;
+  const int slot = slots[t];
+  for (int idx = threadIdx.x; idx < hkv * dh; idx += blockDim.x) {
+    const int g = idx / dh, d = idx - g * dh;
+    bool ok;
+    const int64_t o = pool_offset(slot, g, d, bs, hkv, dh, num_blocks, ok);
+    if (!ok) {
+      raise_device_error(err, kErrSlot);
+      continue;
+    }
+    kpool[o] = from_f<T>(keys[(int64_t)t * hkv * dh + idx]);
+    vpool[o] = from_f<T>(values[(int64_t)t * hkv * dh + idx]);
+  }
+}
+
+// keys/values out: (B, max_context, hkv, dh) float32; key j of sequence b
+// lives at slot table[b][j / bs] * bs + j % bs.
+template <typename T>
+__global__ void kv_gather_kernel(const int32_t* __restrict__ tables, int max_blocks,
+                                 int max_context, int hkv, int dh, int bs, int num_blocks,
+                                 const T* __restrict__ kpool, const T* __restrict__ vpool,
+                                 float* __restrict__ keys, float* __restrict__ values,
+                                 int* __restrict__ err) {
+  const int j = blockIdx.x, b = blockIdx.y;
+  int blk = tables[(int64_t)b * max_blocks + j / bs];
+  if (blk < 0 || blk >= num_blocks) {
+    if (threadIdx.x == 0) raise_device_error(err, kErrBlock);
+    blk = 0;
+  }
+  const int slot = blk * bs + j % bs;
+  float* ko = keys + ((int64_t)b * max_context + j) * hkv * dh;
+  float* vo = values + ((int64_t)b * max_context + j) * hkv * dh;
+  for (int idx = threadIdx.x; idx < hkv * dh; idx += blockDim.x) {
+    const int g = idx / dh, d = idx - g * dh;
+    bool ok;
+    const int64_t o = pool_offset(slot, g, d, bs, hkv, dh, num_blocks, ok);
+    ko[idx] = to_f(kpool[o]);
+    vo[idx] = to_f(vpool[o]);
+  }
+}
+
+}  // namespace
+
+int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int n_rows, int dim,
+            float eps, int dtype, cudaStream_t s) {
+  if (n_rows == 0) return MS_OK;
+  ProfScope prof(kClsNorm, s);
+  const int blocks = ceil_div(n_rows, 8);
+  if (dtype == MS_DTYPE_F32)
+    rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(x, w, static_cast<float*>(y), row_idx, n_rows, dim,
+                                                 eps);
+  else if (dtype == MS_DTYPE_BF16)
+    rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(x, w, static_cast<__nv_bfloat16*>(y),
+                                                         row_idx, n_rows, dim, eps);
+  else
+    return fail(MS_ERR_UNSUPPORTED, "rmsnorm: dtype %d", dtype);
+  return check_launch("rmsnorm_kernel");
+}
+
+int embed_rmsnorm(const void* embed, const int32_t* ids, int n_tokens, int vocab, int dim,
+                  const float* w, float eps, float* x, void* y, int dtype, cudaStream_t s) {
+  if (n_tokens == 0) return MS_OK;
+  ProfScope prof(kClsNorm, s);
+  const int blocks = ceil_div(n_tokens, 8);
+  if (dtype == MS_DTYPE_F32)
+    embed_rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(embed), ids,
+                                                       n_tokens, vocab, dim, w, eps, x,
+                                                       static_cast<float*>(y), device_error_word());
+  else if (dtype == MS_DTYPE_BF16)
+    embed_rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(embed), ids, n_tokens, vocab, dim, w, eps, x,
+        static_cast<__nv_bfloat16*>(y), device_error_word());
+  else
+    return fail(MS_ERR_UNSUPPORTED, "embed_rmsnorm: dtype %d", dtype);
+  return check_launch("embed_rmsnorm_kernel");
+}
+
+int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, const float* cos_t,
+                  const float* sin_t, int max_pos, int n_tokens, int hq, int hkv, int dh,
+                  const ms_kv_cache& cache, int layer, int dtype, cudaStream_t s) {
+  if (n_tokens == 0) return MS_OK;
+  ProfScope prof(kClsNorm, s);
+  const int threads = 128;
+  if (dtype == MS_DTYPE_F32)
+    rope_kv_kernel<float><<<n_tokens, threads, 0, s>>>(
+        static_cast<float*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
+        cache.block_size, cache.num_blocks, static_cast<float*>(cache.k_pool[layer]),
+        static_cast<float*>(cache.v_pool[layer]), device_error_word());
+  else if (dtype == MS_DTYPE_BF16)
+    rope_kv_kernel<__nv_bfloat16><<<n_tokens, threads, 0, s>>>(
+        static_cast<__nv_bfloat16*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
+        cache.block_size, cache.num_blocks, static_cast<__nv_bfloat16*>(cache.k_pool[layer]),
+        static_cast<__nv_bfloat16*>(cache.v_pool[layer]), device_error_word());
+  else
+    return fail(MS_ERR_UNSUPPORTED, "rope_kv_write: dtype %d", dtype);
+  return check_launch("rope_kv_kernel");
+}
+
+int validate_cache(const ms_kv_cache* c, int layer) {
+  MS_REQUIRE(c != nullptr, "null ms_kv_cache");
+  MS_REQUIRE(c->k_pool && c->v_pool, "ms_kv_cache: null pool arrays");
+  MS_REQUIRE(layer >= 0 && layer < c->n_layers, "layer %d out of range [0,%d)", layer, c->n_layers);
+  MS_REQUIRE(c->k_pool[layer] && c->v_pool[layer], "ms_kv_cache: null pool for layer %d", layer);
+  MS_REQUIRE(c->block_size > 0 && c->num_blocks > 0 && c->n_kv_heads > 0 && c->d_head > 0,
+             "ms_kv_cache: bad geometry");
+  return MS_OK;
+}
+
+}  // namespace ms
+
+using namespace ms;
+
+extern "C" int ms_rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx,
+                          int n_rows, int dim, float eps, int dtype, void* stream) {
+  MS_REQUIRE(n_rows >= 0 && dim > 0, "ms_rmsnorm: bad sizes");
+  MS_REQUIRE(n_rows == 0 || (x && w && y), "ms_rmsnorm: null pointer");
+  return rmsnorm(x, w, y, row_idx, n_rows, dim, eps, dtype, as_stream(stream));
+}
+
+extern "C" int ms_kv_write(const ms_kv_cache* cache, int layer, const int32_t* slots,
+                           int n_tokens, const float* keys, const float* values, void* stream) {
+  MS_TRY(validate_cache(cache, layer));
+  MS_REQUIRE(n_tokens >= 0, "ms_kv_write: n_tokens < 0");
+  if (n_tokens == 0) return MS_OK;
+  MS_REQUIRE(slots && keys && values, "ms_kv_write: null pointer");
+  const ms_kv_cache& c = *cache;
+  cudaStream_t s = as_stream(stream);
+  if (c.dtype == MS_DTYPE_F32)
+    kv_write_kernel<float><<<n_tokens, 128, 0, s>>>(slots, n_tokens, keys, values, c.n_kv_heads,
+                                                    c.d_head, c.block_size, c.num_blocks,
+                                                    static_cast<float*>(c.k_pool[layer]),
+                                                    static_cast<float*>(c.v_pool[layer]),
+                                                    device_error_word());
+  else if (c.dtype == MS_DTYPE_BF16)
+    kv_write_kernel<__nv_bfloat16><<<n_tokens, 128, 0, s>>>(
+        slots, n_tokens, keys, values, c.n_kv_heads, c.d_head, c.block_size, c.num_blocks,
+        static_cast<__nv_bfloat16*>(c.k_pool[layer]), static_cast<__nv_bfloat16*>(c.v_pool[layer]),
+        device_error_word());
+  else
+    return fail(MS_ERR_UNSUPPORTED, "ms_kv_write: dtype %d", c.dtype);
+  return check_launch("kv_write_kernel");
+}
+
+extern "C" int ms_kv_gather(const ms_kv_cache* cache, int layer, const int32_t* block_tables,
+                            int n_seqs, int max_blocks, int max_context, float* keys,
+                            float* values, void* stream) {
+  MS_TRY(validate_cache(cache, layer));
+  MS_REQUIRE(n_seqs >= 0 && max_context >= 0 && max_blocks > 0, "ms_kv_gather: bad sizes");
+  if (n_seqs == 0 || max_context == 0) return MS_OK;
+  MS_REQUIRE(block_tables && keys && values, "ms_kv_gather: null pointer");
+  const ms_kv_cache& c = *cache;
+  MS_REQUIRE((int64_t)max_blocks * c.block_size >= max_context,
+             "ms_kv_gather: max_context %d beyond the table (%d blocks of %d)", max_context,
+             max_blocks, c.block_size);
+  dim3 grid(max_context, n_seqs);
+  cudaStream_t s = as_stream(stream);
+  if (c.dtype == MS_DTYPE_F32)
+    kv_gather_kernel<float><<<grid, 128, 0, s>>>(block_tables, max_blocks, max_context,
+                                                 c.n_kv_heads, c.d_head, c.block_size,
+                                                 c.num_blocks,
+                                                 static_cast<const float*>(c.k_pool[layer]),
+                                                 static_cast<const float*>(c.v_pool[layer]), keys,
+                                                 values, device_error_word());
+  else if (c.dtype == MS_DTYPE_BF16)
+    kv_gather_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+        block_tables, max_blocks, max_context, c.n_kv_heads, c.d_head, c.block_size, c.num_blocks,
+        static_cast<const __nv_bfloat16*>(c.k_pool[layer]),
+        static_cast<const __nv_bfloat16*>(c.v_pool[layer]), keys, values, device_error_word());
+  else
+    return fail(MS_ERR_UNSUPPORTED, "ms_kv_gather: dtype %d", c.dtype);
+  return check_launch("kv_gather_kernel");
+}

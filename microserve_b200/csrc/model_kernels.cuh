@@ -1,0 +1,20 @@
+// Host-side launchers shared by forward.cu.
+#pragma once
+#include "common.cuh"
+
+namespace ms {
+
+int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int n_rows, int dim,
+            float eps, int dtype, cudaStream_t s);
+int embed_rmsnorm(const void* embed, const int32_t* ids, int n_tokens, int vocab, int dim,
+                  const float* w, float eps, float* x, void* y, int dtype, cudaStream_t s);
+int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, const float* cos_t,
+                  const float* sin_t, int max_pos, int n_tokens, int hq, int hkv, int dh,
+                  const ms_kv_cache& cache, int layer, int dtype, cudaStream_t s);
+int validate_cache(const ms_kv_cache* c, int layer);
+// Paged attention (attention.cu).  q: token t's head h at q + t*q_stride +
+// h*dh; out: (T, hq*dh).
+int paged_attention(const void* q, int q_stride, const ms_kv_cache& cache, int layer,
+                    const ms_batch& batch, int hq, void* out, cudaStream_t s);
+
+}  // namespace ms

@@ -1,0 +1,725 @@
+// Sampling kernels: one CTA per vocabulary row (K8) or per request (K9).
+//
+// A row is processed the way reference sampling.py:17-74 does it
+// (temperature -> top-k -> top-p -> softmax) but without sorting:
+//   * top-k: radix select of the k-th largest value over the float bits
+//     (4 passes of 8 bits, per-warp histograms in shared memory); keep x >= it
+//     (ties keep more, as apply_top_k does);
+//   * top-p: radix descent on probability mass to the "crossing" value, the
+//     first value in descending order whose inclusive cumulative mass reaches
+//     top_p; keep x >= it (apply_top_p keeps the crossing token);
+//   * draws: inverse CDF in vocabulary order on unnormalised weights with a
+//     Philox uniform (u * total), instead of torch.multinomial's CPU stream.
+// The row is staged in shared memory when it fits, otherwise every pass
+// re-reads it from global memory (L2-resident after the first pass).
+#include <cfloat>
+#include <cmath>
+
+#include "common.cuh"
+
+namespace ms {
+namespace {
+
+constexpr int kMaxStagedV = 40960;  // 160 KB of float32 in shared memory
+constexpr int kHistBins = 256;
+
+__device__ __forceinline__ uint32_t fkey(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float kfloat(uint32_t k) {
+  const uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(u);
+}
+
+// Shared scratch used by every row routine.  `hist` holds one 256-bin
+// histogram per warp (ints or floats), `red` small reduction slots.
+struct RowSmem {
+  float* stage;  // V floats when staged, else nullptr
+  uint32_t* hist;
+  float* red;       // 64 floats
+  double* red_d;    // 64 doubles
+  int* red_i;       // 64 ints
+};
+
+// Distribution over one row.  mode 0: logits (x = raw / T, p = exp(x-m)/z
+// for x >= thresh); mode 1: probabilities as stored; mode 2: one-hot.
+struct Dist {
+  const float* row;
+  int mode;
+  bool divide;  // apply temperature when reading (row not pre-divided)
+  float temp;
+  float m, thresh, z;
+  int argmax;
+
+  __device__ __forceinline__ float x(int i) const {
+    const float v = row[i];
+    return divide ? __fdiv_rn(v, temp) : v;
+  }
+  // Unnormalised weight, the quantity the inverse CDF walks.
+  __device__ __forceinline__ float weight(int i) const {
+    if (mode == 1) return row[i];
+    if (mode == 2) return i == argmax ? 1.f : 0.f;
+    const float xv = x(i);
+    return xv >= thresh ? expf(xv - m) : 0.f;
+  }
+  __device__ __forceinline__ float prob(int i) const {
+    if (mode == 1) return row[i];
+    if (mode == 2) return i == argmax ? 1.f : 0.f;
+    const float xv = x(i);
+    return xv >= thresh ? __fdiv_rn(expf(xv - m), z) : 0.f;
+  }
+};
+
+// ---- block reductions with broadcast ---------------------------------------
+__device__ float block_sum_b(float v, RowSmem& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) sm.red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? sm.red[lane] : 0.f;
+  return warp_sum(t);
+}
+
+// Max with first-index tie break.
+__device__ void block_argmax(float v, int idx, RowSmem& sm, float& out_v, int& out_i) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  __syncthreads();
+  if (lane == 0) {
+    sm.red[warp] = v;
+    sm.red_i[warp] = idx;
+  }
+  __syncthreads();
+  v = lane < nw ? sm.red[lane] : -INFINITY;
+  idx = lane < nw ? sm.red_i[lane] : 0x7fffffff;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > v || (ov == v && oi < idx)) {
+      v = ov;
+      idx = oi;
+    }
+  }
+  out_v = v;
+  out_i = idx;
+}
+
+// Pass over the row computing max and first argmax of x.
+__device__ void row_argmax(const Dist& d, int V, RowSmem& sm, float& m, int& am) {
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = d.x(i);
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  block_argmax(best, bi, sm, m, am);
+  if (am == 0x7fffffff) am = 0;  // all NaN: degenerate, pick index 0
+}
+
+// Clears the per-warp histograms.
+__device__ __forceinline__ void hist_clear(RowSmem& sm) {
+  const int n = (blockDim.x >> 5) * kHistBins;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sm.hist[i] = 0u;
+  __syncthreads();
+}
+
+// Sums the per-warp histograms into bins [0,256) of warp 0's histogram.
+template <bool kFloat>
+__device__ __forceinline__ void hist_reduce(RowSmem& sm) {
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  for (int b = threadIdx.x; b < kHistBins; b += blockDim.x) {
+    if (kFloat) {
+      float s = 0.f;
+      for (int w = 0; w < nw; ++w) s += __uint_as_float(sm.hist[w * kHistBins + b]);
+      sm.hist[b] = __float_as_uint(s);
+    } else {
+      uint32_t s = 0;
+      for (int w = 0; w < nw; ++w) s += sm.hist[w * kHistBins + b];
+      sm.hist[b] = s;
+    }
+  }
+  __syncthreads();
+}
+
+// Warp 0 walks the 256 reduced bins from the top and finds the first bin at
+// which `above + bin >= target` (counts or masses).  Returns through smem:
+// red_i[0] = bin (-1 if none), red[0]/red_i[1] = amount strictly above it.
+template <bool kFloat>
+__device__ void hist_find_from_top(RowSmem& sm, float target_f, uint32_t target_u) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    // lane l owns bins [255-8l-7, 255-8l], walked from the top.
+    float sf = 0.f;
+    uint32_t su = 0;
+    float vf[8];
+    uint32_t vu[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int b = 255 - 8 * lane - j;
+      if (kFloat) {
+        vf[j] = __uint_as_float(sm.hist[b]);
+        sf += vf[j];
+      } else {
+        vu[j] = sm.hist[b];
+        su += vu[j];
+      }
+    }
+    // inclusive prefix over lanes (lane 0 = top bins)
+    float incf = sf;
+    uint32_t incu = su;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float tf = __shfl_up_sync(0xffffffffu, incf, o);
+      const uint32_t tu = __shfl_up_sync(0xffffffffu, incu, o);
+      if (lane >= o) {
+        incf += tf;
+        incu += tu;
+      }
+    }
+    const bool hit = kFloat ? (incf >= target_f) : (incu >= target_u);
+    const unsigned ballot = __ballot_sync(0xffffffffu, hit);
+    if (ballot == 0u) {
+      if (lane == 0) {
+        sm.red_i[0] = -1;
+        sm.red[0] = incf;  // total (unused)
+      }
+    } else {
+      const int first = __ffs(ballot) - 1;
+      if (lane == first) {
+        float af = incf - sf;
+        uint32_t au = incu - su;
+        int bin = 255 - 8 * lane - 7;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool h = kFloat ? (af + vf[j] >= target_f) : (au + vu[j] >= target_u);
+          if (h) {
+            bin = 255 - 8 * lane - j;
+            break;
+          }
+          af += kFloat ? vf[j] : 0.f;
+          au += kFloat ? 0u : vu[j];
+        }
+        sm.red_i[0] = bin;
+        sm.red[0] = af;
+        sm.red_i[1] = (int)au;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// k-th largest x over the row (1 <= k <= V), exact.
+__device__ float radix_kth_largest(const Dist& d, int V, int k, RowSmem& sm) {
+  uint32_t prefix = 0, mask = 0;
+  uint32_t k_rem = (uint32_t)k;
+  const int warp = threadIdx.x >> 5;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist_clear(sm);
+    uint32_t* h = sm.hist + warp * kHistBins;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const uint32_t key = fkey(d.x(i));
+      if ((key & mask) == prefix) atomicAdd(&h[(key >> shift) & 255u], 1u);
+    }
+    hist_reduce<false>(sm);
+    hist_find_from_top<false>(sm, 0.f, k_rem);
+    const int bin = sm.red_i[0];
+    const uint32_t above = (uint32_t)sm.red_i[1];
+    __syncthreads();
+    if (bin < 0) break;  // cannot happen for 1 <= k <= V; keeps everything
+    prefix |= (uint32_t)bin << shift;
+    mask |= 255u << shift;
+    k_rem -= above;
+  }
+  if (mask != 0xffffffffu) return -INFINITY;
+  return kfloat(prefix);
+}
+
+// The top-p crossing value: first x in descending order whose inclusive
+// cumulative probability reaches top_p.  Returns -inf if it never does.
+__device__ float radix_top_p(const Dist& d, int V, float top_p, RowSmem& sm) {
+  uint32_t prefix = 0, mask = 0;
+  float above_total = 0.f;
+  const int warp = threadIdx.x >> 5;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    hist_clear(sm);
+    uint32_t* h = sm.hist + warp * kHistBins;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float xv = d.x(i);
+      if (xv < d.thresh) continue;
+      const uint32_t key = fkey(xv);
+      if ((key & mask) == prefix) {
+        const float p = __fdiv_rn(expf(xv - d.m), d.z);
+        atomicAdd(reinterpret_cast<float*>(&h[(key >> shift) & 255u]), p);
+      }
+    }
+    hist_reduce<true>(sm);
+    hist_find_from_top<true>(sm, top_p - above_total, 0u);
+    const int bin = sm.red_i[0];
+    const float above = sm.red[0];
+    __syncthreads();
+    if (bin < 0) return -INFINITY;
+    prefix |= (uint32_t)bin << shift;
+    mask |= 255u << shift;
+    above_total += above;
+  }
+  return kfloat(prefix);
+}
+
+// Fills d.m / d.thresh / d.z / d.argmax for a logits row (mode 0).
+__device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm) {
+  float m;
+  int am;
+  row_argmax(d, V, sm, m, am);
+  d.m = m;
+  d.argmax = am;
+  d.thresh = -INFINITY;
+  if (top_k > 0 && top_k < V) d.thresh = radix_kth_largest(d, V, top_k, sm);
+  float zl = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float xv = d.x(i);
+    if (xv >= d.thresh) zl += expf(xv - m);
+  }
+  d.z = block_sum_b(zl, sm);
+  if (top_p < 1.f) {
+    float cut;
+    if (__fdiv_rn(1.f, d.z) >= top_p) {
+      cut = m;  // the maximum alone already covers top_p
+    } else {
+      cut = radix_top_p(d, V, top_p, sm);
+    }
+    if (cut > d.thresh) {
+      d.thresh = cut;
+      zl = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float xv = d.x(i);
+        if (xv >= d.thresh) zl += expf(xv - m);
+      }
+      d.z = block_sum_b(zl, sm);
+    }
+  }
+}
+
+// Inverse-CDF draw over weights w(i) in vocabulary order: the first index
+// whose running sum exceeds u * total.  Falls back to the last positive
+// weight when rounding leaves the target past the end.
+template <typename W>
+__device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int seg = (V + nw - 1) / nw;
+  seg = (seg + 31) & ~31;
+  const int s0 = min(V, warp * seg), s1 = min(V, s0 + seg);
+  // phase 1: segment totals and the last positive index
+  float part = 0.f;
+  int last = -1;
+  for (int i = s0 + lane; i < s1; i += 32) {
+    const float v = w(i);
+    part += v;
+    if (v > 0.f) last = i;
+  }
+  part = warp_sum(part);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
+  __syncthreads();
+  if (lane == 0) {
+    sm.red_d[warp] = (double)part;
+    sm.red_i[warp] = last;
+  }
+  __syncthreads();
+  // phase 2: warp 0 scans the segment totals in double
+  if (warp == 0) {
+    double v = lane < nw ? sm.red_d[lane] : 0.0;
+    int lp = lane < nw ? sm.red_i[lane] : -1;
+    double inc = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    const double total = __shfl_sync(0xffffffffu, inc, 31);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+    const double target = (double)u * total;
+    const unsigned hit = __ballot_sync(0xffffffffu, lane < nw && inc > target && v > 0.0);
+    if (lane == 0) {
+      sm.red_i[32] = hit ? (__ffs(hit) - 1) : -1;  // target warp
+      sm.red_i[33] = lp;                            // global last positive
+      sm.red_d[32] = target;
+    }
+    if (hit) {
+      const int tw = __ffs(hit) - 1;
+      const double base = __shfl_sync(0xffffffffu, inc - v, tw);
+      if (lane == 0) sm.red_d[33] = base;
+    }
+  }
+  __syncthreads();
+  const int tw = sm.red_i[32];
+  if (tw >= 0 && warp == tw) {
+    const double target = sm.red_d[32];
+    double run = sm.red_d[33];
+    int found = -1;
+    for (int b0 = s0; b0 < s1 && found < 0; b0 += 32) {
+      const int i = b0 + lane;
+      const float v = i < s1 ? w(i) : 0.f;
+      float inc = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += t;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, i < s1 && v > 0.f && run + (double)inc > target);
+      if (hit) found = b0 + __ffs(hit) - 1;
+      run += (double)__shfl_sync(0xffffffffu, inc, 31);
+    }
+    if (lane == 0) sm.red_i[34] = found >= 0 ? found : sm.red_i[warp];
+  }
+  __syncthreads();
+  int res = tw >= 0 ? sm.red_i[34] : sm.red_i[33];
+  if (res < 0) res = 0;
+  __syncthreads();
+  return res;
+}
+
+__device__ void setup_smem(RowSmem& sm, int V, bool stage) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int nw = blockDim.x >> 5;
+  unsigned char* p = smem_raw;
+  sm.red_d = reinterpret_cast<double*>(p);
+  p += 64 * sizeof(double);
+  sm.red = reinterpret_cast<float*>(p);
+  p += 64 * sizeof(float);
+  sm.red_i = reinterpret_cast<int*>(p);
+  p += 64 * sizeof(int);
+  sm.hist = reinterpret_cast<uint32_t*>(p);
+  p += (size_t)nw * kHistBins * sizeof(uint32_t);
+  sm.stage = stage ? reinterpret_cast<float*>(p) : nullptr;
+  (void)V;
+}
+
+size_t smem_bytes(int threads, int V, bool stage) {
+  size_t b = 64 * sizeof(double) + 64 * sizeof(float) + 64 * sizeof(int) +
+             (size_t)(threads / 32) * kHistBins * sizeof(uint32_t);
+  if (stage) b += (size_t)V * sizeof(float);
+  return b;
+}
+
+// Loads a logits row into a Dist: staged (pre-divided by T) when it fits.
+__device__ void load_logits(Dist& d, const float* row, int V, float temp, RowSmem& sm) {
+  d.mode = 0;
+  d.temp = temp;
+  if (sm.stage != nullptr) {
+    __syncthreads();  // previous users of the stage are done
+    const bool div = temp != 1.f;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = __ldg(row + i);
+      sm.stage[i] = div ? __fdiv_rn(v, temp) : v;
+    }
+    __syncthreads();
+    d.row = sm.stage;
+    d.divide = false;
+  } else {
+    d.row = row;
+    d.divide = temp != 1.f;
+  }
+}
+
+// ---- K8: one draw per row ----------------------------------------------------
+__global__ void sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
+                                   const ms_sampling_params* __restrict__ params,
+                                   const int32_t* __restrict__ pidx, uint32_t lane_id,
+                                   int32_t* __restrict__ tokens, float* __restrict__ probs,
+                                   ms_row_stats* __restrict__ stats, int32_t* scatter_dst,
+                                   const int32_t* __restrict__ scatter_idx, int stage) {
+  RowSmem sm;
+  setup_smem(sm, V, stage != 0);
+  const int r = blockIdx.x;
+  const ms_sampling_params P = params[pidx ? pidx[r] : r];
+  const float* row = logits + (int64_t)r * stride;
+  Dist d;
+  int token;
+  if (P.temperature == 0.f) {
+    d.row = row;
+    d.mode = 0;
+    d.divide = false;
+    d.temp = 1.f;
+    float m;
+    int am;
+    row_argmax(d, V, sm, m, am);
+    d.mode = 2;
+    d.argmax = am;
+    d.m = m;
+    d.thresh = m;
+    d.z = 1.f;
+    token = am;
+  } else {
+    load_logits(d, row, V, P.temperature, sm);
+    row_stats(d, V, P.top_k, P.top_p < 1.f ? P.top_p : 1.f, sm);
+    const float u = philox_uniform(P.seed, P.step, lane_id);
+    token = inverse_cdf([&](int i) { return d.weight(i); }, V, u, sm);
+  }
+  if (threadIdx.x == 0) {
+    tokens[r] = token;
+    if (stats) stats[r] = ms_row_stats{d.m, d.thresh, d.z, d.argmax};
+    if (scatter_dst && scatter_idx) scatter_dst[scatter_idx[r]] = token;
+  }
+  if (probs) {
+    float* out = probs + (int64_t)r * V;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) out[i] = d.prob(i);
+  }
+}
+
+// ---- K9: fused accept / resample / bonus, one CTA per request ---------------
+struct AcceptArgs {
+  const float* target;
+  int64_t tstride;
+  int target_probs;  // 1: target rows are probabilities
+  const float* draft;
+  int64_t dstride;
+  const ms_row_stats* dstats;
+  int draft_probs;  // 1: draft rows are probabilities
+  const int32_t* proposals;
+  const ms_sampling_params* params;  // nullable in probability mode
+  const float* accept_u;             // explicit uniforms (nullable)
+  const float* draw_u;
+  int gamma, V;
+  int32_t* out_tokens;
+  int32_t* out_nacc;
+  int* err;
+};
+
+__global__ void spec_accept_kernel(AcceptArgs a, int stage) {
+  RowSmem sm;
+  setup_smem(sm, a.V, stage != 0);
+  const int b = blockIdx.x;
+  const int V = a.V, G = a.gamma;
+  ms_sampling_params P;
+  if (a.params) {
+    P = a.params[b];
+  } else {
+    P.temperature = 1.f;
+    P.top_p = 1.f;
+    P.top_k = 0;
+    P.seed = 0;
+    P.step = 0;
+  }
+  const bool greedy = a.params && P.temperature == 0.f;
+  const float top_p = P.top_p < 1.f ? P.top_p : 1.f;
+  int32_t* out = a.out_tokens + (int64_t)b * (G + 1);
+
+  // Builds the target distribution for position i.
+  auto target_dist = [&](int i, Dist& p) {
+    const float* row = a.target + (int64_t)(b * (G + 1) + i) * a.tstride;
+    if (a.target_probs) {
+      p.row = row;
+      p.mode = 1;
+      p.divide = false;
+      return;
+    }
+    if (greedy) {
+      p.row = row;
+      p.mode = 0;
+      p.divide = false;
+      p.temp = 1.f;
+      float m;
+      int am;
+      row_argmax(p, V, sm, m, am);
+      p.mode = 2;
+      p.argmax = am;
+      return;
+    }
+    load_logits(p, row, V, P.temperature, sm);
+    row_stats(p, V, P.top_k, top_p, sm);
+  };
+  // Builds the draft distribution for position i (never staged).
+  auto draft_dist = [&](int i, Dist& q) {
+    const int r = i * (int)gridDim.x + b;  // position-major: row of (b, i)
+    const float* row = a.draft + (int64_t)r * a.dstride;
+    q.row = row;
+    if (a.draft_probs) {
+      q.mode = 1;
+      q.divide = false;
+      return;
+    }
+    q.temp = greedy ? 1.f : P.temperature;
+    q.divide = !greedy && P.temperature != 1.f;
+    if (a.dstats) {
+      const ms_row_stats s = a.dstats[r];
+      q.m = s.max;
+      q.thresh = s.thresh;
+      q.z = s.z;
+      q.argmax = s.argmax;
+      q.mode = greedy ? 2 : 0;
+      return;
+    }
+    q.mode = 0;
+    if (greedy) {
+      float m;
+      int am;
+      row_argmax(q, V, sm, m, am);
+      q.mode = 2;
+      q.argmax = am;
+      return;
+    }
+    row_stats(q, V, P.top_k, top_p, sm);
+  };
+
+  for (int i = 0; i < G; ++i) {
+    Dist p, q;
+    target_dist(i, p);
+    draft_dist(i, q);
+    int x = a.proposals[i * (int)gridDim.x + b];
+    if (x < 0 || x >= V) {
+      if (threadIdx.x == 0) raise_device_error(a.err, kErrToken);
+      x = 0;
+    }
+    const float px = p.prob(x);
+    const float qx = q.prob(x);
+    const float ratio = fminf(__fdiv_rn(px, fmaxf(qx, 1e-10f)), 1.f);
+    const float u = a.accept_u ? a.accept_u[i * (int)gridDim.x + b]
+                               : philox_uniform(P.seed, P.step, MS_LANE_ACCEPT + i);
+    if (u < ratio) {
+      if (threadIdx.x == 0) out[i] = x;
+      continue;
+    }
+    // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0.
+    float part = 0.f;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(p.prob(j) - q.prob(j), 0.f);
+    const float total = block_sum_b(part, sm);
+    const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
+    int tok;
+    if (total <= 1e-9f) {
+      tok = inverse_cdf([&](int j) { return p.prob(j); }, V, u2, sm);
+    } else {
+      tok = inverse_cdf([&](int j) { return fmaxf(p.prob(j) - q.prob(j), 0.f); }, V, u2, sm);
+    }
+    if (threadIdx.x == 0) {
+      out[i] = tok;
+      a.out_nacc[b] = i;
+    }
+    return;
+  }
+  // Every proposal survived: the bonus token comes from p[gamma].
+  Dist p;
+  target_dist(G, p);
+  const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
+  const int tok = inverse_cdf([&](int j) { return p.weight(j); }, V, u2, sm);
+  if (threadIdx.x == 0) {
+    out[G] = tok;
+    a.out_nacc[b] = G;
+  }
+}
+
+int row_threads(int V) {
+  int t = ((V / 16) + 31) & ~31;
+  if (t < 128) t = 128;
+  if (t > 1024) t = 1024;
+  return t;
+}
+
+int launch_accept(AcceptArgs a, int B, void* stream) {
+  a.err = device_error_word();
+  const int threads = row_threads(a.V);
+  const bool stage = a.V <= kMaxStagedV && !a.target_probs;
+  const size_t smem = smem_bytes(threads, a.V, stage);
+  cudaError_t e = cudaFuncSetAttribute(spec_accept_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return fail(MS_ERR_CUDA, "spec_accept: smem attribute: %s", cudaGetErrorString(e));
+  ProfScope prof(kClsAccept, as_stream(stream));
+  spec_accept_kernel<<<B, threads, smem, as_stream(stream)>>>(a, stage ? 1 : 0);
+  return check_launch("spec_accept_kernel");
+}
+
+}  // namespace
+}  // namespace ms
+
+using namespace ms;
+
+extern "C" int ms_sample(const float* logits, int64_t row_stride, int n_rows, int vocab,
+                         const ms_sampling_params* params, const int32_t* pidx, int lane,
+                         int32_t* tokens, float* probs, ms_row_stats* stats, int32_t* scatter_dst,
+                         const int32_t* scatter_idx, void* stream) {
+  MS_REQUIRE(n_rows >= 0 && vocab > 0, "ms_sample: bad sizes rows=%d vocab=%d", n_rows, vocab);
+  if (n_rows == 0) return MS_OK;
+  MS_REQUIRE(logits && params && tokens, "ms_sample: null pointer");
+  MS_REQUIRE(row_stride >= vocab, "ms_sample: row_stride < vocab");
+  const int threads = row_threads(vocab);
+  const bool stage = vocab <= kMaxStagedV;
+  const size_t smem = smem_bytes(threads, vocab, stage);
+  cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem);
+  if (e != cudaSuccess) return fail(MS_ERR_CUDA, "ms_sample: smem attribute: %s", cudaGetErrorString(e));
+  ProfScope prof(kClsSample, as_stream(stream));
+  sample_rows_kernel<<<n_rows, threads, smem, as_stream(stream)>>>(
+      logits, row_stride, vocab, params, pidx, (uint32_t)lane, tokens, probs, stats, scatter_dst,
+      scatter_idx, stage ? 1 : 0);
+  return check_launch("sample_rows_kernel");
+}
+
+extern "C" int ms_spec_accept(const float* target_logits, int64_t target_stride,
+                              const float* draft_rows, int64_t draft_stride,
+                              const ms_row_stats* draft_stats, int draft_probs_mode,
+                              const int32_t* proposals, const ms_sampling_params* params,
+                              int n_requests, int gamma, int vocab, int32_t* out_tokens,
+                              int32_t* out_num_accepted, void* stream) {
+  MS_REQUIRE(n_requests >= 0 && gamma >= 1 && vocab > 0, "ms_spec_accept: bad sizes");
+  if (n_requests == 0) return MS_OK;
+  MS_REQUIRE(target_logits && draft_rows && proposals && params && out_tokens && out_num_accepted,
+             "ms_spec_accept: null pointer");
+  MS_REQUIRE(target_stride >= vocab && draft_stride >= vocab, "ms_spec_accept: stride < vocab");
+  AcceptArgs a{};
+  a.target = target_logits;
+  a.tstride = target_stride;
+  a.target_probs = 0;
+  a.draft = draft_rows;
+  a.dstride = draft_stride;
+  a.dstats = draft_stats;
+  a.draft_probs = draft_probs_mode ? 1 : 0;
+  a.proposals = proposals;
+  a.params = params;
+  a.gamma = gamma;
+  a.V = vocab;
+  a.out_tokens = out_tokens;
+  a.out_nacc = out_num_accepted;
+  return launch_accept(a, n_requests, stream);
+}
+
+extern "C" int ms_verify_probs(const float* target_probs, const float* draft_probs,
+                               const int32_t* proposals, const float* accept_u, const float* draw_u,
+                               int n_requests, int gamma, int vocab, int32_t* out_tokens,
+                               int32_t* out_num_accepted, void* stream) {
+  MS_REQUIRE(n_requests >= 0 && gamma >= 1 && vocab > 0, "ms_verify_probs: bad sizes");
+  if (n_requests == 0) return MS_OK;
+  MS_REQUIRE(target_probs && draft_probs && proposals && accept_u && draw_u && out_tokens &&
+                 out_num_accepted,
+             "ms_verify_probs: null pointer");
+  AcceptArgs a{};
+  a.target = target_probs;
+  a.tstride = vocab;
+  a.target_probs = 1;
+  a.draft = draft_probs;
+  a.dstride = vocab;
+  a.draft_probs = 1;
+  a.proposals = proposals;
+  a.params = nullptr;
+  a.accept_u = accept_u;
+  a.draw_u = draw_u;
+  a.gamma = gamma;
+  a.V = vocab;
+  a.out_tokens = out_tokens;
+  a.out_nacc = out_num_accepted;
+  return launch_accept(a, n_requests, stream);
+}

@@ -1,0 +1,400 @@
+"""Speculative decoding on the device: draft gamma tokens, verify, accept, roll back.
+
+Reference: src/microserve/speculative.py.  Same API (``SpeculativeDecoder``
+with ``step``/``free``/``reset``/``generate``, ``verify_proposals``,
+``VerificationResult``) and the same Leviathan et al. accept/reject rule:
+
+    accept x ~ q with probability min(1, p(x) / q(x)); on the first reject
+    resample from normalise(max(0, p - q)) (p if that mass is <= 1e-9);
+    if all gamma proposals survive, draw a bonus token from p[gamma].
+
+One round (``step``) is, on one stream: gamma draft passes (each a paged
+forward that computes logits only for each request's last row, then a draw
+that writes the proposal straight into the next pass's inputs and into the
+verify batch), one target verify pass over ``[uncached tokens] + proposals``
+with logits for the last gamma+1 rows of each request, and the fused
+accept/resample/bonus kernel.  All metadata for the round goes up in one
+pinned copy and the accepted tokens come back in one; the host then rolls
+both caches back with ``truncate`` as the reference does
+(speculative.py:213-226).
+
+Random draws use Philox uniforms keyed by the request generator's seed and
+``Request.rng_step`` (see sampling.py), one step per round: draft draw j on
+lane j, accept roll i on lane 64+i, the residual/bonus draw on lane 128.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _lib
+from .batching import HostStaging, batch_from_host, pack_int32
+from .cache import PagedKVCache
+from .config import CacheConfig, SamplingConfig
+from .model import PagedBatch, Transformer
+from .sampling import generator_seed_and_step, make_params, validate
+from .scheduler import Request
+
+
+@dataclass
+class VerificationResult:
+    """Outcome of verifying one sequence's proposals."""
+
+    tokens: list[int]  # accepted drafts followed by exactly one extra token
+    num_accepted: int
+    num_proposed: int
+
+
+def _u64_tensor(values: list[int], device: torch.device) -> torch.Tensor:
+    """uint64 values carried in an int64 device tensor (same bits)."""
+    arr = np.asarray([v & 0xFFFFFFFFFFFFFFFF for v in values], dtype=np.uint64)
+    return torch.from_numpy(arr.view(np.int64)).to(device)
+
+
+def _philox_device(seed: int, step: int, lanes: list[int], device: torch.device) -> torch.Tensor:
+    out = torch.empty(len(lanes), dtype=torch.float32, device=device)
+    seeds = _u64_tensor([seed], device)
+    steps = _u64_tensor([step], device)
+    for i, lane in enumerate(lanes):
+        _lib.call("ms_philox_uniforms", seeds.data_ptr(), steps.data_ptr(), 1, lane,
+                  out[i:].data_ptr(), _lib.stream_ptr(device))
+    return out
+
+
+def verify_proposals(
+    draft_probs: torch.Tensor,
+    target_probs: torch.Tensor,
+    proposals: list[int],
+    generator: torch.Generator | None = None,
+) -> VerificationResult:
+    """Accept/reject test for one sequence (reference speculative.py:44-86).
+
+    ``draft_probs`` is ``(gamma, vocab)``, ``target_probs`` ``(gamma+1, vocab)``.
+    """
+    gamma = len(proposals)
+    if draft_probs.shape[0] != gamma or target_probs.shape[0] != gamma + 1:
+        raise ValueError("probability tensors do not match the proposal length")
+    dev = draft_probs.device if draft_probs.device.type == "cuda" else torch.device("cuda")
+    _lib.require_cuda(dev)
+    vocab = int(target_probs.shape[-1])
+    q = draft_probs.to(device=dev, dtype=torch.float32).contiguous()
+    p = target_probs.to(device=dev, dtype=torch.float32).contiguous()
+    x = torch.tensor(proposals, dtype=torch.int32, device=dev)
+    seed, step = generator_seed_and_step(generator)
+    u = _philox_device(seed, step, [_lib.LANE_ACCEPT + i for i in range(gamma)]
+                       + [_lib.LANE_RESAMPLE], dev)
+    out = torch.empty(gamma + 1, dtype=torch.int32, device=dev)
+    nacc = torch.empty(1, dtype=torch.int32, device=dev)
+    _lib.call("ms_verify_probs", p.data_ptr(), q.data_ptr(), x.data_ptr(), u.data_ptr(),
+              u[gamma:].data_ptr(), 1, gamma, vocab, out.data_ptr(), nacc.data_ptr(),
+              _lib.stream_ptr(dev))
+    n = int(nacc.item())
+    return VerificationResult(out[: n + 1].tolist(), n, gamma)
+
+
+class _Buffers:
+    """Grow-only flat device (and pinned host) buffers, viewed at the exact
+    shape of each round so position-major rows are exactly B apart."""
+
+    def __init__(self, device: torch.device) -> None:
+        self.device = device
+        self._store: dict[str, torch.Tensor] = {}
+
+    def get(self, name: str, numel: int, dtype: torch.dtype, pinned: bool = False) -> torch.Tensor:
+        t = self._store.get(name)
+        if t is None or t.numel() < numel:
+            cap = max(numel, 2 * (0 if t is None else t.numel()))
+            if pinned:
+                t = torch.empty(cap, dtype=dtype, pin_memory=True)
+            else:
+                t = torch.empty(cap, dtype=dtype, device=self.device)
+            self._store[name] = t
+        return t[:numel]
+
+    def round_views(self, B: int, G: int, V: int) -> None:
+        f32, i32 = torch.float32, torch.int32
+        self.dlogits = self.get("dlogits", G * B * V, f32).view(G, B, V)
+        self.vlogits = self.get("vlogits", B * (G + 1) * V, f32).view(B * (G + 1), V)
+        self.dstats = self.get("dstats", G * B * 4, i32).view(G, B, 4)
+        self.proposals = self.get("proposals", G * B, i32).view(G, B)
+        self.out = self.get("out", B * (G + 2), i32)
+        self.out_host = self.get("out_host", B * (G + 2), i32, pinned=True)
+
+
+class SpeculativeDecoder:
+    """Batched draft-then-verify over decoding requests (reference speculative.py:89-261)."""
+
+    def __init__(
+        self,
+        target: Transformer,
+        draft: Transformer,
+        cache_cfg: CacheConfig,
+        gamma: int = 4,
+        device: str | torch.device = "cuda",
+    ) -> None:
+        if gamma < 1:
+            raise ValueError("gamma must be at least 1")
+        if target.cfg.vocab_size != draft.cfg.vocab_size:
+            raise ValueError("draft and target must share a vocabulary")
+        self.target = target.eval()
+        self.draft = draft.eval()
+        self.gamma = gamma
+        self.device = _lib.require_cuda(device)
+        # The draft keeps its own pool, sized by the same CacheConfig as the target's.
+        dcfg = CacheConfig(cache_cfg.block_size, cache_cfg.num_blocks, draft.cfg.dtype)
+        self.draft_cache = PagedKVCache(draft.cfg, dcfg, self.device)
+        self.num_proposed = 0
+        self.num_accepted = 0
+        self._staging = HostStaging(self.device)
+        self._buf = _Buffers(self.device)
+        self.last_round_launches = 0
+        # Measurement hooks (set by benchmarks): when ``round_events`` is a
+        # list, each round appends a (start, end) CUDA event pair around its
+        # kernels; the last round's shapes and copy sizes are kept below.
+        self.round_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] | None = None
+        self.last_round_shape: dict[str, int] = {}
+        self.last_h2d_bytes = 0
+        self.last_d2h_bytes = 0
+
+    # -- one round ------------------------------------------------------------
+    def step(
+        self,
+        requests: list[Request],
+        target_cache: PagedKVCache,
+        generators: dict[int, torch.Generator],
+    ) -> list[list[int]]:
+        """Advance every request by one speculative round; returns the emitted
+        tokens (1..gamma+1) per request.  The caller appends them."""
+        if not requests:
+            return []
+        G, B, V = self.gamma, len(requests), self.target.cfg.vocab_size
+        for r in requests:
+            validate(r.sampling)
+        plan = self._plan(requests, target_cache, generators)
+        launches0 = _lib.launch_count()
+        self._launch(plan, target_cache)
+        self.last_round_launches = _lib.launch_count() - launches0
+        buf = self._buf
+        n_out = B * (G + 2)
+        buf.out_host[:n_out].copy_(buf.out[:n_out], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        res = buf.out_host[:n_out].numpy()
+        tokens = res[: B * (G + 1)].reshape(B, G + 1)
+        nacc = res[B * (G + 1) : B * (G + 2)].astype(np.int64)
+        return self._finish(requests, target_cache, plan, tokens, nacc)
+
+    def _plan(
+        self,
+        requests: list[Request],
+        target_cache: PagedKVCache,
+        generators: dict[int, torch.Generator],
+    ) -> dict[str, object]:
+        """Reserve every slot of the round and pack its metadata into one blob."""
+        G, B = self.gamma, len(requests)
+        ids = [r.request_id for r in requests]
+        dcache = self.draft_cache
+        d_cached = np.fromiter((dcache.num_tokens(i) for i in ids), np.int64, B)
+        t_cached = np.fromiter((target_cache.num_tokens(i) for i in ids), np.int64, B)
+        pending = [r.tail(int(c)) for r, c in zip(requests, d_cached, strict=True)]
+        prefix = [r.tail(int(c)) for r, c in zip(requests, t_cached, strict=True)]
+        n0 = np.fromiter((len(p) for p in pending), np.int64, B)
+        npre = np.fromiter((len(p) for p in prefix), np.int64, B)
+        if np.any(npre < 1):
+            raise ValueError("every request needs at least one uncomputed token")
+
+        # Slots for the whole round, reserved up front (all-or-nothing).
+        dslots = dcache.append_many(ids, n0 + (G - 1))
+        tslots = target_cache.append_many(ids, npre + G)
+        dtab, _, dw = dcache.table_rows(ids)
+        ttab, _, tw = target_cache.table_rows(ids)
+
+        # Draft pass 0: the catch-up tokens (usually 1 or 2 per request).
+        dstart = np.zeros(B + 1, np.int64)
+        np.cumsum(n0 + (G - 1), out=dstart[1:])
+        q0 = np.zeros(B + 1, np.int64)
+        np.cumsum(n0, out=q0[1:])
+        T0 = int(q0[-1])
+        seg0 = np.repeat(np.arange(B), n0)
+        within0 = np.arange(T0) - q0[:-1][seg0]
+        ids0 = np.fromiter((t for p in pending for t in p), np.int32, T0)
+        pos0 = d_cached[seg0] + within0
+        slots0 = dslots[dstart[:-1][seg0] + within0]
+        ctx0 = d_cached + n0
+        rows0 = q0[1:] - 1
+        # Draft passes 1..G-1: one token per request (the previous proposal).
+        unit_qs = np.arange(B + 1)
+        ones = np.ones(B, np.int64)
+        pos_j = [d_cached + n0 + j - 1 for j in range(1, G)]
+        slots_j = [dslots[dstart[:-1] + n0 + j - 1] for j in range(1, G)]
+        ctx_j = [d_cached + n0 + j for j in range(1, G)]
+
+        # Target verify: [uncached tokens] + G proposals per request.
+        qv = np.zeros(B + 1, np.int64)
+        np.cumsum(npre + G, out=qv[1:])
+        Tv = int(qv[-1])
+        segv = np.repeat(np.arange(B), npre + G)
+        withinv = np.arange(Tv) - qv[:-1][segv]
+        idsv = np.zeros(Tv, np.int32)
+        is_prefix = withinv < npre[segv]
+        idsv[is_prefix] = np.fromiter((t for p in prefix for t in p), np.int32, int(npre.sum()))
+        posv = t_cached[segv] + withinv
+        ctxv = t_cached + npre + G
+        rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
+        scat = [qv[:-1] + npre + j for j in range(G)]
+
+        seeds = [generators[i].initial_seed() for i in ids]
+        steps = [r.rng_step for r in requests]
+        params = make_params([r.sampling for r in requests], seeds, steps)
+        pwords = params.view(np.int32)
+
+        parts = [
+            pwords,
+            # draft pass 0 batch (order matches batch_from_host)
+            ids0, pos0, slots0, q0, ctx0, n0, dtab,
+            rows0,
+            # shared unit batch arrays for passes >= 1
+            unit_qs, ones,
+            *[a for j in range(G - 1) for a in (pos_j[j], slots_j[j], ctx_j[j])],
+            # verify batch
+            idsv, posv, tslots, qv, ctxv, npre + G, ttab,
+            rowsv,
+            *scat,
+        ]
+        blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
+        return {
+            "blob": blob, "spans": spans, "B": B, "dw": dw, "tw": tw, "T0": T0, "Tv": Tv,
+            "max_q0": int(n0.max()), "max_qv": int((npre + G).max()),
+            "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
+        }
+
+    def _launch(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
+        G, V = self.gamma, self.target.cfg.vocab_size
+        B = int(plan["B"])  # type: ignore[arg-type]
+        self._buf.round_views(B, G, V)
+        buf = self._buf
+        dev_blob = self._staging.upload(plan["blob"])  # type: ignore[arg-type]
+        spans: list[tuple[int, int]] = plan["spans"]  # type: ignore[assignment]
+        v = [dev_blob[o : o + n] for o, n in spans]
+        stream = _lib.stream_ptr(self.device)
+        params = v[0]
+        k = 1
+        b0 = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["dw"]), int(plan["max_q0"]),
+                             int(plan["T0"]))
+        dtab = v[k + 6].view(B, int(plan["dw"]))
+        k += 7
+        rows0 = v[k]
+        k += 1
+        unit_qs, ones = v[k], v[k + 1]
+        k += 2
+        batches: list[tuple[PagedBatch, torch.Tensor | None]] = [(b0, rows0)]
+        for j in range(1, G):
+            pos, slots, ctx = v[k], v[k + 1], v[k + 2]
+            k += 3
+            bj = PagedBatch(
+                input_ids=buf.proposals[j - 1], positions=pos, slot_mapping=slots,
+                block_tables=dtab, context_lens=ctx, q_lens=ones, q_start=unit_qs, max_q=1,
+                n_tokens=B,
+            )
+            batches.append((bj, None))
+        bv = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["tw"]), int(plan["max_qv"]),
+                             int(plan["Tv"]))
+        k += 7
+        rowsv = v[k]
+        k += 1
+        scat = v[k : k + G]
+        self.last_round_shape = {"B": B, "T0": int(plan["T0"]), "Tv": int(plan["Tv"]),  # type: ignore[arg-type]
+                                 "gamma": G}
+        self.last_h2d_bytes = int(plan["blob"].nbytes)  # type: ignore[union-attr]
+        self.last_d2h_bytes = B * (G + 2) * 4
+        ev = None
+        if self.round_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+
+        for j, (bj, rows) in enumerate(batches):
+            out = buf.dlogits[j]
+            self.draft.forward_paged(bj, self.draft_cache, logit_rows=rows, out=out,
+                                     out_row_stride=V)
+            _lib.call(
+                "ms_sample", out.data_ptr(), V, B, V, params.data_ptr(), None, _lib.LANE_DRAFT + j,
+                buf.proposals[j].data_ptr(), None, buf.dstats[j].data_ptr(),
+                bv.input_ids.data_ptr(), scat[j].data_ptr(), stream,
+            )
+        self.target.forward_paged(bv, target_cache, logit_rows=rowsv, out=buf.vlogits,
+                                  out_row_stride=V)
+        _lib.call(
+            "ms_spec_accept", buf.vlogits.data_ptr(), V, buf.dlogits.data_ptr(), V,
+            buf.dstats.data_ptr(), 0, buf.proposals.data_ptr(), params.data_ptr(), B, G, V,
+            buf.out.data_ptr(), buf.out[B * (G + 1) :].data_ptr(), stream,
+        )
+        if ev is not None and self.round_events is not None:
+            ev[1].record()
+            self.round_events.append(ev)
+
+    def _finish(
+        self,
+        requests: list[Request],
+        target_cache: PagedKVCache,
+        plan: dict[str, object],
+        tokens: np.ndarray,
+        nacc: np.ndarray,
+    ) -> list[list[int]]:
+        G = self.gamma
+        ids: list[int] = plan["ids"]  # type: ignore[assignment]
+        n_tok = np.fromiter((r.num_tokens for r in requests), np.int64, len(requests))
+        keep = n_tok + nacc
+        target_cache.truncate_many(ids, keep)
+        d_len = plan["d_cached"] + plan["n0"] + (G - 1)  # type: ignore[operator]
+        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep))
+        results: list[list[int]] = []
+        for b, r in enumerate(requests):
+            n = int(nacc[b])
+            r.num_computed = int(keep[b])
+            r.num_draft_proposed += G
+            r.num_draft_accepted += n
+            r.rng_step += 1
+            results.append(tokens[b, : n + 1].tolist())
+        self.num_proposed += G * len(requests)
+        self.num_accepted += int(nacc.sum())
+        return results
+
+    # -- lifecycle ----------------------------------------------------------------
+    def free(self, seq_id: int) -> None:
+        self.draft_cache.free(seq_id)
+
+    def reset(self) -> None:
+        self.draft_cache.reset()
+        self.num_proposed = 0
+        self.num_accepted = 0
+
+    def generate(
+        self,
+        prompt_ids: list[int],
+        sampling: SamplingConfig,
+        seq_id: int = 0,
+        generator: torch.Generator | None = None,
+        target_cache: PagedKVCache | None = None,
+    ) -> list[int]:
+        """Single-sequence speculative generation (reference speculative.py:237-261)."""
+        ccfg = CacheConfig(self.draft_cache.cfg.block_size, self.draft_cache.cfg.num_blocks,
+                           self.target.cfg.dtype)
+        cache = target_cache or PagedKVCache(self.target.cfg, ccfg, self.device)
+        gen = generator or torch.Generator().manual_seed(0)
+        request = Request(request_id=seq_id, prompt_ids=list(prompt_ids), sampling=sampling)
+        generators = {seq_id: gen}
+        try:
+            while len(request.output_ids) < sampling.max_new_tokens:
+                for token in self.step([request], cache, generators)[0]:
+                    if request.should_stop():
+                        break
+                    request.output_ids.append(token)
+                if request.should_stop():
+                    break
+            return request.output_ids
+        finally:
+            cache.free(seq_id)
+            self.draft_cache.free(seq_id)

@@ -1,0 +1,185 @@
+"""Generate the golden fixtures by running the unmodified MicroServe reference.
+
+Run in a container that has the reference source tree:
+
+    python tests/golden/make_golden.py /path/to/microserve
+
+It imports ``microserve`` from ``<root>/src`` and writes small ``.npz`` files
+next to this script.  The tests only read the ``.npz`` files (the reference
+is not needed at test time).  Every fixture records the reference call it
+came from.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+
+
+def state_arrays(model: torch.nn.Module, prefix: str) -> dict[str, np.ndarray]:
+    return {prefix + k: v.detach().cpu().numpy().astype(np.float32)
+            for k, v in model.state_dict().items()}
+
+
+def main(ref_root: str) -> None:
+    sys.path.insert(0, str(Path(ref_root) / "src"))
+    from microserve.batching import build_paged_batch
+    from microserve.cache import PagedKVCache
+    from microserve.config import (CacheConfig, EngineConfig, ModelConfig, SamplingConfig,
+                                   SchedulerConfig, SpeculativeConfig)
+    from microserve.engine import LLMEngine
+    from microserve.model import Transformer
+    from microserve.sampling import probs_from_logits
+    from microserve.speculative import SpeculativeDecoder, verify_proposals
+
+    torch.set_num_threads(1)
+
+    def make_model(cfg: ModelConfig, seed: int, amplify: float) -> Transformer:
+        # the reference test fixture recipe (tests/conftest.py:41-56)
+        torch.manual_seed(seed)
+        m = Transformer(cfg).eval()
+        with torch.no_grad():
+            for blk in m.blocks:
+                blk.attn.o_proj.weight *= amplify
+                blk.ffn.down_proj.weight *= amplify
+        return m
+
+    def dense_greedy(model: Transformer, prompt: list[int], n: int) -> list[int]:
+        # tests/conftest.py:74-85
+        past = None
+        cur = torch.tensor(prompt)[None]
+        out = []
+        for _ in range(n):
+            with torch.no_grad():
+                logits, past = model(cur, past_kv=past, return_cache=True)
+            tok = int(logits[0, -1].argmax())
+            out.append(tok)
+            cur = torch.tensor([[tok]])
+        return out
+
+    tcfg = ModelConfig(vocab_size=32, n_layers=2, d_model=32, n_heads=4, max_seq_len=128)
+    dcfg = ModelConfig(vocab_size=32, n_layers=1, d_model=16, n_heads=2, max_seq_len=128)
+    target = make_model(tcfg, 0, 20.0)
+    draft = make_model(dcfg, 1, 20.0)
+    out: dict[str, np.ndarray] = {}
+    out.update(state_arrays(target, "target/"))
+    out.update(state_arrays(draft, "draft/"))
+    out["target_cfg"] = np.array([32, 2, 32, 4, 4, int(tcfg.d_ff), 128])
+    out["draft_cfg"] = np.array([32, 1, 16, 2, 2, int(dcfg.d_ff), 128])
+
+    # -- paged forward logits (model.py:339 forward_paged via batching.py:19) --
+    gen = torch.Generator().manual_seed(7)
+    rnd = lambda n: torch.randint(0, 32, (n,), generator=gen).tolist()  # noqa: E731
+    cases = {
+        "prefill11": ([rnd(11)], None),
+        "unequal": ([rnd(n) for n in (3, 9, 16, 1)], None),
+    }
+    for name, (seqs, _) in cases.items():
+        cache = PagedKVCache(tcfg, CacheConfig(block_size=8, num_blocks=32))
+        batch = build_paged_batch(cache, list(range(len(seqs))), seqs, [0] * len(seqs))
+        with torch.no_grad():
+            logits = target.forward_paged(batch, cache)
+        out[f"fwd/{name}/tokens"] = np.concatenate([np.asarray(s) for s in seqs])
+        out[f"fwd/{name}/lens"] = np.asarray([len(s) for s in seqs])
+        out[f"fwd/{name}/logits"] = logits.numpy()
+    # decode after prefill, with a mixed prefill+decode pass (test_model.py:145-162)
+    a, b = rnd(7), rnd(5)
+    tok = rnd(1)
+    cache = PagedKVCache(tcfg, CacheConfig(block_size=8, num_blocks=32))
+    build = lambda ids, toks, st: build_paged_batch(cache, ids, toks, st)  # noqa: E731
+    with torch.no_grad():
+        target.forward_paged(build([0], [a], [0]), cache)
+        mixed = target.forward_paged(build([0, 1], [tok, b], [7, 0]), cache)
+    out["fwd/mixed/a"] = np.asarray(a)
+    out["fwd/mixed/b"] = np.asarray(b)
+    out["fwd/mixed/tok"] = np.asarray(tok)
+    out["fwd/mixed/logits"] = mixed.numpy()
+
+    # -- greedy streams: dense reference and SpeculativeDecoder.generate --
+    prompts = [rnd(6), rnd(11), rnd(3)]
+    for i, p in enumerate(prompts):
+        out[f"greedy/{i}/prompt"] = np.asarray(p)
+        out[f"greedy/{i}/dense"] = np.asarray(dense_greedy(target, p, 20))
+        for gamma in (1, 2, 3, 5):
+            dec = SpeculativeDecoder(target, draft, CacheConfig(block_size=8, num_blocks=32),
+                                     gamma=gamma)
+            got = dec.generate(p, SamplingConfig(temperature=0.0, max_new_tokens=20))
+            out[f"greedy/{i}/spec{gamma}"] = np.asarray(got)
+            out[f"greedy/{i}/spec{gamma}_counts"] = np.asarray([dec.num_accepted, dec.num_proposed])
+
+    # -- engine greedy (test_speculative.py:211-245 shape) --
+    eprompts = [rnd(n) for n in (4, 9, 6)]
+    for gamma in (1, 3, 5):
+        cfg = EngineConfig(model=tcfg, cache=CacheConfig(block_size=8, num_blocks=128),
+                           scheduler=SchedulerConfig(max_batch_size=3),
+                           speculative=SpeculativeConfig(enabled=True, gamma=gamma))
+        eng = LLMEngine(target, cfg, draft_model=draft)
+        reqs = [eng.add_request(p, SamplingConfig(temperature=0.0, max_new_tokens=16))
+                for p in eprompts]
+        outs = {o.request_id: o.output_ids for o in eng.run()}
+        for j, r in enumerate(reqs):
+            out[f"engine/g{gamma}/{j}"] = np.asarray(outs[r.request_id])
+        out[f"engine/g{gamma}/counts"] = np.asarray(
+            [eng.stats.num_draft_accepted, eng.stats.num_draft_proposed])
+    for j, p in enumerate(eprompts):
+        out[f"engine/prompt/{j}"] = np.asarray(p)
+
+    # -- sampling filters (sampling.py:54-74 probs_from_logits) --
+    g2 = torch.Generator().manual_seed(11)
+    settings = [(0.8, None, None), (1.0, 5, None), (1.0, None, 0.9), (0.7, 5, 0.9),
+                (1.3, None, 0.5), (1.0, 50, 0.9), (0.0, None, None)]
+    for vocab in (32, 1000):
+        logits = torch.randn(6, vocab, generator=g2) * 2.0
+        out[f"filter/v{vocab}/logits"] = logits.numpy()
+        for si, (t, k, p) in enumerate(settings):
+            probs = probs_from_logits(logits, SamplingConfig(temperature=t, top_k=k, top_p=p))
+            out[f"filter/v{vocab}/s{si}"] = probs.numpy()
+    out["filter/settings"] = np.asarray(
+        [[t, -1 if k is None else k, -1.0 if p is None else p] for t, k, p in settings])
+
+    # -- verify_proposals deterministic cases (test_speculative.py:36-61) --
+    r1 = verify_proposals(torch.tensor([[0.5, 0.5]]), torch.tensor([[1.0, 0.0], [1.0, 0.0]]), [0],
+                          torch.Generator().manual_seed(0))
+    r2 = verify_proposals(torch.tensor([[0.0, 1.0]]), torch.tensor([[1.0, 0.0], [1.0, 0.0]]), [1],
+                          torch.Generator().manual_seed(0))
+    out["verify/dominates"] = np.asarray([r1.num_accepted, *r1.tokens])
+    out["verify/impossible"] = np.asarray([r2.num_accepted, *r2.tokens])
+
+    # -- GQA pin: a grouped model equals the reference MHA model with each
+    # kv head's rows repeated per group --
+    gcfg = ModelConfig(vocab_size=48, n_layers=2, d_model=64, n_heads=8, max_seq_len=64)
+    torch.manual_seed(3)
+    mha = Transformer(gcfg).eval()
+    hkv, dh, group = 2, 8, 4
+    gqa_state = {}
+    with torch.no_grad():
+        for i, blk in enumerate(mha.blocks):
+            for nm in ("k_proj", "v_proj"):
+                w = getattr(blk.attn, nm).weight
+                small = torch.randn(hkv * dh, 64) * 0.3
+                gqa_state[f"blocks.{i}.attn.{nm}.weight"] = small.numpy()
+                w.copy_(small.view(hkv, dh, 64).repeat_interleave(group, 0).reshape(64, 64))
+            blk.attn.o_proj.weight *= 10
+            blk.ffn.down_proj.weight *= 10
+    for k, v in mha.state_dict().items():
+        if k not in gqa_state:
+            gqa_state[k] = v.numpy().astype(np.float32)
+    seq = torch.randint(0, 48, (13,), generator=gen).tolist()
+    with torch.no_grad():
+        dense, _ = mha(torch.tensor(seq)[None])
+    for k, v in gqa_state.items():
+        out["gqa/" + k] = v
+    out["gqa/tokens"] = np.asarray(seq)
+    out["gqa/logits"] = dense[0].numpy()
+
+    np.savez_compressed(HERE / "reference_fixtures.npz", **out)
+    print(f"wrote {HERE / 'reference_fixtures.npz'} with {len(out)} arrays")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

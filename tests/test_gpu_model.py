@@ -1,0 +1,213 @@
+"""Device paged forward against the reference's logits and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.model import Dims, OracleModel, SeqKV
+
+from .conftest import tiny_state
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+FP32_TOL = dict(rtol=1e-4, atol=1e-5)  # north-star fp32 logits tolerance (1e-4 relative)
+BF16_TOL = dict(rtol=2e-2, atol=2e-2)  # north-star bf16 logits tolerance
+
+
+def tiny_model_cfg(golden, which: str, **kw):
+    from microserve_b200.config import ModelConfig
+
+    v, L, d, h, hkv, ff, msl = (int(x) for x in golden[f"{which}_cfg"])
+    return ModelConfig(vocab_size=v, n_layers=L, d_model=d, n_heads=h, n_kv_heads=hkv, d_ff=ff,
+                       max_seq_len=msl, **kw)
+
+
+def device_model(golden, which: str):
+    from microserve_b200.model import Transformer
+
+    cfg = tiny_model_cfg(golden, which)
+    return Transformer.from_state_dict(cfg, tiny_state(golden, which), DEV)
+
+
+def run(model, cache, seq_ids, token_lists, starts):
+    from microserve_b200.batching import build_paged_batch
+
+    batch = build_paged_batch(cache, seq_ids, token_lists, starts)
+    out = model.forward_paged(batch, cache)
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def new_cache(model, block_size=8, num_blocks=32):
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import CacheConfig
+
+    return PagedKVCache(model.cfg, CacheConfig(block_size, num_blocks, model.cfg.dtype), DEV)
+
+
+@pytest.mark.parametrize("case", ["prefill11", "unequal"])
+def test_forward_matches_reference_logits(golden, case: str) -> None:
+    m = device_model(golden, "target")
+    toks = golden[f"fwd/{case}/tokens"].tolist()
+    lens = golden[f"fwd/{case}/lens"].tolist()
+    seqs, o = [], 0
+    for n in lens:
+        seqs.append(toks[o : o + n])
+        o += n
+    out = run(m, new_cache(m), list(range(len(seqs))), seqs, [0] * len(seqs))
+    np.testing.assert_allclose(out, golden[f"fwd/{case}/logits"], **FP32_TOL)
+
+
+def test_mixed_prefill_and_decode_matches_reference(golden) -> None:
+    m = device_model(golden, "target")
+    cache = new_cache(m)
+    a, b, tok = (golden[f"fwd/mixed/{k}"].tolist() for k in ("a", "b", "tok"))
+    run(m, cache, [0], [a], [0])
+    out = run(m, cache, [0, 1], [tok, b], [7, 0])
+    np.testing.assert_allclose(out, golden["fwd/mixed/logits"], **FP32_TOL)
+
+
+@pytest.mark.parametrize("block_size", [1, 2, 4, 8, 16, 64])
+def test_block_size_and_non_contiguous_tables(golden, block_size: int) -> None:
+    """Two sequences written alternately so neither owns contiguous blocks."""
+    m = device_model(golden, "target")
+    cache = new_cache(m, block_size, max(4, 512 // block_size))
+    ref = OracleModel(Dims(32, 32, 2, 4, 4, int(golden["target_cfg"][5]), 128),
+                      tiny_state(golden, "target"))
+    rng = np.random.default_rng(block_size)
+    a = rng.integers(0, 32, 23).tolist()
+    b = rng.integers(0, 32, 23).tolist()
+    ka, kb = SeqKV(), SeqKV()
+    for i in range(0, 20, 2):
+        got = run(m, cache, [0, 1], [a[i : i + 2], b[i : i + 2]], [i, i])
+        want = np.concatenate(ref.forward([a[i : i + 2], b[i : i + 2]], [ka, kb]))
+        np.testing.assert_allclose(got, want, **FP32_TOL)
+    if block_size <= 4:
+        assert cache.tables[0].blocks != sorted(cache.tables[0].blocks) or block_size >= 16
+    assert set(cache.tables[0].blocks).isdisjoint(cache.tables[1].blocks)
+
+
+def test_gqa_matches_reference_head_expansion(golden) -> None:
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    state = {k[4:]: v for k, v in golden.items() if k.startswith("gqa/blocks") or
+             k in ("gqa/embed.weight", "gqa/norm.weight", "gqa/lm_head.weight")}
+    ff = state["blocks.0.ffn.gate_proj.weight"].shape[0]
+    cfg = ModelConfig(vocab_size=48, n_layers=2, d_model=64, n_heads=8, n_kv_heads=2, d_ff=ff,
+                      max_seq_len=64)
+    m = Transformer.from_state_dict(cfg, state, DEV)
+    toks = golden["gqa/tokens"].tolist()
+    out = run(m, new_cache(m), [0], [toks], [0])
+    np.testing.assert_allclose(out, golden["gqa/logits"], **FP32_TOL)
+
+
+def _random_state(cfg, seed: int, scale_out: float = 1.0) -> dict[str, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    d, hq, hkv, dh, ff = cfg.d_model, cfg.n_heads, cfg.kv_heads, cfg.d_head, cfg.ffn_hidden
+    n = lambda *s, std=0.02: (rng.standard_normal(s) * std).astype(np.float32)  # noqa: E731
+    st = {"embed.weight": n(cfg.vocab_size, d), "norm.weight": 1 + n(d, std=0.1)}
+    st["lm_head.weight"] = st["embed.weight"]
+    for i in range(cfg.n_layers):
+        p = f"blocks.{i}."
+        st[p + "attn.q_proj.weight"] = n(hq * dh, d)
+        st[p + "attn.k_proj.weight"] = n(hkv * dh, d)
+        st[p + "attn.v_proj.weight"] = n(hkv * dh, d)
+        st[p + "attn.o_proj.weight"] = n(d, hq * dh, std=0.02 * scale_out)
+        st[p + "ffn.gate_proj.weight"] = n(ff, d)
+        st[p + "ffn.up_proj.weight"] = n(ff, d)
+        st[p + "ffn.down_proj.weight"] = n(d, ff, std=0.02 * scale_out)
+        st[p + "attn_norm.weight"] = 1 + n(d, std=0.1)
+        st[p + "ffn_norm.weight"] = 1 + n(d, std=0.1)
+    return st
+
+
+def _dims(cfg) -> Dims:
+    return Dims(cfg.vocab_size, cfg.d_model, cfg.n_layers, cfg.n_heads, cfg.kv_heads,
+                cfg.ffn_hidden, cfg.max_seq_len, cfg.rope_theta, cfg.norm_eps)
+
+
+def test_char_model_shape_matches_oracle() -> None:
+    """The d_model=128 / 4-layer char-model target with a verify-shaped batch."""
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    cfg = ModelConfig(vocab_size=65, n_layers=4, d_model=128, n_heads=4, d_ff=352, max_seq_len=512)
+    st = _random_state(cfg, 0, scale_out=10.0)
+    m = Transformer.from_state_dict(cfg, st, DEV)
+    ref = OracleModel(_dims(cfg), st)
+    cache = new_cache(m, 16, 256)
+    rng = np.random.default_rng(1)
+    prompts = [rng.integers(0, 65, int(n)).tolist() for n in (100, 37, 8, 211)]
+    kvs = [SeqKV() for _ in prompts]
+    got = run(m, cache, [0, 1, 2, 3], prompts, [0] * 4)
+    want = np.concatenate(ref.forward(prompts, kvs))
+    np.testing.assert_allclose(got, want, **FP32_TOL)
+    verify = [rng.integers(0, 65, 4).tolist() for _ in prompts]
+    got = run(m, cache, [0, 1, 2, 3], verify, [len(p) for p in prompts])
+    want = np.concatenate(ref.forward(verify, kvs))
+    np.testing.assert_allclose(got, want, **FP32_TOL)
+
+
+@pytest.mark.parametrize("dh,hkv", [(64, 2), (128, 2)])
+def test_bf16_gqa_model_matches_oracle(dh: int, hkv: int) -> None:
+    """A Llama-style bf16 model (GQA, d_head 64/128) against the float32 oracle
+    on the same bf16-rounded weights."""
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    hq = 8
+    cfg = ModelConfig(vocab_size=1000, n_layers=3, d_model=hq * dh, n_heads=hq, n_kv_heads=hkv,
+                      d_ff=1024, max_seq_len=512, dtype="bfloat16")
+    st = _random_state(cfg, 2, scale_out=5.0)
+    st = {k: torch.from_numpy(v).bfloat16().float().numpy() for k, v in st.items()}
+    m = Transformer.from_state_dict(cfg, st, DEV)
+    ref = OracleModel(_dims(cfg), st)
+    cache = new_cache(m, 16, 128)
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(0, 1000, int(n)).tolist() for n in (50, 130, 9)]
+    kvs = [SeqKV() for _ in prompts]
+    got = run(m, cache, [0, 1, 2], prompts, [0] * 3)
+    want = np.concatenate(ref.forward(prompts, kvs))
+    np.testing.assert_allclose(got, want, **BF16_TOL)
+    step = [rng.integers(0, 1000, 5).tolist() for _ in prompts]
+    got = run(m, cache, [0, 1, 2], step, [len(p) for p in prompts])
+    want = np.concatenate(ref.forward(step, kvs))
+    np.testing.assert_allclose(got, want, **BF16_TOL)
+
+
+def test_cache_write_gather_round_trip() -> None:
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import CacheConfig, ModelConfig
+
+    cfg = ModelConfig(vocab_size=32, n_layers=2, d_model=32, n_heads=4, max_seq_len=128)
+    cache = PagedKVCache(cfg, CacheConfig(8, 32), DEV)
+    n = 20
+    slots = torch.tensor(cache.append(0, n))
+    keys = torch.randn(n, 4, 8)
+    values = torch.randn(n, 4, 8)
+    cache.write(0, slots, keys, values)
+    tables, lens = cache.build_block_tables([0])
+    assert int(lens[0]) == n
+    k, v = cache.gather(0, tables, n)
+    torch.testing.assert_close(k[0].cpu(), keys)
+    torch.testing.assert_close(v[0].cpu(), values)
+    k1, _ = cache.gather(1, tables, n)
+    assert (k1 == 0).all()
+
+
+def test_device_error_word_flags_bad_slots() -> None:
+    """A slot outside the pool is skipped and reported, not written."""
+    from microserve_b200 import _lib
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import CacheConfig, ModelConfig
+
+    assert _lib.device_error() == 0
+    cfg = ModelConfig(vocab_size=32, n_layers=1, d_model=32, n_heads=4, max_seq_len=128)
+    cache = PagedKVCache(cfg, CacheConfig(8, 4), DEV)
+    cache.write(0, torch.tensor([5, 10_000]), torch.ones(2, 4, 8), torch.ones(2, 4, 8))
+    assert _lib.device_error() == 1  # kErrSlot
+    assert _lib.device_error() == 0  # read clears it

@@ -1,0 +1,148 @@
+"""The speculative step and engine on the device against the reference and the oracle."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.model import OracleModel
+from oracle.spec import OracleRequest, spec_round
+
+from .conftest import tiny_dims, tiny_state
+from .test_gpu_model import device_model
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _cache_cfg(block_size=8, num_blocks=32):
+    from microserve_b200.config import CacheConfig
+
+    return CacheConfig(block_size, num_blocks)
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_greedy_generate_matches_reference(golden, i: int) -> None:
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    prompt = golden[f"greedy/{i}/prompt"].tolist()
+    assert golden[f"greedy/{i}/dense"].tolist() == golden[f"greedy/{i}/spec1"].tolist()
+    for gamma in (1, 2, 3, 5):
+        dec = SpeculativeDecoder(target, draft, _cache_cfg(), gamma=gamma)
+        got = dec.generate(prompt, SamplingConfig(temperature=0.0, max_new_tokens=20))
+        assert got == golden[f"greedy/{i}/spec{gamma}"].tolist()
+        assert [dec.num_accepted, dec.num_proposed] == golden[f"greedy/{i}/spec{gamma}_counts"].tolist()
+        assert dec.draft_cache.num_free_blocks == dec.draft_cache.cfg.num_blocks
+
+
+@pytest.mark.parametrize("gamma", [1, 3, 5])
+def test_engine_speculative_matches_reference(golden, gamma: int) -> None:
+    from microserve_b200.config import (CacheConfig, EngineConfig, SamplingConfig,
+                                        SchedulerConfig, SpeculativeConfig)
+    from microserve_b200.engine import LLMEngine
+
+    from .test_gpu_model import tiny_model_cfg
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    cfg = EngineConfig(model=tiny_model_cfg(golden, "target"),
+                       cache=CacheConfig(block_size=8, num_blocks=128),
+                       scheduler=SchedulerConfig(max_batch_size=3),
+                       speculative=SpeculativeConfig(enabled=True, gamma=gamma))
+    eng = LLMEngine(target, cfg, draft_model=draft)
+    reqs = [eng.add_request(golden[f"engine/prompt/{j}"].tolist(),
+                            SamplingConfig(temperature=0.0, max_new_tokens=16)) for j in range(3)]
+    outs = {o.request_id: o.output_ids for o in eng.run()}
+    for j, r in enumerate(reqs):
+        assert outs[r.request_id] == golden[f"engine/g{gamma}/{j}"].tolist()
+    assert [eng.stats.num_draft_accepted, eng.stats.num_draft_proposed] == \
+        golden[f"engine/g{gamma}/counts"].tolist()
+    assert eng.cache.num_free_blocks == cfg.cache.num_blocks
+    assert eng.spec.draft_cache.num_free_blocks == cfg.cache.num_blocks
+    eng.cache.allocator.check_invariants()
+
+
+def test_rollback_restores_the_engine_invariant(golden) -> None:
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.scheduler import Request
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    dec = SpeculativeDecoder(target, draft, _cache_cfg(), gamma=4)
+    cache = PagedKVCache(target.cfg, _cache_cfg(), DEV)
+    request = Request(0, [1, 2, 3, 4], SamplingConfig(temperature=0.0, max_new_tokens=40))
+    gens = {0: torch.Generator().manual_seed(0)}
+    for _ in range(5):
+        tokens = dec.step([request], cache, gens)[0]
+        request.output_ids.extend(tokens)
+        assert cache.num_tokens(0) == request.num_tokens - 1
+        assert request.num_computed == request.num_tokens - 1
+    cache.free(0)
+    dec.free(0)
+    cache.allocator.check_invariants()
+    assert dec.draft_cache.num_free_blocks == dec.draft_cache.cfg.num_blocks
+
+
+def test_exact_token_budgets(golden) -> None:
+    from microserve_b200.config import (CacheConfig, EngineConfig, SamplingConfig,
+                                        SchedulerConfig, SpeculativeConfig)
+    from microserve_b200.engine import LLMEngine
+
+    from .test_gpu_model import tiny_model_cfg
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    cfg = EngineConfig(model=tiny_model_cfg(golden, "target"), cache=CacheConfig(8, 128),
+                       scheduler=SchedulerConfig(max_batch_size=2),
+                       speculative=SpeculativeConfig(enabled=True, gamma=5))
+    eng = LLMEngine(target, cfg, draft_model=draft)
+    budgets = {}
+    for b in (1, 2, 3, 7, 13):
+        r = eng.add_request([1, 2, 3], SamplingConfig(temperature=0.0, max_new_tokens=b))
+        budgets[r.request_id] = b
+    for out in eng.run():
+        assert len(out.output_ids) == budgets[out.request_id]
+
+
+@pytest.mark.parametrize("setting", [(0.8, None, None), (1.0, 5, 0.9), (0.8, None, 0.9)])
+def test_sampled_rounds_match_oracle_draw_for_draw(golden, setting) -> None:
+    """Sampled streams are exact given shared uniforms: proposals, accepted
+    lengths and emitted tokens per round, for a batch of requests."""
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.scheduler import Request
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    t, k, p = setting
+    gamma = 3
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    o_t = OracleModel(tiny_dims(golden, "target"), tiny_state(golden, "target"))
+    o_d = OracleModel(tiny_dims(golden, "draft"), tiny_state(golden, "draft"))
+    dec = SpeculativeDecoder(target, draft, _cache_cfg(8, 64), gamma=gamma)
+    cache = PagedKVCache(target.cfg, _cache_cfg(8, 64), DEV)
+    rng = np.random.default_rng(4)
+    sc = SamplingConfig(temperature=t, top_k=k, top_p=p, max_new_tokens=64)
+    prompts = [rng.integers(0, 32, int(n)).tolist() for n in (5, 12, 3, 9)]
+    reqs = [Request(i, pr, sc) for i, pr in enumerate(prompts)]
+    gens = {i: torch.Generator().manual_seed(500 + i) for i in range(len(reqs))}
+    oreqs = [OracleRequest(i, pr, t, k, p, seed=500 + i) for i, pr in enumerate(prompts)]
+    diverged = set()
+    for _ in range(6):
+        live = [i for i in range(len(reqs)) if i not in diverged]
+        if not live:
+            break
+        got = dec.step([reqs[i] for i in live], cache, gens)
+        tr = spec_round(o_t, o_d, gamma, [oreqs[i] for i in live])
+        for j, i in enumerate(live):
+            if got[j] != tr.emitted[j]:
+                # a draw or roll that sits within float rounding of a CDF step
+                # may legitimately go the other way; it must stay rare
+                diverged.add(i)
+                continue
+            reqs[i].output_ids.extend(got[j])
+            oreqs[i].output_ids.extend(tr.emitted[j])
+            assert cache.num_tokens(i) == reqs[i].num_tokens - 1
+    assert len(diverged) <= 1

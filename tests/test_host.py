@@ -1,0 +1,238 @@
+"""Host-side logic without a GPU: allocator, tables, rollback, scheduler, configs.
+
+Cases follow reference tests/test_cache.py and tests/test_scheduler.py.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from microserve_b200.cache import BlockAllocator, OutOfCacheMemory, PagedKVCache
+from microserve_b200.config import (CacheConfig, EngineConfig, ModelConfig, SamplingConfig,
+                                    SchedulerConfig, SpeculativeConfig, load_config)
+from microserve_b200.scheduler import Request, Scheduler
+
+
+def host_cache(block_size: int = 8, num_blocks: int = 32) -> PagedKVCache:
+    cfg = ModelConfig(vocab_size=32, n_layers=2, d_model=32, n_heads=4, max_seq_len=128)
+    return PagedKVCache(cfg, CacheConfig(block_size, num_blocks), device="cpu")
+
+
+class TestAllocator:
+    def test_round_trip(self) -> None:
+        a = BlockAllocator(4)
+        blocks = [a.allocate() for _ in range(4)]
+        assert blocks == [3, 2, 1, 0]  # pops from the end, as the reference
+        assert a.num_free == 0
+        for b in blocks:
+            a.free(b)
+        assert a.num_free == 4
+        a.check_invariants()
+
+    def test_exhaustion_and_double_free(self) -> None:
+        a = BlockAllocator(2)
+        a.allocate_many(2)
+        with pytest.raises(OutOfCacheMemory):
+            a.allocate()
+        with pytest.raises(OutOfCacheMemory):
+            a.allocate_many(1)
+        a.free(0)
+        with pytest.raises(ValueError, match="double free"):
+            a.free(0)
+
+    def test_refcounts(self) -> None:
+        a = BlockAllocator(2)
+        b = a.allocate()
+        a.incref(b)
+        a.free(b)
+        assert a.num_free == 1
+        a.free(b)
+        assert a.num_free == 2
+        with pytest.raises(ValueError):
+            a.incref(b)
+
+    def test_allocate_many_matches_sequential_allocation(self) -> None:
+        a, b = BlockAllocator(10), BlockAllocator(10)
+        assert a.allocate_many(4) == [b.allocate() for _ in range(4)]
+
+
+class TestCacheTables:
+    def test_slots_follow_the_block_table(self) -> None:
+        c = host_cache(block_size=4)
+        slots = c.append(0, 6)
+        blocks = c.tables[0].blocks
+        assert slots == [blocks[p // 4] * 4 + p % 4 for p in range(6)]
+        assert c.num_tokens(0) == 6
+
+    def test_blocks_needed_is_exact(self) -> None:
+        c = host_cache(block_size=8)
+        assert c.blocks_needed(0, 1) == 1
+        assert c.blocks_needed(0, 8) == 1
+        assert c.blocks_needed(0, 9) == 2
+        c.append(0, 5)
+        assert c.blocks_needed(0, 3) == 0
+        assert c.blocks_needed(0, 4) == 1
+
+    def test_can_append_reports_exhaustion(self) -> None:
+        c = host_cache(block_size=4, num_blocks=2)
+        assert c.can_append(0, 8)
+        assert not c.can_append(0, 9)
+
+    def test_truncate_releases_tail_blocks(self) -> None:
+        c = host_cache()
+        total = c.num_free_blocks
+        c.append(0, 24)
+        assert c.num_free_blocks == total - 3
+        c.truncate(0, 9)
+        assert c.num_free_blocks == total - 2
+        assert c.num_tokens(0) == 9
+        c.allocator.check_invariants()
+
+    def test_truncate_cannot_grow(self) -> None:
+        c = host_cache()
+        c.append(0, 4)
+        with pytest.raises(ValueError, match="cannot grow"):
+            c.truncate(0, 5)
+
+    def test_append_after_truncate_reuses_the_partial_block(self) -> None:
+        c = host_cache()
+        c.append(0, 24)
+        c.truncate(0, 9)
+        before = c.tables[0].blocks
+        slots = c.append(0, 3)
+        assert c.num_tokens(0) == 12
+        assert len(slots) == 3
+        assert c.tables[0].blocks == before
+        assert slots == [before[1] * 8 + p for p in (1, 2, 3)]
+
+    def test_free_and_reset(self) -> None:
+        c = host_cache()
+        total = c.num_free_blocks
+        c.append(0, 10)
+        c.append(1, 3)
+        c.free(999)  # unknown: no-op
+        c.free(0)
+        assert 0 not in c.tables
+        c.reset()
+        assert c.num_free_blocks == total
+        assert c.tables == {}
+        c.allocator.check_invariants()
+
+    def test_append_many_is_all_or_nothing(self) -> None:
+        c = host_cache(block_size=4, num_blocks=3)
+        c.append(0, 4)
+        with pytest.raises(OutOfCacheMemory):
+            c.append_many([0, 1], [4, 8])  # 1 + 2 blocks, 2 free
+        assert c.num_tokens(0) == 4
+        assert c.num_free_blocks == 2
+
+    def test_vectorised_paths_match_single_calls(self) -> None:
+        rng = np.random.default_rng(0)
+        a, b = host_cache(4, 64), host_cache(4, 64)
+        ids = [3, 1, 7]
+        for _ in range(6):
+            counts = rng.integers(1, 6, 3)
+            got = a.append_many(ids, counts).tolist()
+            want = [s for i, n in zip(ids, counts) for s in b.append(i, int(n))]
+            assert got == want
+            keep = [max(0, a.num_tokens(i) - int(rng.integers(0, 4))) for i in ids]
+            a.truncate_many(ids, keep)
+            for i, k in zip(ids, keep):
+                b.truncate(i, k)
+            assert a.tables == b.tables
+        a.allocator.check_invariants()
+
+    def test_table_rows_and_block_tables(self) -> None:
+        c = host_cache(block_size=2)
+        c.append(0, 5)
+        c.append(1, 1)
+        tables, lens = c.build_block_tables([0, 1])
+        assert tables.shape == (2, 3)
+        assert lens.tolist() == [5, 1]
+        assert tables[1, 1:].tolist() == [0, 0]
+
+    def test_tensor_methods_need_a_device(self) -> None:
+        import torch
+
+        c = host_cache()
+        with pytest.raises(RuntimeError, match="CUDA"):
+            c.write(0, torch.zeros(1, dtype=torch.long), torch.zeros(1, 4, 8), torch.zeros(1, 4, 8))
+
+
+class TestScheduler:
+    def _sched(self, **kw) -> tuple[Scheduler, PagedKVCache]:
+        c = host_cache(block_size=4, num_blocks=kw.pop("num_blocks", 16))
+        return Scheduler(SchedulerConfig(**kw), c), c
+
+    def test_admission_never_over_commits(self) -> None:
+        s, c = self._sched(max_batch_size=8, num_blocks=8)
+        for i in range(6):
+            s.add(Request(i, [1] * 9, SamplingConfig()))
+        out = s.schedule(0.0)
+        need = sum(c.blocks_needed(r.request_id, r.num_uncomputed) for r in out.scheduled)
+        assert need <= c.num_free_blocks
+
+    def test_fcfs_order_and_batch_cap(self) -> None:
+        s, _ = self._sched(max_batch_size=2)
+        for i, t in enumerate([3.0, 1.0, 2.0]):
+            s.add(Request(i, [1, 2], SamplingConfig(), arrival_time=t))
+        out = s.schedule(0.0)
+        assert [r.request_id for r in out.scheduled] == [1, 2]
+
+    def test_speculative_reservation(self) -> None:
+        s, c = self._sched(max_batch_size=4, num_blocks=4)
+        s.tokens_per_step = 6
+        for i in range(3):
+            s.add(Request(i, [1], SamplingConfig()))
+        out = s.schedule(0.0)
+        # each request reserves ceil(6/4) = 2 blocks of the 4
+        assert len(out.scheduled) == 2
+
+    def test_preemption_frees_the_victim(self) -> None:
+        s, c = self._sched(max_batch_size=4, num_blocks=4)
+        reqs = [Request(i, [1] * 4, SamplingConfig(), arrival_time=float(i)) for i in range(2)]
+        for r in reqs:
+            s.add(r)
+        out = s.schedule(0.0)
+        for r in out.scheduled:
+            c.append(r.request_id, r.num_uncomputed)
+            r.num_computed = r.num_tokens
+            r.output_ids.extend([1] * 8)  # each now needs 2 more blocks; 2 are free
+        out = s.schedule(1.0)
+        assert out.preempted and out.preempted[0].request_id == 1
+        assert out.preempted[0].num_computed == 0
+        assert c.num_tokens(1) == 0
+
+    def test_request_tail(self) -> None:
+        r = Request(0, [1, 2, 3], SamplingConfig(), output_ids=[4, 5])
+        for s in range(6):
+            assert r.tail(s) == r.all_ids[s:]
+
+
+class TestConfig:
+    def test_defaults_follow_the_reference(self) -> None:
+        m = ModelConfig()
+        assert m.d_ff == 352 and m.n_kv_heads == 4 and m.d_head == 32
+        assert ModelConfig(d_model=64, n_heads=2).d_ff == 160
+        assert SamplingConfig(temperature=0.0).greedy
+        assert CacheConfig().num_slots == 16 * 512
+
+    def test_validation(self) -> None:
+        with pytest.raises(ValueError):
+            ModelConfig(d_model=30, n_heads=4)
+        with pytest.raises(ValueError):
+            ModelConfig(n_heads=4, n_kv_heads=3)
+        with pytest.raises(ValueError):
+            SchedulerConfig(policy="nope")
+        with pytest.raises(ValueError):
+            ModelConfig(dtype="float16")
+
+    def test_round_trip(self, tmp_path) -> None:
+        cfg = EngineConfig(model=ModelConfig(n_kv_heads=2, dtype="bfloat16"),
+                           speculative=SpeculativeConfig(enabled=True, gamma=3))
+        p = tmp_path / "e.json"
+        cfg.save(p)
+        assert load_config(p) == cfg
+        with pytest.raises(ValueError, match="unknown config key"):
+            EngineConfig.from_dict({"bogus": 1})

@@ -1,0 +1,157 @@
+"""Pin the CPU oracle against the reference's own outputs (tests/golden)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import philox
+from oracle.model import Dims, OracleModel, SeqKV
+from oracle.sampling import Row, draw, filter_row, verify, verify_probs
+from oracle.spec import OracleRequest, spec_round
+
+from .conftest import tiny_dims, tiny_state
+
+TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+def test_philox_known_answers() -> None:
+    """Random123 philox4x32_10 known-answer vectors."""
+    cases = [
+        ((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+        ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+        ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+         (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)),
+    ]
+    for ctr, key, want in cases:
+        got = tuple(int(x) for x in philox.philox4x32_10(ctr, key))
+        assert got == want
+
+
+def test_uniforms_in_unit_interval_and_lane_independent() -> None:
+    u = philox.uniform(1234, np.arange(10000), 0)
+    assert u.dtype == np.float32 and u.min() >= 0.0 and u.max() < 1.0
+    assert abs(float(u.mean()) - 0.5) < 0.01
+    v = philox.uniform(1234, np.arange(10000), 64)
+    assert np.corrcoef(u, v)[0, 1] < 0.05
+
+
+def _model(golden, which: str) -> OracleModel:
+    return OracleModel(tiny_dims(golden, which), tiny_state(golden, which))
+
+
+@pytest.mark.parametrize("case", ["prefill11", "unequal"])
+def test_forward_matches_reference(golden, case: str) -> None:
+    m = _model(golden, "target")
+    toks = golden[f"fwd/{case}/tokens"].tolist()
+    lens = golden[f"fwd/{case}/lens"].tolist()
+    seqs, o = [], 0
+    for n in lens:
+        seqs.append(toks[o : o + n])
+        o += n
+    out = np.concatenate(m.forward(seqs, [SeqKV() for _ in seqs]))
+    np.testing.assert_allclose(out, golden[f"fwd/{case}/logits"], **TOL)
+
+
+def test_mixed_prefill_decode_matches_reference(golden) -> None:
+    m = _model(golden, "target")
+    a, b, tok = (golden[f"fwd/mixed/{k}"].tolist() for k in ("a", "b", "tok"))
+    ka, kb = SeqKV(), SeqKV()
+    m.forward([a], [ka])
+    out = np.concatenate(m.forward([tok, b], [ka, kb]))
+    np.testing.assert_allclose(out, golden["fwd/mixed/logits"], **TOL)
+
+
+def _dense_greedy(m: OracleModel, prompt: list[int], n: int) -> list[int]:
+    kv = SeqKV()
+    cur, out = list(prompt), []
+    for _ in range(n):
+        logits = m.forward([cur], [kv], logit_rows=[[len(cur) - 1]])[0][0]
+        t = int(np.argmax(logits))
+        out.append(t)
+        cur = [t]
+    return out
+
+
+@pytest.mark.parametrize("i", [0, 1, 2])
+def test_greedy_dense_and_speculative_match_reference(golden, i: int) -> None:
+    tgt, drf = _model(golden, "target"), _model(golden, "draft")
+    prompt = golden[f"greedy/{i}/prompt"].tolist()
+    assert _dense_greedy(tgt, prompt, 20) == golden[f"greedy/{i}/dense"].tolist()
+    for gamma in (1, 2, 3, 5):
+        r = OracleRequest(0, prompt, 0.0, None, None, seed=0)
+        while len(r.output_ids) < 20:
+            tr = spec_round(tgt, drf, gamma, [r])
+            for t in tr.emitted[0]:
+                if len(r.output_ids) >= 20:
+                    break
+                r.output_ids.append(t)
+        assert r.output_ids == golden[f"greedy/{i}/spec{gamma}"].tolist()
+        acc, prop = golden[f"greedy/{i}/spec{gamma}_counts"].tolist()
+        assert (r.num_accepted, r.num_proposed) == (acc, prop)
+
+
+@pytest.mark.parametrize("vocab", [32, 1000])
+def test_filters_match_reference(golden, vocab: int) -> None:
+    logits = golden[f"filter/v{vocab}/logits"]
+    for si, (t, k, p) in enumerate(golden["filter/settings"].tolist()):
+        want = golden[f"filter/v{vocab}/s{si}"]
+        for r in range(logits.shape[0]):
+            row = filter_row(logits[r], t, None if k < 0 else int(k), None if p < 0 else p)
+            np.testing.assert_allclose(row.probs, want[r], rtol=1e-5, atol=1e-7)
+
+
+def test_verify_deterministic_cases(golden) -> None:
+    toks, n = verify_probs(np.array([[1.0, 0.0], [1.0, 0.0]]), np.array([[0.5, 0.5]]), [0],
+                           np.array([0.3], np.float32), 0.5)
+    assert [n, *toks] == golden["verify/dominates"].tolist()
+    toks, n = verify_probs(np.array([[1.0, 0.0], [1.0, 0.0]]), np.array([[0.0, 1.0]]), [1],
+                           np.array([0.3], np.float32), 0.5)
+    assert [n, *toks] == golden["verify/impossible"].tolist()
+
+
+def test_gqa_equals_reference_head_expansion(golden) -> None:
+    state = {k[4:]: v for k, v in golden.items() if k.startswith("gqa/blocks") or
+             k in ("gqa/embed.weight", "gqa/norm.weight", "gqa/lm_head.weight")}
+    ff = state["blocks.0.ffn.gate_proj.weight"].shape[0]
+    dims = Dims(vocab_size=48, d_model=64, n_layers=2, n_heads=8, n_kv_heads=2, d_ff=ff,
+                max_seq_len=64)
+    m = OracleModel(dims, state)
+    toks = golden["gqa/tokens"].tolist()
+    out = m.forward([toks], [SeqKV()])[0]
+    np.testing.assert_allclose(out, golden["gqa/logits"], rtol=1e-4, atol=1e-5)
+
+
+def test_draw_is_inverse_cdf() -> None:
+    w = np.array([0.0, 0.25, 0.0, 0.5, 0.25], np.float32)
+    assert draw(w, 0.0) == 1
+    assert draw(w, 0.2499) == 1
+    assert draw(w, 0.25) == 3
+    assert draw(w, 0.7499) == 3
+    assert draw(w, 0.75) == 4
+    assert draw(w, 0.99999994) == 4
+
+
+def test_rejection_rule_is_unbiased() -> None:
+    """gamma=1: emitted token ~ p_target for any q (speculative.py's proof, on the oracle)."""
+    rng = np.random.default_rng(5)
+    V = 8
+    q = rng.random(V).astype(np.float32) + 1e-3
+    q /= q.sum()
+    p = rng.random(V).astype(np.float32) + 1e-3
+    p /= p.sum()
+    n = 30000
+    us = philox.uniform(99, np.arange(n), 0)
+    ua = philox.uniform(99, np.arange(n), 64)
+    ud = philox.uniform(99, np.arange(n), 128)
+    counts = np.zeros(V)
+    for i in range(n):
+        x = draw(q, float(us[i]))
+        toks, _ = verify([Row(p, 1.0), Row(p, 1.0)], [Row(q, 1.0)], [x], ua[i : i + 1], float(ud[i]))
+        counts[toks[0]] += 1
+    from scipy.stats import chisquare
+
+    expected = p.astype(np.float64) / p.astype(np.float64).sum() * counts.sum()
+    assert chisquare(counts, expected).pvalue > 0.01
+    biased = np.bincount([draw(q, float(u)) for u in us], minlength=V)
+    assert chisquare(biased, expected).pvalue < 0.01
