@@ -27,7 +27,8 @@ __global__ void __launch_bounds__(kWarps * 32)
                      const int32_t* __restrict__ context_lens, const int32_t* __restrict__ positions,
                      const int32_t* __restrict__ tables, int max_blocks, int bs, int num_blocks,
                      int hq, int hkv, float scale, T* __restrict__ out, int* __restrict__ err) {
-  constexpr int PER_LANE = DH / 32;
+  // Lane l owns output dims l, l+32, ...; for d_head < 32 lanes >= DH idle.
+  constexpr int PER_LANE = DH >= 32 ? DH / 32 : 1;
   constexpr int kRowsPerWarp = rows_per_warp<DH>();
   constexpr int kRowsPerCta = kWarps * kRowsPerWarp;
   __shared__ float Qs[kRowsPerCta][DH];
@@ -119,7 +120,8 @@ __global__ void __launch_bounds__(kWarps * 32)
       for (int kk = 0; kk < kChunk; ++kk) {
         const float pk = __shfl_sync(0xffffffffu, p, kk);
 #pragma unroll
-        for (int e = 0; e < PER_LANE; ++e) acc[i][e] = fmaf(pk, Vs[kk][lane + 32 * e], acc[i][e]);
+        for (int e = 0; e < PER_LANE; ++e)
+          if (DH >= 32 || lane < DH) acc[i][e] = fmaf(pk, Vs[kk][lane + 32 * e], acc[i][e]);
       }
       m[i] = mn;
     }
@@ -132,7 +134,8 @@ __global__ void __launch_bounds__(kWarps * 32)
     const float inv = l[i] > 0.f ? 1.f / l[i] : 0.f;
     T* o = out + ((int64_t)(t0 + t) * hq + h) * DH;
 #pragma unroll
-    for (int e = 0; e < PER_LANE; ++e) o[lane + 32 * e] = from_f<T>(acc[i][e] * inv);
+    for (int e = 0; e < PER_LANE; ++e)
+      if (DH >= 32 || lane < DH) o[lane + 32 * e] = from_f<T>(acc[i][e] * inv);
   }
 }
 
@@ -155,10 +158,12 @@ template <typename T>
 int attn_by_dh(const void* q, int q_stride, const ms_kv_cache& c, int layer, const ms_batch& bt,
                int hq, void* out, cudaStream_t s) {
   switch (c.d_head) {
+    case 8: return launch_attn<T, 8>(q, q_stride, c, layer, bt, hq, out, s);
+    case 16: return launch_attn<T, 16>(q, q_stride, c, layer, bt, hq, out, s);
     case 32: return launch_attn<T, 32>(q, q_stride, c, layer, bt, hq, out, s);
     case 64: return launch_attn<T, 64>(q, q_stride, c, layer, bt, hq, out, s);
     case 128: return launch_attn<T, 128>(q, q_stride, c, layer, bt, hq, out, s);
-    default: return fail(MS_ERR_UNSUPPORTED, "paged_attention: d_head %d (32/64/128)", c.d_head);
+    default: return fail(MS_ERR_UNSUPPORTED, "paged_attention: d_head %d (8/16/32/64/128)", c.d_head);
   }
 }
 
