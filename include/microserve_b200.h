@@ -221,6 +221,25 @@ MS_API int ms_forward(const ms_model* model, const ms_kv_cache* cache,
                int n_logit_rows, float* logits, int64_t logits_row_stride,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* ms_forward without a caller-provided workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory (a
+ * host that reaches this library only through an FFI and has no CUDA
+ * allocator of its own, or a running serving loop that must not call
+ * cudaMalloc).  Its scratch is an array compiled into the library, 16 MiB
+ * per device, held by every GPU that loads the library until exit; a batch
+ * whose workspace (ms_forward_workspace_size) exceeds it is rejected with
+ * MS_ERR_TOO_LARGE before anything is launched.  The first call on a device
+ * looks up the array's device address (make it before any stream capture).
+ * All calls on a device share the array, so calls that overlap on the GPU
+ * race; nothing in it needs clearing between calls.  Arguments and results
+ * are those of ms_forward. */
+MS_API int ms_forward_static_scratch(const ms_model* model,
+                                     const ms_kv_cache* cache,
+                                     const ms_batch* batch,
+                                     const int32_t* logit_rows,
+                                     int n_logit_rows, float* logits,
+                                     int64_t logits_row_stride, void* stream);
+
 /* ---- building blocks, exported for tests and for callers that compose
  *      their own forward ---------------------------------------------- */
 /* y[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * w  (reference model.py:77-79);

@@ -142,6 +142,11 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [POINTER(MsModel), POINTER(MsKVCache), POINTER(MsBatch), c_void_p, c_int, c_void_p,
          c_int64, c_void_p, c_size_t, c_void_p],
     ),
+    "ms_forward_static_scratch": (
+        c_int,
+        [POINTER(MsModel), POINTER(MsKVCache), POINTER(MsBatch), c_void_p, c_int, c_void_p,
+         c_int64, c_void_p],
+    ),
     "ms_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int,
                            c_void_p]),
     "ms_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int,
