@@ -1,14 +1,423 @@
-// tcgen05 tensor-core GEMM for bf16 (sm_100a).  Not wired in yet: every
-// bf16 shape currently takes the CUDA-core kernel.
+// tcgen05 tensor-core GEMM for bf16 (sm_100a): C = A[M,K] * B[N,K]^T, float32
+// accumulation in tensor memory.
+//
+// One CTA per 128 x BN output tile (BN = 128 or 256), 128 threads:
+//   warp 0 lane 0  TMA producer: K-major 128B-swizzled tiles of A (128 x 64)
+//                  and B (BN x 64) into a STAGES-deep shared-memory ring;
+//   warp 1         allocates BN TMEM columns; lane 0 issues
+//                  tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) four
+//                  times per stage and tcgen05.commit frees the stage;
+//   all 4 warps    epilogue: tcgen05.ld 32x32b (warp w owns TMEM lanes
+//                  32w..32w+31 = tile rows), fused store / residual add /
+//                  SwiGLU, vectorised global stores.
+// Loads are plain TMA tile loads of this GPU's memory (no multicast).  Every
+// mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA records
+// kErrTimeout in the device error word, drains its own copies, frees its
+// TMEM and returns.
+#include <cuda.h>
+
+#include <mutex>
+#include <unordered_map>
+
 #include "gemm.cuh"
 
 namespace ms {
+namespace {
 
-bool gemm_tc_supported(int, int, int, int64_t, int, int) { return false; }
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
+constexpr int kThreads = 128;
+constexpr long long kWaitCycles = 1ll << 32;  // ~2.2 s at 1.965 GHz
+constexpr int kErrTimeout = 5;
 
-int gemm_tc(const void*, const void*, void*, const float*, int, int, int, int64_t, int, int,
-            cudaStream_t) {
-  return fail(MS_ERR_UNSUPPORTED, "gemm_tc: not available");
+template <int BN> struct TileCfg {
+  static constexpr int kStages = BN == 128 ? 6 : 4;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: false on timeout or when another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+  uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
+  d |= (uint64_t)1 << 46;                 // version
+  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M=128.
+template <int BN> __device__ __forceinline__ uint32_t idesc() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+         ((uint32_t)(BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Epilogue for one thread's 32 consecutive columns [n, n+32) of row m.
+template <int EPI, typename TC>
+__device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const float* R, int m,
+                                            int n, int N, int64_t ldc) {
+  if constexpr (EPI == kEpiSwiGLU) {
+    // columns [16g, 16g+8) gate, [16g+8, 16g+16) up -> outputs 8g..8g+7
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n / 2;
+    uint32_t w[8];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float g0 = v[16 * g + j], g1 = v[16 * g + j + 1];
+        const float u0 = v[16 * g + 8 + j], u1 = v[16 * g + 8 + j + 1];
+        const float s0 = g0 / (1.f + expf(-g0)) * u0;
+        const float s1 = g1 / (1.f + expf(-g1)) * u1;
+        w[g * 4 + j / 2] = pack_bf16(s0, s1);
+      }
+    }
+    if (n + 32 <= N) {
+      uint4* o = reinterpret_cast<uint4*>(out);
+      o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+  } else if constexpr (EPI == kEpiResidual) {
+    float* out = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+    const float* res = R + (int64_t)m * ldc + n;
+    if (n + 32 <= N) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        const float4 r4 = *reinterpret_cast<const float4*>(res + i);
+        *reinterpret_cast<float4*>(out + i) =
+            make_float4(r4.x + v[i], r4.y + v[i + 1], r4.z + v[i + 2], r4.w + v[i + 3]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (n + i < N) out[i] = res[i] + v[i];
+    }
+  } else if constexpr (sizeof(TC) == 4) {
+    float* out = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+    if (n + 32 <= N) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (n + i < N) out[i] = v[i];
+    }
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
+    if (n + 32 <= N) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        *reinterpret_cast<uint4*>(out + i) =
+            make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
+                       pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (n + i < N) out[i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+template <int BN, int EPI, typename TC>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                   const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
+                   const float* __restrict__ R, int M, int N, int K, int64_t ldc, int* err) {
+  using Cfg = TileCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  unsigned char* smem = smem_raw + pad;
+  const uint32_t sbase = raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, done = full0 + 16 * S;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int num_k = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    int issued = 0;
+    for (int kt = 0; kt < num_k; ++kt) {
+      const int s = kt % S;
+      if (kt >= S && !mbar_wait(empty0 + 8 * s, ((kt / S) - 1) & 1, abort_flag, err)) break;
+      const uint32_t a_dst = sbase + s * Cfg::kStageBytes;
+      const uint32_t b_dst = a_dst + Cfg::kABytes;
+      mbar_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
+      tma_load_2d(a_dst, &tmap_a, full0 + 8 * s, kt * BK, m0);
+      tma_load_2d(b_dst, &tmap_b, full0 + 8 * s, kt * BK, n0);
+      ++issued;
+    }
+    if (*abort_flag) {
+      // drain the loads this thread may still have in flight before exiting
+      const long long t0 = clock64();
+      for (int kt = issued > S ? issued - S : 0; kt < issued; ++kt)
+        while (!mbar_try_wait(full0 + 8 * (kt % S), (kt / S) & 1) && clock64() - t0 < kWaitCycles) {
+        }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    const uint32_t id = idesc<BN>();
+    for (int kt = 0; kt < num_k; ++kt) {
+      const int s = kt % S;
+      if (!mbar_wait(full0 + 8 * s, (kt / S) & 1, abort_flag, err)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t a_addr = sbase + s * Cfg::kStageBytes;
+      const uint32_t b_addr = a_addr + Cfg::kABytes;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk)
+        umma(tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), id, (kt | kk) != 0);
+      umma_commit(empty0 + 8 * s);
+    }
+    umma_commit(done);
+  }
+  __syncwarp();
+
+  // ---- epilogue: every warp drains its 32 TMEM lanes ----
+  const bool ok = mbar_wait(done, 0, abort_flag, err) && !*abort_flag;
+  __syncwarp();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (ok) {
+    const int m = m0 + warp * 32 + lane;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld32(lane_base + c, v);
+      const int n = n0 + c;
+      if (m < M && n < N) store_chunk<EPI, TC>(v, C, R, m, n, N, ldc);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+  }
+}
+
+// ---- host side ------------------------------------------------------------------------
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* ptr;
+  int rows, cols, box_rows, dev;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && box_rows == o.box_rows &&
+           dev == o.dev;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<const void*>()(k.ptr) ^ ((size_t)k.rows << 1) ^ ((size_t)k.cols << 21) ^
+           ((size_t)k.box_rows << 41) ^ ((size_t)k.dev << 53);
+  }
+};
+
+// A row-major (rows x cols) bf16 matrix as a K-major 2-D tensor map with a
+// (64 x box_rows) box and 128-byte swizzle.  Cached: weights and the
+// forward's workspace keep their addresses from call to call.
+int tensor_map(const void* ptr, int rows, int cols, int box_rows, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const MapKey key{ptr, rows, cols, box_rows, dev};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return MS_OK;
+  }
+  EncodeFn enc = encode_fn();
+  if (!enc) return fail(MS_ERR_CUDA, "gemm_tc: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MS_ERR_CUDA, "gemm_tc: tensor map encode failed (%d)", (int)r);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, map);
+  *out = map;
+  return MS_OK;
+}
+
+template <int BN, int EPI, typename TC>
+int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
+              int64_t ldc, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  MS_TRY(tensor_map(A, M, K, BM, &ta));
+  MS_TRY(tensor_map(B, N, K, BN, &tb));
+  using Cfg = TileCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, EPI, TC>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    if (e != cudaSuccess) return fail(MS_ERR_CUDA, "gemm_tc: smem attribute: %s", cudaGetErrorString(e));
+    attr_set = true;
+  }
+  dim3 grid(ceil_div(N, BN), ceil_div(M, BM));
+  kern<<<grid, kThreads, Cfg::kSmem, s>>>(ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
+                                          device_error_word());
+  return check_launch("gemm_tc_kernel");
+}
+
+}  // namespace
+
+bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi) {
+  if (M <= 0 || K % 8 != 0 || N % 128 != 0) return false;
+  if (epi == kEpiResidual && c_dtype != MS_DTYPE_F32) return false;
+  const int64_t align = (epi == kEpiSwiGLU || c_dtype == MS_DTYPE_BF16) ? 8 : 4;
+  return ldc % align == 0;
+}
+
+int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K, int64_t ldc,
+            int c_dtype, int epi, cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
+       reinterpret_cast<uintptr_t>(C)) & 15)
+    return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
+  if (epi == kEpiSwiGLU) return launch_tc<128, kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, s);
+  if (epi == kEpiResidual) return launch_tc<128, kEpiResidual, float>(A, B, C, R, M, N, K, ldc, s);
+  if (c_dtype == MS_DTYPE_F32) return launch_tc<128, kEpiStore, float>(A, B, C, R, M, N, K, ldc, s);
+  return launch_tc<128, kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, s);
 }
 
 }  // namespace ms
