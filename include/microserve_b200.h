@@ -197,8 +197,10 @@ typedef struct {
 typedef struct {
   int32_t n_tokens;
   int32_t n_seqs;
-  int32_t max_blocks; /* row stride of block_tables */
+  int32_t max_blocks;  /* row stride of block_tables */
   int32_t max_q_len;
+  int32_t max_context; /* max of context_lens; 0 = unknown (bounded by the table) */
+  int32_t reserved_;
   const int32_t* input_ids;
   const int32_t* positions;
   const int32_t* slot_mapping;

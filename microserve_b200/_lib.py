@@ -98,6 +98,8 @@ class MsBatch(ctypes.Structure):
         ("n_seqs", c_int32),
         ("max_blocks", c_int32),
         ("max_q_len", c_int32),
+        ("max_context", c_int32),
+        ("reserved_", c_int32),
         ("input_ids", c_void_p),
         ("positions", c_void_p),
         ("slot_mapping", c_void_p),

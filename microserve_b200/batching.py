@@ -71,6 +71,7 @@ def batch_from_host(
     width: int,
     max_q: int,
     n_tokens: int,
+    max_context: int = 0,
 ) -> PagedBatch:
     """Device views of a packed [ids, positions, slots, q_start, ctx, q_lens, tables] blob."""
     v = [dev_blob[o : o + n] for o, n in spans]
@@ -84,6 +85,7 @@ def batch_from_host(
         block_tables=v[6].view(n_seqs, width),
         max_q=max_q,
         n_tokens=n_tokens,
+        max_context=max_context,
     )
 
 
@@ -139,7 +141,8 @@ def build_paged_batch(
         dev_blob = staging.upload(blob)
     else:
         dev_blob = torch.from_numpy(blob).to(dev)
-    return batch_from_host(dev_blob, spans, len(seq_ids), width, max_q, n_tokens)
+    return batch_from_host(dev_blob, spans, len(seq_ids), width, max_q, n_tokens,
+                           int(parts[4].max()) if len(seq_ids) else 0)
 
 
 def last_token_rows(q_lens: torch.Tensor) -> torch.Tensor:

@@ -9,6 +9,7 @@
 // accumulator) for up to kRowsPerWarp rows.
 #include <cfloat>
 
+#include "attention_tc.cuh"
 #include "common.cuh"
 #include "model_kernels.cuh"
 
@@ -170,13 +171,20 @@ int attn_by_dh(const void* q, int q_stride, const ms_kv_cache& c, int layer, con
 }  // namespace
 
 int paged_attention(const void* q, int q_stride, const ms_kv_cache& c, int layer,
-                    const ms_batch& bt, int hq, void* out, cudaStream_t s) {
+                    const ms_batch& bt, int hq, void* out, void* scratch, size_t scratch_bytes,
+                    cudaStream_t s) {
   if (bt.n_seqs == 0 || bt.n_tokens == 0) return MS_OK;
   if (hq % c.n_kv_heads != 0)
     return fail(MS_ERR_INVALID, "paged_attention: n_heads %d not a multiple of n_kv_heads %d", hq,
                 c.n_kv_heads);
   if (bt.max_q_len <= 0) return fail(MS_ERR_INVALID, "paged_attention: max_q_len must be > 0");
   ProfScope prof(kClsAttention, s);
+  if (attn_tc_supported(c, hq) && q_stride % 8 == 0) {
+    const int table_bound = bt.max_blocks * c.block_size;
+    const int max_ctx = bt.max_context > 0 ? min(bt.max_context, table_bound) : table_bound;
+    return paged_attention_tc(q, q_stride, c, layer, bt, hq, out, max_ctx, scratch, scratch_bytes,
+                              s);
+  }
   if (c.dtype == MS_DTYPE_F32) return attn_by_dh<float>(q, q_stride, c, layer, bt, hq, out, s);
   if (c.dtype == MS_DTYPE_BF16)
     return attn_by_dh<__nv_bfloat16>(q, q_stride, c, layer, bt, hq, out, s);
@@ -193,6 +201,6 @@ extern "C" int ms_paged_attention(const void* q, const ms_kv_cache* cache, int l
   MS_REQUIRE(batch != nullptr && q && out, "ms_paged_attention: null pointer");
   MS_REQUIRE(batch->q_start && batch->context_lens && batch->positions && batch->block_tables,
              "ms_paged_attention: batch has null arrays");
-  return paged_attention(q, n_heads * cache->d_head, *cache, layer, *batch, n_heads, out,
-                         as_stream(stream));
+  return paged_attention(q, n_heads * cache->d_head, *cache, layer, *batch, n_heads, out, nullptr,
+                         0, as_stream(stream));
 }

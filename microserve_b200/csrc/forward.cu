@@ -97,6 +97,9 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
   const int d = m.d_model, hq = m.n_heads, hkv = m.n_kv_heads, dh = m.d_head;
   const int qkv_w = (hq + 2 * hkv) * dh;
   const int dt = m.dtype;
+  // workspace past the carve is scratch for the attention's split-KV partials
+  void* attn_scratch = static_cast<unsigned char*>(workspace) + w.bytes;
+  const size_t attn_scratch_bytes = workspace_bytes - w.bytes;
 
   MS_TRY(embed_rmsnorm(m.embed, bt.input_ids, T, m.vocab_size, d, m.attn_norm[0], m.norm_eps, w.x,
                        w.xn, dt, s));
@@ -105,7 +108,8 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
     MS_TRY(rope_kv_write(w.qkv, bt.positions, bt.slot_mapping, m.rope_cos, m.rope_sin, m.max_seq_len,
                          T, hq, hkv, dh, c, l, dt, s));
     // q occupies the first hq*dh columns of each qkv row.
-    MS_TRY(paged_attention(w.qkv, qkv_w, c, l, bt, hq, w.attn, s));
+    MS_TRY(paged_attention(w.qkv, qkv_w, c, l, bt, hq, w.attn, attn_scratch, attn_scratch_bytes,
+                           s));
     MS_TRY(gemm_dispatch(w.attn, m.w_o[l], w.x, w.x, T, d, hq * dh, 0, dt, MS_DTYPE_F32,
                          kEpiResidual, s));
     MS_TRY(rmsnorm(w.x, m.ffn_norm[l], w.xn, nullptr, T, d, m.norm_eps, dt, s));

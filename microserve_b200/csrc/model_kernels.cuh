@@ -14,7 +14,9 @@ int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, con
 int validate_cache(const ms_kv_cache* c, int layer);
 // Paged attention (attention.cu).  q: token t's head h at q + t*q_stride +
 // h*dh; out: (T, hq*dh).
+// `scratch` (may be null) holds split-KV partials for the tensor-core path.
 int paged_attention(const void* q, int q_stride, const ms_kv_cache& cache, int layer,
-                    const ms_batch& batch, int hq, void* out, cudaStream_t s);
+                    const ms_batch& batch, int hq, void* out, void* scratch, size_t scratch_bytes,
+                    cudaStream_t s);
 
 }  // namespace ms

@@ -266,7 +266,8 @@ class LLMEngine:
         self._last_q_start = parts[3]
         blob, spans = pack_int32(parts)
         dev_blob = self._staging.upload(blob)
-        return batch_from_host(dev_blob, spans, len(ids), width, max_q, n_tokens)
+        return batch_from_host(dev_blob, spans, len(ids), width, max_q, n_tokens,
+                               int(parts[4].max()))
 
     # -- results ------------------------------------------------------------------
     def make_output(self, request: Request) -> RequestOutput:

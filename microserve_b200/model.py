@@ -49,6 +49,7 @@ class PagedBatch:
     q_start: torch.Tensor  # (B + 1,) int32 prefix sums of q_lens
     max_q: int
     n_tokens: int
+    max_context: int = 0  # max of context_lens (0: unknown, bounded by the table)
 
     @property
     def batch_size(self) -> int:
@@ -69,6 +70,8 @@ class PagedBatch:
             self.batch_size,
             int(self.block_tables.shape[1]),
             self.max_q,
+            self.max_context,
+            0,
             self.input_ids.data_ptr(),
             self.positions.data_ptr(),
             self.slot_mapping.data_ptr(),
@@ -101,6 +104,12 @@ def split_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     two_ff, d = w.shape
     v = w.reshape(two_ff // 16, 2, 8, d)
     return v[:, 0].reshape(-1, d), v[:, 1].reshape(-1, d)
+
+
+# Workspace bytes past ms_forward's own carve; the attention kernel uses them
+# for split-KV partials when a batch has too few (sequence, kv head) tiles to
+# fill the GPU (otherwise it runs one KV range per tile and needs none).
+ATTN_SCRATCH_BYTES = 32 << 20
 
 
 class Transformer:
@@ -239,6 +248,7 @@ class Transformer:
     def workspace(self, n_tokens: int, n_rows: int) -> torch.Tensor:
         need = int(_lib.load().ms_forward_workspace_size(ctypes.byref(self._c_model), n_tokens,
                                                            n_rows))
+        need += ATTN_SCRATCH_BYTES
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
         return self._ws

@@ -268,6 +268,8 @@ class SpeculativeDecoder:
         return {
             "blob": blob, "spans": spans, "B": B, "dw": dw, "tw": tw, "T0": T0, "Tv": Tv,
             "max_q0": int(n0.max()), "max_qv": int((npre + G).max()),
+            "ctx0": int(ctx0.max()), "ctxv": int(ctxv.max()),
+            "ctx_j": [int(c.max()) for c in ctx_j],
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
         }
 
@@ -283,7 +285,7 @@ class SpeculativeDecoder:
         params = v[0]
         k = 1
         b0 = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["dw"]), int(plan["max_q0"]),
-                             int(plan["T0"]))
+                             int(plan["T0"]), int(plan["ctx0"]))  # type: ignore[arg-type]
         dtab = v[k + 6].view(B, int(plan["dw"]))
         k += 7
         rows0 = v[k]
@@ -297,11 +299,11 @@ class SpeculativeDecoder:
             bj = PagedBatch(
                 input_ids=buf.proposals[j - 1], positions=pos, slot_mapping=slots,
                 block_tables=dtab, context_lens=ctx, q_lens=ones, q_start=unit_qs, max_q=1,
-                n_tokens=B,
+                n_tokens=B, max_context=plan["ctx_j"][j - 1],  # type: ignore[index]
             )
             batches.append((bj, None))
         bv = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["tw"]), int(plan["max_qv"]),
-                             int(plan["Tv"]))
+                             int(plan["Tv"]), int(plan["ctxv"]))  # type: ignore[arg-type]
         k += 7
         rowsv = v[k]
         k += 1

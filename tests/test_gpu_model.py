@@ -179,6 +179,31 @@ def test_bf16_gqa_model_matches_oracle(dh: int, hkv: int) -> None:
     np.testing.assert_allclose(got, want, **BF16_TOL)
 
 
+def test_bf16_long_context_split_kv_matches_oracle() -> None:
+    """Few sequences with long contexts: the attention splits each context
+    into KV ranges and merges their partials (decode/verify after a prefill)."""
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    cfg = ModelConfig(vocab_size=512, n_layers=2, d_model=512, n_heads=8, n_kv_heads=2,
+                      d_ff=512, max_seq_len=2048, dtype="bfloat16")
+    st = _random_state(cfg, 6, scale_out=5.0)
+    st = {k: torch.from_numpy(v).bfloat16().float().numpy() for k, v in st.items()}
+    m = Transformer.from_state_dict(cfg, st, DEV)
+    ref = OracleModel(_dims(cfg), st)
+    cache = new_cache(m, 16, 256)
+    rng = np.random.default_rng(7)
+    prompts = [rng.integers(0, 512, int(n)).tolist() for n in (1500, 700)]
+    kvs = [SeqKV() for _ in prompts]
+    got = run(m, cache, [0, 1], prompts, [0, 0])
+    want = np.concatenate(ref.forward(prompts, kvs))
+    np.testing.assert_allclose(got, want, **BF16_TOL)
+    step = [rng.integers(0, 512, 5).tolist() for _ in prompts]
+    got = run(m, cache, [0, 1], step, [len(p) for p in prompts])
+    want = np.concatenate(ref.forward(step, kvs))
+    np.testing.assert_allclose(got, want, **BF16_TOL)
+
+
 def test_cache_write_gather_round_trip() -> None:
     from microserve_b200.cache import PagedKVCache
     from microserve_b200.config import CacheConfig, ModelConfig

@@ -49,6 +49,6 @@ def test_struct_layouts_match_the_header() -> None:
     from microserve_b200 import _lib
 
     assert ctypes.sizeof(_lib.MsKVCache) == 6 * 4 + 2 * 8
-    assert ctypes.sizeof(_lib.MsBatch) == 4 * 4 + 6 * 8
+    assert ctypes.sizeof(_lib.MsBatch) == 6 * 4 + 6 * 8
     assert _lib.SAMPLING_PARAMS_DTYPE.itemsize == 32
     assert _lib.ROW_STATS_DTYPE.itemsize == 16
