@@ -258,6 +258,13 @@ MS_API int ms_gemm(const void* A, const void* B, void* C, const float* R, int M,
             int N, int K, int64_t ldc, int ab_dtype, int c_dtype,
             int epilogue, void* stream);
 
+/* Scratch bytes the tensor-core attention would use for split-KV partials on
+ * this batch.  ms_forward uses workspace bytes past
+ * ms_forward_workspace_size() for them; with fewer it runs one KV range per
+ * tile (same results, less parallelism).  No reference counterpart. */
+MS_API size_t ms_attention_scratch_size(const ms_kv_cache* cache, int n_heads,
+                                        const ms_batch* batch);
+
 /* Paged attention over one layer: q (T, n_heads, d_head) in `dtype`, causal
  * by absolute position (key j visible to a query at position p iff j <= p;
  * reference model.py:200-221), output (T, n_heads*d_head) in `dtype`. */

@@ -182,6 +182,9 @@ int paged_attention(const void* q, int q_stride, const ms_kv_cache& c, int layer
   if (attn_tc_supported(c, hq) && q_stride % 8 == 0) {
     const int table_bound = bt.max_blocks * c.block_size;
     const int max_ctx = bt.max_context > 0 ? min(bt.max_context, table_bound) : table_bound;
+    if (attn_tma_supported(c, hq))
+      return paged_attention_tma(q, q_stride, c, layer, bt, hq, out, max_ctx, scratch,
+                                 scratch_bytes, s);
     return paged_attention_tc(q, q_stride, c, layer, bt, hq, out, max_ctx, scratch, scratch_bytes,
                               s);
   }
@@ -203,4 +206,18 @@ extern "C" int ms_paged_attention(const void* q, const ms_kv_cache* cache, int l
              "ms_paged_attention: batch has null arrays");
   return paged_attention(q, n_heads * cache->d_head, *cache, layer, *batch, n_heads, out, nullptr,
                          0, as_stream(stream));
+}
+
+extern "C" size_t ms_attention_scratch_size(const ms_kv_cache* cache, int n_heads,
+                                            const ms_batch* batch) {
+  if (cache == nullptr || batch == nullptr || n_heads <= 0 || cache->n_kv_heads <= 0) return 0;
+  if (!attn_tc_supported(*cache, n_heads) || batch->n_seqs <= 0 || batch->max_q_len <= 0) return 0;
+  const int table_bound = batch->max_blocks * cache->block_size;
+  const int max_ctx =
+      batch->max_context > 0 ? min(batch->max_context, table_bound) : table_bound;
+  int row_tiles = 0, n_splits = 1, split_len = 0;
+  attn_tc_plan(batch->max_q_len, n_heads / cache->n_kv_heads, max_ctx, batch->n_seqs,
+               cache->n_kv_heads, &row_tiles, &n_splits, &split_len);
+  return attn_tc_scratch_bytes(batch->n_seqs, cache->n_kv_heads, cache->d_head, row_tiles,
+                               n_splits);
 }

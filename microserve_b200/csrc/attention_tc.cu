@@ -380,15 +380,20 @@ size_t attn_tc_scratch_bytes(int n_seqs, int hkv, int dh, int row_tiles, int n_s
 void attn_tc_plan(int max_q_len, int group, int max_context, int n_seqs, int hkv, int* row_tiles,
                   int* n_splits, int* split_len) {
   *row_tiles = (max_q_len * group + kRows - 1) / kRows;
-  // aim for ~4 CTAs per SM over 148 SMs; ranges are whole 64-key chunks
+  // Split the KV range only when the (sequence, kv head, row tile) units do
+  // not fill one wave (148 SMs x 3 resident CTAs): a split costs a partials
+  // round trip and a combine launch, which a full grid does not recover.
+  // At least 256 keys per range; ranges are whole 64-key chunks.
   const int units = n_seqs * hkv * *row_tiles;
-  int splits = 1;
-  if (units < 600 && max_context > 256) splits = (600 + units - 1) / units;
-  const int by_len = (max_context + 255) / 256;  // at least 256 keys per range
+  const int wave = 148 * 3;
+  int splits = units < wave ? (2 * wave + units - 1) / units : 1;
+  const int by_len = (max_context + 255) / 256;
   splits = max(1, min(splits, min(by_len, 32)));
   int len = (max_context + splits - 1) / splits;
   len = ((len + kChunk - 1) / kChunk) * kChunk;
+  if (len <= 0) len = kChunk;
   *n_splits = (max_context + len - 1) / len;
+  if (*n_splits < 1) *n_splits = 1;
   *split_len = len;
 }
 

@@ -1,0 +1,575 @@
+// Paged attention for bf16 caches with TMA tile loads (sm_100a).
+//
+// Same work decomposition and arithmetic as attention_tc.cu (one CTA per
+// (64-row query tile, kv head, sequence, KV range); the GQA query heads of a
+// kv head share M), but the K/V traffic is moved by the tensor memory
+// accelerator instead of per-thread cp.async:
+//   warp 4 lane 0  producer: for each 64-key chunk, looks up the chunk's
+//                  blocks in the block table and issues one 2-D TMA load per
+//                  (block, kv head, 64-column half) of K and of V into a
+//                  STAGES-deep ring, 128-byte swizzled, completing on the
+//                  stage's "full" mbarrier;
+//   warps 0-3      consumers: wait "full", S = Q K^T and O += P V with
+//                  ldmatrix (swizzle-aware addresses) + mma.sync m16n8k16,
+//                  online softmax, then arrive on the stage's "empty" barrier.
+// The pools are viewed as 2-D tensors [num_blocks * n_kv_heads * block_size
+// rows][d_head columns]; a (block, kv head) tile is block_size consecutive
+// rows.  No multicast; only this GPU's memory is read.  Every mbarrier wait
+// is bounded and reports kErrTimeout through the device error word.
+#include <cuda.h>
+
+#include <cfloat>
+#include <mutex>
+#include <unordered_map>
+
+#include "attention_tc.cuh"
+#include "model_kernels.cuh"
+
+namespace ms {
+namespace {
+
+constexpr int kRows = 64;
+constexpr int kChunk = 64;
+constexpr int kConsumers = 4;
+constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr long long kWaitCycles = 1ll << 32;
+constexpr int kErrTimeout = 5;
+constexpr int kTblCap = 64;  // block-table entries staged per refill (multiple of 8)
+
+template <int DH> struct TmaCfg {
+  static constexpr int kHalves = DH / 64;                  // 128-byte column halves
+  static constexpr int kStages = DH == 64 ? 4 : 3;
+  static constexpr int kTileBytes = kChunk * DH * 2;       // one operand, one chunk
+  static constexpr int kStageBytes = 2 * kTileBytes;       // K + V
+  static constexpr int kLdQ = DH + 8;
+  static constexpr int kQBytes = kRows * kLdQ * 2;
+  static constexpr int kSmem =
+      1024 + kStages * kStageBytes + kQBytes + kRows * 4 + 128 + kTblCap * 4;
+};
+
+__device__ __forceinline__ uint32_t s_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      atomicCAS(err, 0, kErrTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                       uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldm_x4_t(uint32_t addr, uint32_t& a, uint32_t& b, uint32_t& c,
+                                         uint32_t& d) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(a), "=r"(b), "=r"(c), "=r"(d)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+// Address of the 16-byte chunk `c` (0 .. DH/8-1) of key row `k` (0..63) in a
+// swizzled operand tile: half c/8, row k of 128 bytes, chunk (c%8) ^ (k%8).
+template <int DH>
+__device__ __forceinline__ uint32_t tile_addr(uint32_t tile, int k, int c) {
+  return tile + (uint32_t)((c >> 3) * (kChunk * 128) + k * 128 + (((c & 7) ^ (k & 7)) << 4));
+}
+
+struct TmaArgs {
+  const __nv_bfloat16* q;
+  int q_stride;
+  const int32_t* q_start;
+  const int32_t* context_lens;
+  const int32_t* positions;
+  const int32_t* tables;
+  int max_blocks, bs, log2_bs, num_blocks, hq, hkv, row_tiles, n_splits, split_len;
+  float scale_log2;
+  __nv_bfloat16* out;
+  float* part_o;
+  float* part_ml;
+  int* err;
+};
+
+template <int DH>
+__global__ void __launch_bounds__(kThreads)
+    attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                    TmaArgs a) {
+  using Cfg = TmaCfg<DH>;
+  constexpr int S = Cfg::kStages;
+  constexpr int NT = DH / 8;
+  constexpr int LDQ = Cfg::kLdQ;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = s_addr(smem_raw);
+  unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  const uint32_t stage0 = s_addr(smem);
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem + S * Cfg::kStageBytes);
+  int* rowpos = reinterpret_cast<int*>(smem + S * Cfg::kStageBytes + Cfg::kQBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(rowpos + kRows);
+  const uint32_t full0 = s_addr(bars), empty0 = full0 + 8 * S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * S);
+  int* tbl = reinterpret_cast<int*>(smem + S * Cfg::kStageBytes + Cfg::kQBytes + kRows * 4 + 128);
+
+  const int split = blockIdx.x % a.n_splits, rt = blockIdx.x / a.n_splits;
+  const int g = blockIdx.y, b = blockIdx.z;
+  const int group = a.hq / a.hkv;
+  const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
+  const int nrows = qlen * group;
+  const int r0 = rt * kRows;
+  if (r0 >= nrows) return;
+  const int nr = min(kRows, nrows - r0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  for (int r = threadIdx.x; r < kRows; r += kThreads)
+    rowpos[r] = r < nr ? a.positions[t0 + (r0 + r) / group] : -1;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kConsumers);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  // Stage tiles start zeroed: key rows a chunk never loads must hold finite
+  // values (their probabilities are 0, and 0 * NaN would poison O).
+  for (int i = threadIdx.x; i < S * Cfg::kStageBytes / 16; i += kThreads)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  // Q tile (zero rows past nr).
+  for (int idx = threadIdx.x; idx < kRows * (DH / 8); idx += kThreads) {
+    const int r = idx / (DH / 8), c = (idx % (DH / 8)) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nr) {
+      const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+      v = *reinterpret_cast<const uint4*>(a.q + (int64_t)(t0 + t) * a.q_stride + h * DH + c);
+    }
+    *reinterpret_cast<uint4*>(Qs + r * LDQ + c) = v;
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeros before TMA writes
+  __syncthreads();
+
+  int kmax = 0;
+  for (int r = 0; r < nr; ++r) kmax = max(kmax, rowpos[r] + 1);
+  kmax = min(kmax, a.context_lens[b]);
+  const int splits_here = max(1, (kmax + a.split_len - 1) / a.split_len);
+  if (split >= splits_here) return;
+  const int kbeg = split * a.split_len;
+  const int kend = min(kmax, kbeg + a.split_len);
+  const int nchunks = (kend - kbeg + kChunk - 1) / kChunk;
+
+  if (warp == kConsumers) {
+    // ---- producer: block-table slice staged in smem, one lane issues TMA ----
+    const int32_t* table = a.tables + (int64_t)b * a.max_blocks;
+    const int bpc = kChunk >> a.log2_bs;  // blocks per chunk
+    const int first_blk = kbeg >> a.log2_bs;
+    const int n_blk = (kend - kbeg + a.bs - 1) >> a.log2_bs;
+    int issued = 0;
+    bool stop = false;
+    for (int base = 0; base < n_blk && !stop; base += kTblCap) {
+      const int cnt = min(kTblCap, n_blk - base);
+      __syncwarp();
+      for (int i = lane; i < cnt; i += 32) {
+        int blk = table[first_blk + base + i];
+        if (blk < 0 || blk >= a.num_blocks) {
+          atomicCAS(a.err, 0, (int)kErrBlock);
+          blk = 0;
+        }
+        tbl[i] = blk;
+      }
+      __syncwarp();
+      if (lane == 0) {
+        const int ch_end = min(nchunks, (base + cnt + bpc - 1) / bpc);
+        for (int ch = base / bpc; ch < ch_end; ++ch) {
+          const int s = ch % S;
+          if (ch >= S && !mbar_wait(empty0 + 8 * s, ((ch / S) - 1) & 1, abort_flag, a.err)) {
+            stop = true;
+            break;
+          }
+          const int j0 = kbeg + ch * kChunk;
+          const int nb = (min(kend, j0 + kChunk) - j0 + a.bs - 1) >> a.log2_bs;
+          mbar_expect_tx(full0 + 8 * s, (uint32_t)(nb * a.bs * DH * 2 * 2));
+          const uint32_t kdst = stage0 + s * Cfg::kStageBytes;
+          const uint32_t vdst = kdst + Cfg::kTileBytes;
+          const int t0b = ch * bpc - base;
+          for (int i = 0; i < nb; ++i) {
+            const int y = (tbl[t0b + i] * a.hkv + g) * a.bs;
+            const uint32_t off = (uint32_t)(i * a.bs * 128);
+#pragma unroll
+            for (int h = 0; h < Cfg::kHalves; ++h) {
+              tma_load_2d(kdst + h * kChunk * 128 + off, &kmap, full0 + 8 * s, h * 64, y);
+              tma_load_2d(vdst + h * kChunk * 128 + off, &vmap, full0 + 8 * s, h * 64, y);
+            }
+          }
+          ++issued;
+        }
+      }
+      stop = __shfl_sync(0xffffffffu, stop ? 1 : 0, 0) != 0;
+    }
+    if (lane == 0 && *abort_flag) {
+      const long long t0c = clock64();
+      for (int ch = issued > S ? issued - S : 0; ch < issued; ++ch)
+        while (!mbar_try_wait(full0 + 8 * (ch % S), (ch / S) & 1) && clock64() - t0c < kWaitCycles) {
+        }
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  const int wr = warp * 16;
+  const int ra = wr + (lane >> 2), rb = ra + 8;
+  const int pos_a = rowpos[ra], pos_b = rowpos[rb];
+  const bool live = wr < nr;
+  float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+  float o[NT][4];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  bool ok = true;
+  for (int ch = 0; ch < nchunks && ok; ++ch) {
+    const int s = ch % S;
+    ok = mbar_wait(full0 + 8 * s, (ch / S) & 1, abort_flag, a.err);
+    if (!ok) break;
+    if (live) {
+      const uint32_t Kt = stage0 + s * Cfg::kStageBytes;
+      const uint32_t Vt = Kt + Cfg::kTileBytes;
+      float sc[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+#pragma unroll
+      for (int k0 = 0; k0 < DH; k0 += 16) {
+        uint32_t a0, a1, a2, a3;
+        ldm_x4(s_addr(Qs + (wr + (lane & 15)) * LDQ + k0 + (lane >> 4) * 8), a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < 8; nt += 2) {
+          uint32_t b0, b1, b2, b3;
+          const int key = nt * 8 + (lane & 7) + ((lane >> 4) << 3);
+          const int c = (k0 >> 3) + ((lane >> 3) & 1);
+          ldm_x4(tile_addr<DH>(Kt, key, c), b0, b1, b2, b3);
+          mma_bf16(sc[nt], a0, a1, a2, a3, b0, b1);
+          mma_bf16(sc[nt + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+      const int jbase = kbeg + ch * kChunk + 2 * (lane & 3);
+      float mx_a = -INFINITY, mx_b = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int j = jbase + nt * 8 + e;
+          const bool va = j < kend && j <= pos_a, vb = j < kend && j <= pos_b;
+          sc[nt][e] = va ? sc[nt][e] * a.scale_log2 : -INFINITY;
+          sc[nt][2 + e] = vb ? sc[nt][2 + e] * a.scale_log2 : -INFINITY;
+          mx_a = fmaxf(mx_a, sc[nt][e]);
+          mx_b = fmaxf(mx_b, sc[nt][2 + e]);
+        }
+      }
+#pragma unroll
+      for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+        mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o_));
+        mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o_));
+      }
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float al_a = mn_a == -INFINITY ? 1.f : exp2f(m_a - mn_a);
+      const float al_b = mn_b == -INFINITY ? 1.f : exp2f(m_b - mn_b);
+      float ps_a = 0.f, ps_b = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          sc[nt][e] = mn_a == -INFINITY ? 0.f : exp2f(sc[nt][e] - mn_a);
+          sc[nt][2 + e] = mn_b == -INFINITY ? 0.f : exp2f(sc[nt][2 + e] - mn_b);
+          ps_a += sc[nt][e];
+          ps_b += sc[nt][2 + e];
+        }
+      }
+      l_a = l_a * al_a + ps_a;
+      l_b = l_b * al_b + ps_b;
+      m_a = mn_a;
+      m_b = mn_b;
+#pragma unroll
+      for (int i = 0; i < NT; ++i) {
+        o[i][0] *= al_a;
+        o[i][1] *= al_a;
+        o[i][2] *= al_b;
+        o[i][3] *= al_b;
+      }
+#pragma unroll
+      for (int kt = 0; kt < 4; ++kt) {
+        const uint32_t p0 = pack2(sc[2 * kt][0], sc[2 * kt][1]);
+        const uint32_t p1 = pack2(sc[2 * kt][2], sc[2 * kt][3]);
+        const uint32_t p2 = pack2(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
+        const uint32_t p3 = pack2(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
+        const int key = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldm_x4_t(tile_addr<DH>(Vt, key, nt + (lane >> 4)), b0, b1, b2, b3);
+          mma_bf16(o[nt], p0, p1, p2, p3, b0, b1);
+          mma_bf16(o[nt + 1], p0, p1, p2, p3, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+  }
+  if (!live || !ok) return;
+
+#pragma unroll
+  for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+    l_a += __shfl_xor_sync(0xffffffffu, l_a, o_);
+    l_b += __shfl_xor_sync(0xffffffffu, l_b, o_);
+  }
+  const int col = 2 * (lane & 3);
+  if (splits_here == 1) {
+    const float ia = l_a > 0.f ? 1.f / l_a : 0.f, ib = l_b > 0.f ? 1.f / l_b : 0.f;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = half ? rb : ra;
+      if (r >= nr) continue;
+      const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+      __nv_bfloat16* dst = a.out + ((int64_t)(t0 + t) * a.hq + h) * DH + col;
+      const float inv = half ? ib : ia;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<uint32_t*>(dst + nt * 8) =
+            pack2(o[nt][2 * half] * inv, o[nt][2 * half + 1] * inv);
+    }
+  } else {
+    const int64_t unit = (((int64_t)b * a.hkv + g) * a.row_tiles + rt) * a.n_splits + split;
+    float* po = a.part_o + unit * kRows * DH;
+    float* pml = a.part_ml + unit * kRows * 2;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = half ? rb : ra;
+      if (r >= nr) continue;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        *reinterpret_cast<float2*>(po + r * DH + nt * 8 + col) =
+            make_float2(o[nt][2 * half], o[nt][2 * half + 1]);
+      if ((lane & 3) == 0) {
+        pml[r * 2] = half ? m_b : m_a;
+        pml[r * 2 + 1] = half ? l_b : l_a;
+      }
+    }
+  }
+}
+
+// ---- host ----------------------------------------------------------------------
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                              const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                              const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                              CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn encode_fn() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(p);
+  });
+  return fn;
+}
+
+struct PoolKey {
+  const void* ptr;
+  int64_t rows;
+  int dh, bs, dev;
+  bool operator==(const PoolKey& o) const {
+    return ptr == o.ptr && rows == o.rows && dh == o.dh && bs == o.bs && dev == o.dev;
+  }
+};
+struct PoolKeyHash {
+  size_t operator()(const PoolKey& k) const {
+    return std::hash<const void*>()(k.ptr) ^ ((size_t)k.rows << 7) ^ ((size_t)k.dh << 40) ^
+           ((size_t)k.bs << 50) ^ ((size_t)k.dev << 58);
+  }
+};
+
+// The pool as [rows][dh] bf16 with (64 x block_size) boxes, 128-byte swizzle.
+int pool_map(const void* pool, int64_t rows, int dh, int bs, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::unordered_map<PoolKey, CUtensorMap, PoolKeyHash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const PoolKey key{pool, rows, dh, bs, dev};
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return MS_OK;
+  }
+  EncodeFn enc = encode_fn();
+  if (!enc) return fail(MS_ERR_CUDA, "attn_tma: cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {(cuuint64_t)dh, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)dh * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)bs};
+  const cuuint32_t estr[2] = {1, 1};
+  CUtensorMap map;
+  const CUresult r = enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MS_ERR_CUDA, "attn_tma: tensor map encode failed (%d)", (int)r);
+  if (cache.size() > 4096) cache.clear();
+  cache.emplace(key, map);
+  *out = map;
+  return MS_OK;
+}
+
+__global__ void attn_tma_combine_kernel(TmaArgs a, int dh) {
+  const int rt = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int group = a.hq / a.hkv;
+  const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
+  const int nrows = qlen * group;
+  const int r0 = rt * kRows;
+  if (r0 >= nrows) return;
+  const int nr = min(kRows, nrows - r0);
+  int kmax = 0;
+  for (int r = 0; r < nr; ++r) kmax = max(kmax, a.positions[t0 + (r0 + r) / group] + 1);
+  kmax = min(kmax, a.context_lens[b]);
+  const int splits = max(1, (kmax + a.split_len - 1) / a.split_len);
+  if (splits == 1) return;
+  const int64_t unit0 = (((int64_t)b * a.hkv + g) * a.row_tiles + rt) * a.n_splits;
+  for (int idx = threadIdx.x; idx < nr * dh; idx += blockDim.x) {
+    const int r = idx / dh, d = idx % dh;
+    float mx = -INFINITY;
+    for (int s = 0; s < splits; ++s) mx = fmaxf(mx, a.part_ml[((unit0 + s) * kRows + r) * 2]);
+    float l = 0.f, acc = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float ms = a.part_ml[((unit0 + s) * kRows + r) * 2];
+      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mx);
+      l += w * a.part_ml[((unit0 + s) * kRows + r) * 2 + 1];
+      acc += w * a.part_o[(unit0 + s) * kRows * dh + r * dh + d];
+    }
+    const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+    a.out[((int64_t)(t0 + t) * a.hq + h) * dh + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+  }
+}
+
+template <int DH>
+int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
+               cudaStream_t s) {
+  using Cfg = TmaCfg<DH>;
+  static bool attr = false;
+  if (!attr) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        attn_tma_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    if (e != cudaSuccess) return fail(MS_ERR_CUDA, "attn_tma: smem attribute: %s", cudaGetErrorString(e));
+    attr = true;
+  }
+  dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
+  attn_tma_kernel<DH><<<grid, kThreads, Cfg::kSmem, s>>>(km, vm, a);
+  MS_TRY(check_launch("attn_tma_kernel"));
+  if (a.n_splits > 1) {
+    attn_tma_combine_kernel<<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a, DH);
+    MS_TRY(check_launch("attn_tma_combine_kernel"));
+  }
+  return MS_OK;
+}
+
+}  // namespace
+
+bool attn_tma_supported(const ms_kv_cache& c, int hq) {
+  const int bs = c.block_size;
+  const bool pow2 = bs >= 8 && bs <= 64 && (bs & (bs - 1)) == 0;
+  const int64_t rows = (int64_t)c.num_blocks * c.n_kv_heads * bs;
+  return c.dtype == MS_DTYPE_BF16 && (c.d_head == 64 || c.d_head == 128) && pow2 &&
+         hq % c.n_kv_heads == 0 && rows < (1ll << 31);
+}
+
+int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int layer,
+                        const ms_batch& bt, int hq, void* out, int max_context, void* scratch,
+                        size_t scratch_bytes, cudaStream_t s) {
+  if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15 || q_stride % 8)
+    return fail(MS_ERR_INVALID, "attn_tma: q/out must be 16-byte aligned");
+  TmaArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_stride;
+  a.q_start = bt.q_start;
+  a.context_lens = bt.context_lens;
+  a.positions = bt.positions;
+  a.tables = bt.block_tables;
+  a.max_blocks = bt.max_blocks;
+  a.bs = c.block_size;
+  a.log2_bs = __builtin_ctz((unsigned)c.block_size);
+  a.num_blocks = c.num_blocks;
+  a.hq = hq;
+  a.hkv = c.n_kv_heads;
+  attn_tc_plan(bt.max_q_len, hq / c.n_kv_heads, max_context, bt.n_seqs, c.n_kv_heads,
+               &a.row_tiles, &a.n_splits, &a.split_len);
+  a.scale_log2 = kLog2e / sqrtf((float)c.d_head);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.err = device_error_word();
+  const size_t need =
+      attn_tc_scratch_bytes(bt.n_seqs, c.n_kv_heads, c.d_head, a.row_tiles, a.n_splits);
+  if (need > scratch_bytes) {
+    a.n_splits = 1;
+    a.split_len = ((max_context + kChunk - 1) / kChunk) * kChunk;
+    if (a.split_len <= 0) a.split_len = kChunk;
+  } else if (need > 0) {
+    const size_t units = (size_t)bt.n_seqs * a.hkv * a.row_tiles * a.n_splits;
+    a.part_o = static_cast<float*>(scratch);
+    a.part_ml = a.part_o + units * kRows * c.d_head;
+  }
+  const int64_t rows = (int64_t)c.num_blocks * c.n_kv_heads * c.block_size;
+  CUtensorMap km, vm;
+  MS_TRY(pool_map(c.k_pool[layer], rows, c.d_head, c.block_size, &km));
+  MS_TRY(pool_map(c.v_pool[layer], rows, c.d_head, c.block_size, &vm));
+  if (c.d_head == 64) return launch_tma<64>(a, km, vm, bt.n_seqs, s);
+  return launch_tma<128>(a, km, vm, bt.n_seqs, s);
+}
+
+}  // namespace ms

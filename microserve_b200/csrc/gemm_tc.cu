@@ -1,15 +1,22 @@
-// tcgen05 tensor-core GEMM for bf16 (sm_100a): C = A[M,K] * B[N,K]^T, float32
-// accumulation in tensor memory.
+// tcgen05 tensor-core GEMM for bf16 (sm_100a): C = A[M,K] * B[N,K]^T with
+// float32 accumulation in tensor memory.  Persistent and warp-specialised.
 //
-// One CTA per 128 x BN output tile (BN = 128 or 256), 128 threads:
-//   warp 0 lane 0  TMA producer: K-major 128B-swizzled tiles of A (128 x 64)
-//                  and B (BN x 64) into a STAGES-deep shared-memory ring;
-//   warp 1         allocates BN TMEM columns; lane 0 issues
-//                  tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) four
-//                  times per stage and tcgen05.commit frees the stage;
-//   all 4 warps    epilogue: tcgen05.ld 32x32b (warp w owns TMEM lanes
-//                  32w..32w+31 = tile rows), fused store / residual add /
-//                  SwiGLU, vectorised global stores.
+// Grid: one CTA per SM (at most), 192 threads:
+//   warp 0 lane 0  TMA producer: K-major 128B-swizzled A (128 x 64) and B
+//                  (BN x 64) tiles into a STAGES-deep shared-memory ring;
+//   warp 1         allocates 2 x BN TMEM columns (a double-buffered
+//                  accumulator); lane 0 issues tcgen05.mma.cta_group::1
+//                  .kind::f16 (M=128, N=BN, K=16), commits each stage back to
+//                  the producer and each finished accumulator to the epilogue;
+//   warps 2-5      epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
+//                  32*(w%4)..+31 = tile rows), fused store / SwiGLU / residual
+//                  reduction, while the MMA warp fills the other accumulator.
+// Work: output tiles are dealt round-robin to the CTAs; for the in-place
+// residual GEMM (C += A B^T, R == C) the (tile, k-step) space is instead cut
+// into equal contiguous ranges (stream-K), and every piece is added into C
+// with red.global.add, so small grids (o_proj/down at 1280 tokens: 80 tiles)
+// keep every SM busy.  Partial sums then land in C in a hardware-chosen
+// order, so those outputs can differ run to run by float rounding.
 // Loads are plain TMA tile loads of this GPU's memory (no multicast).  Every
 // mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA records
 // kErrTimeout in the device error word, drains its own copies, frees its
@@ -26,7 +33,8 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;
+constexpr int kNumSMs = 148;
 constexpr long long kWaitCycles = 1ll << 32;  // ~2.2 s at 1.965 GHz
 constexpr int kErrTimeout = 5;
 
@@ -41,16 +49,16 @@ template <int BN> struct TileCfg {
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
-
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                : "memory");
 }
-
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -62,7 +70,6 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-
 // Bounded wait: false on timeout or when another role has aborted.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
@@ -77,7 +84,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
   return true;
 }
-
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
   asm volatile(
@@ -86,24 +92,21 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
-
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
 // 1024 bytes apart (SBO), sm100 descriptor version 1.
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
   uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;                 // LBO (unused for swizzled K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;       // SBO
-  d |= (uint64_t)1 << 46;                 // version
-  d |= (uint64_t)2 << 61;                 // SWIZZLE_128B
+  d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // SBO
+  d |= (uint64_t)1 << 46;            // version
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
   return d;
 }
-
 // Instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M=128.
 template <int BN> __device__ __forceinline__ uint32_t idesc() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
          ((uint32_t)(BM >> 4) << 24);
 }
-
 __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id,
                                      uint32_t accumulate) {
   asm volatile(
@@ -113,13 +116,11 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, ui
       "l"(a), "l"(b), "r"(id), "r"(accumulate)
       : "memory");
 }
-
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    bar)
                : "memory");
 }
-
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -136,16 +137,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
 
 // Epilogue for one thread's 32 consecutive columns [n, n+32) of row m.
+// kEpiResidual with `reduce`: C += acc by vector reductions (stream-K pieces
+// and whole tiles alike, C already holding the residual).
 template <int EPI, typename TC>
 __device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const float* R, int m,
-                                            int n, int N, int64_t ldc) {
+                                            int n, int N, int64_t ldc, bool reduce) {
   if constexpr (EPI == kEpiSwiGLU) {
     // columns [16g, 16g+8) gate, [16g+8, 16g+16) up -> outputs 8g..8g+7
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n / 2;
@@ -168,6 +175,17 @@ __device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const f
     }
   } else if constexpr (EPI == kEpiResidual) {
     float* out = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+    if (reduce) {
+      if (n + 32 <= N) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) red_add4(out + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (n + i < N) atomicAdd(out + i, v[i]);
+      }
+      return;
+    }
     const float* res = R + (int64_t)m * ldc + n;
     if (n + 32 <= N) {
 #pragma unroll
@@ -209,11 +227,50 @@ __device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const f
   }
 }
 
+// The sequence of (tile, k-begin, k-end) pieces one CTA works on.  Every role
+// of the CTA walks the same sequence.
+struct Schedule {
+  int tiles, kiters, grid, cta;
+  bool stream_k;
+  int64_t it, it_end;  // stream-K: [it, it_end) over tiles * kiters
+  int next_tile;       // round-robin
+
+  __device__ void init(int tiles_, int kiters_, bool sk) {
+    tiles = tiles_;
+    kiters = kiters_;
+    grid = gridDim.x;
+    cta = blockIdx.x;
+    stream_k = sk;
+    const int64_t total = (int64_t)tiles * kiters;
+    it = total * cta / grid;
+    it_end = total * (cta + 1) / grid;
+    next_tile = cta;
+  }
+  __device__ bool next(int& tile, int& k0, int& k1) {
+    if (stream_k) {
+      if (it >= it_end) return false;
+      tile = (int)(it / kiters);
+      k0 = (int)(it - (int64_t)tile * kiters);
+      const int64_t e = min(it_end, (int64_t)(tile + 1) * kiters);
+      k1 = k0 + (int)(e - it);
+      it = e;
+      return true;
+    }
+    if (next_tile >= tiles) return false;
+    tile = next_tile;
+    k0 = 0;
+    k1 = kiters;
+    next_tile += grid;
+    return true;
+  }
+};
+
 template <int BN, int EPI, typename TC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
-                   const float* __restrict__ R, int M, int N, int K, int64_t ldc, int* err) {
+                   const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
+                   int* err) {
   using Cfg = TileCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -222,20 +279,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* smem = smem_raw + pad;
   const uint32_t sbase = raw + pad;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
-  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S, done = full0 + 16 * S;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 1);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S;
+  const uint32_t tfull0 = full0 + 16 * S, tempty0 = tfull0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-  const int num_k = (K + BK - 1) / BK;
+  const int mt = (M + BM - 1) / BM;
+  const int tiles = mt * (N / BN);
+  const int kiters = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
-    mbar_init(done, 1);
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 4);  // one arrive per epilogue warp
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -243,71 +305,104 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(tmem_slot)),
-                 "r"(BN));
+                 "r"(2 * BN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  Schedule sched;
+  sched.init(tiles, kiters, stream_k != 0);
+  int tile, k0, k1;
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
-    int issued = 0;
-    for (int kt = 0; kt < num_k; ++kt) {
-      const int s = kt % S;
-      if (kt >= S && !mbar_wait(empty0 + 8 * s, ((kt / S) - 1) & 1, abort_flag, err)) break;
-      const uint32_t a_dst = sbase + s * Cfg::kStageBytes;
-      const uint32_t b_dst = a_dst + Cfg::kABytes;
-      mbar_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
-      tma_load_2d(a_dst, &tmap_a, full0 + 8 * s, kt * BK, m0);
-      tma_load_2d(b_dst, &tmap_b, full0 + 8 * s, kt * BK, n0);
-      ++issued;
-    }
-    if (*abort_flag) {
-      // drain the loads this thread may still have in flight before exiting
-      const long long t0 = clock64();
-      for (int kt = issued > S ? issued - S : 0; kt < issued; ++kt)
-        while (!mbar_try_wait(full0 + 8 * (kt % S), (kt / S) & 1) && clock64() - t0 < kWaitCycles) {
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      uint32_t q = 0;
+      bool alive = true;
+      while (alive && sched.next(tile, k0, k1)) {
+        const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+        for (int k = k0; k < k1; ++k, ++q) {
+          const uint32_t s = q % S;
+          if (q >= (uint32_t)S &&
+              !mbar_wait(empty0 + 8 * s, ((q / S) - 1) & 1, abort_flag, err)) {
+            alive = false;
+            break;
+          }
+          const uint32_t a_dst = sbase + s * Cfg::kStageBytes;
+          mbar_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
+          tma_load_2d(a_dst, &tmap_a, full0 + 8 * s, k * BK, m0);
+          tma_load_2d(a_dst + Cfg::kABytes, &tmap_b, full0 + 8 * s, k * BK, n0);
         }
+      }
+      if (*abort_flag) {  // drain this thread's loads before leaving
+        const long long t0 = clock64();
+        for (uint32_t j = q > (uint32_t)S ? q - S : 0; j < q; ++j)
+          while (!mbar_try_wait(full0 + 8 * (j % S), (j / S) & 1) && clock64() - t0 < kWaitCycles) {
+          }
+      }
     }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    const uint32_t id = idesc<BN>();
-    for (int kt = 0; kt < num_k; ++kt) {
-      const int s = kt % S;
-      if (!mbar_wait(full0 + 8 * s, (kt / S) & 1, abort_flag, err)) break;
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t a_addr = sbase + s * Cfg::kStageBytes;
-      const uint32_t b_addr = a_addr + Cfg::kABytes;
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      const uint32_t id = idesc<BN>();
+      uint32_t q = 0, seg = 0;
+      bool alive = true;
+      while (alive && sched.next(tile, k0, k1)) {
+        const uint32_t a = seg & 1, u = seg >> 1;
+        if (u >= 1 && !mbar_wait(tempty0 + 8 * a, (u - 1) & 1, abort_flag, err)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + a * BN;
+        for (int k = k0; k < k1; ++k, ++q) {
+          const uint32_t s = q % S;
+          if (!mbar_wait(full0 + 8 * s, (q / S) & 1, abort_flag, err)) {
+            alive = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = sbase + s * Cfg::kStageBytes;
+          const uint32_t b_addr = a_addr + Cfg::kABytes;
 #pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk)
-        umma(tmem, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), id, (kt | kk) != 0);
-      umma_commit(empty0 + 8 * s);
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma(d, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), id, (k > k0) || (kk > 0));
+          umma_commit(empty0 + 8 * s);
+        }
+        if (!alive) break;
+        umma_commit(tfull0 + 8 * a);
+        ++seg;
+      }
     }
-    umma_commit(done);
-  }
-  __syncwarp();
-
-  // ---- epilogue: every warp drains its 32 TMEM lanes ----
-  const bool ok = mbar_wait(done, 0, abort_flag, err) && !*abort_flag;
-  __syncwarp();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  if (ok) {
-    const int m = m0 + warp * 32 + lane;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  } else {
+    // ---- epilogue warps 2..5 ----
+    const int row_group = warp & 3;  // TMEM lanes 32*row_group .. +31
+    const bool reduce = EPI == kEpiResidual && stream_k;
+    uint32_t seg = 0;
+    while (sched.next(tile, k0, k1)) {
+      const uint32_t a = seg & 1, u = seg >> 1;
+      if (!mbar_wait(tfull0 + 8 * a, u & 1, abort_flag, err)) break;
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+      const int m = m0 + row_group * 32 + lane;
+      const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld32(lane_base + c, v);
-      const int n = n0 + c;
-      if (m < M && n < N) store_chunk<EPI, TC>(v, C, R, m, n, N, ldc);
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(base + c, v);
+        if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty0 + 8 * a);
+      ++seg;
     }
   }
+  __syncwarp();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
   }
 }
 
@@ -381,7 +476,7 @@ int tensor_map(const void* ptr, int rows, int cols, int box_rows, CUtensorMap* o
 
 template <int BN, int EPI, typename TC>
 int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-              int64_t ldc, cudaStream_t s) {
+              int64_t ldc, bool stream_k, cudaStream_t s) {
   CUtensorMap ta, tb;
   MS_TRY(tensor_map(A, M, K, BM, &ta));
   MS_TRY(tensor_map(B, N, K, BN, &tb));
@@ -394,10 +489,30 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "gemm_tc: smem attribute: %s", cudaGetErrorString(e));
     attr_set = true;
   }
-  dim3 grid(ceil_div(N, BN), ceil_div(M, BM));
+  const int tiles = ((M + BM - 1) / BM) * (N / BN);
+  const int kiters = (K + BK - 1) / BK;
+  int grid = stream_k ? (int)std::min<int64_t>((int64_t)tiles * kiters, kNumSMs)
+                      : std::min(tiles, kNumSMs);
+  if (grid < 1) grid = 1;
   kern<<<grid, kThreads, Cfg::kSmem, s>>>(ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-                                          device_error_word());
+                                          stream_k ? 1 : 0, device_error_word());
   return check_launch("gemm_tc_kernel");
+}
+
+// Tile width: 256 columns when N allows it and there are enough tiles to go
+// around, else 128.
+bool use_bn256(int M, int N, bool stream_k) {
+  if (N % 256 != 0) return false;
+  if (stream_k) return true;
+  const int mt = (M + BM - 1) / BM;
+  return mt * (N / 256) >= kNumSMs / 2;
+}
+
+template <int EPI, typename TC>
+int launch_any(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
+               int64_t ldc, bool stream_k, cudaStream_t s) {
+  if (use_bn256(M, N, stream_k)) return launch_tc<256, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s);
+  return launch_tc<128, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s);
 }
 
 }  // namespace
@@ -414,10 +529,14 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
        reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
-  if (epi == kEpiSwiGLU) return launch_tc<128, kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, s);
-  if (epi == kEpiResidual) return launch_tc<128, kEpiResidual, float>(A, B, C, R, M, N, K, ldc, s);
-  if (c_dtype == MS_DTYPE_F32) return launch_tc<128, kEpiStore, float>(A, B, C, R, M, N, K, ldc, s);
-  return launch_tc<128, kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, s);
+  if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+  if (epi == kEpiResidual) {
+    // In place (C += A B^T): stream-K with reductions into C.
+    const bool in_place = static_cast<const void*>(R) == C;
+    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, in_place, s);
+  }
+  if (c_dtype == MS_DTYPE_F32) return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
+  return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
 }
 
 }  // namespace ms

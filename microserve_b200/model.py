@@ -106,12 +106,6 @@ def split_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return v[:, 0].reshape(-1, d), v[:, 1].reshape(-1, d)
 
 
-# Workspace bytes past ms_forward's own carve; the attention kernel uses them
-# for split-KV partials when a batch has too few (sequence, kv head) tiles to
-# fill the GPU (otherwise it runs one KV range per tile and needs none).
-ATTN_SCRATCH_BYTES = 32 << 20
-
-
 class Transformer:
     """Decoder on one CUDA device; ``forward_paged`` is the hot path."""
 
@@ -245,10 +239,12 @@ class Transformer:
         return sum(t.numel() * t.element_size() for t in ts)
 
     # -- forward ---------------------------------------------------------------
-    def workspace(self, n_tokens: int, n_rows: int) -> torch.Tensor:
+    def workspace(self, n_tokens: int, n_rows: int, attn_scratch: int = 0) -> torch.Tensor:
+        """Grow-only device workspace: ms_forward's carve plus ``attn_scratch``
+        bytes for the attention's split-KV partials."""
         need = int(_lib.load().ms_forward_workspace_size(ctypes.byref(self._c_model), n_tokens,
                                                            n_rows))
-        need += ATTN_SCRATCH_BYTES
+        need += attn_scratch
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=self.device)
         return self._ws
@@ -271,8 +267,11 @@ class Transformer:
         if out is None:
             out = torch.empty((n_rows, self.cfg.vocab_size), dtype=torch.float32, device=self.device)
             out_row_stride = 0
-        ws = self.workspace(batch.n_tokens, n_rows)
         cb = batch.c_struct()
+        cc = cache.c_struct()
+        scratch = int(_lib.load().ms_attention_scratch_size(ctypes.byref(cc), self.cfg.n_heads,
+                                                            ctypes.byref(cb)))
+        ws = self.workspace(batch.n_tokens, n_rows, scratch)
         _lib.call(
             "ms_forward", ctypes.byref(self._c_model), ctypes.byref(cache.c_struct()),
             ctypes.byref(cb), _lib.ptr(logit_rows), n_rows, out.data_ptr(), out_row_stride,

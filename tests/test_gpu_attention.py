@@ -1,6 +1,7 @@
 """ms_paged_attention against a float32 torch reference of the same bf16 K/V.
 
-bf16 caches with d_head 64/128 take the tensor-core kernel; float32 and other
+bf16 caches with d_head 64/128 take the tensor-core kernels (TMA-fed for
+power-of-two block sizes 8..64, cp.async-fed otherwise); float32 and other
 head sizes the CUDA-core kernel.  The reference gathers each sequence's keys
 through its block table and applies the reference's causal rule (key j is
 visible to a query at absolute position p iff j <= p)."""
@@ -69,7 +70,7 @@ def _case(dtype: str, hq: int, hkv: int, dh: int, bs: int, ctx: list[int], qlen:
 
 
 @pytest.mark.parametrize("hq,hkv,dh", [(32, 4, 64), (32, 8, 128), (8, 8, 64), (4, 1, 128)])
-@pytest.mark.parametrize("bs", [16, 8, 32])
+@pytest.mark.parametrize("bs", [16, 8, 32, 4])
 def test_tensor_core_attention_decode_and_verify(hq, hkv, dh, bs) -> None:
     ctx = [17, 600, 1290, 64, 5, 333]
     qlen = [1, 5, 5, 6, 5, 2]

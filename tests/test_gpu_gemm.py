@@ -56,6 +56,9 @@ def test_residual_epilogue(M: int, N: int, K: int) -> None:
     B = (torch.randn(N, K, device=DEV, generator=g) * 0.05).bfloat16()
     X = torch.randn(M, N, device=DEV, generator=g)
     want = X + _ref(A, B)
+    Y = torch.full_like(X, float("nan"))
+    _gemm(A, B, Y, X, M, N, K, 0, _lib.DTYPE_BF16, _lib.DTYPE_F32, 1)  # y = x + A B^T
+    torch.testing.assert_close(Y, want, rtol=1e-3, atol=1e-3 * want.abs().max().item())
     _gemm(A, B, X, X, M, N, K, 0, _lib.DTYPE_BF16, _lib.DTYPE_F32, 1)  # in place: x += A B^T
     torch.testing.assert_close(X, want, rtol=1e-3, atol=1e-3 * want.abs().max().item())
 
