@@ -32,6 +32,53 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
   for (int i = lane; i < dim; i += 32) yr[i] = from_f<TY>(xr[i] * r * w[i]);
 }
 
+// Vectorised RMSNorm for dim % 4 == 0 and dim <= 4 * 128 * kVec: one
+// 128-thread CTA per row, the row held in registers (one read of x).
+constexpr int kNormThreads = 128;
+constexpr int kVec = 8;  // float4 per thread -> dim up to 4096
+template <typename TY>
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_vec_kernel(const float* __restrict__ x, const float* __restrict__ w, TY* __restrict__ y,
+                       const int32_t* __restrict__ row_idx, int dim, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int row = blockIdx.x;
+  const int src = row_idx ? row_idx[row] : row;
+  const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)src * dim);
+  const int n4 = dim >> 2;
+  float4 v[kVec];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kVec; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    v[k] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss = fmaf(v[k].x, v[k].x, fmaf(v[k].y, v[k].y, fmaf(v[k].z, v[k].z, fmaf(v[k].w, v[k].w, ss))));
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  ss = red[0] + red[1] + red[2] + red[3];
+  const float r = 1.f / sqrtf(ss / (float)dim + eps);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  TY* yr = y + (int64_t)row * dim;
+#pragma unroll
+  for (int k = 0; k < kVec; ++k) {
+    const int i = threadIdx.x + k * kNormThreads;
+    if (i >= n4) break;
+    const float4 g = wr[i];
+    const float a = v[k].x * r * g.x, b = v[k].y * r * g.y, c = v[k].z * r * g.z,
+                d = v[k].w * r * g.w;
+    if constexpr (sizeof(TY) == 4) {
+      reinterpret_cast<float4*>(yr)[i] = make_float4(a, b, c, d);
+    } else {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+      uint2 pk;
+      pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+      pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(yr)[i] = pk;
+    }
+  }
+}
+
 // x[t] = embed[ids[t]] (float32 residual stream), y[t] = rmsnorm(x[t]) * w.
 template <typename TW>
 __global__ void embed_rmsnorm_kernel(const TW* __restrict__ embed, const int32_t* __restrict__ ids,
@@ -176,6 +223,19 @@ int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int
             float eps, int dtype, cudaStream_t s) {
   if (n_rows == 0) return MS_OK;
   ProfScope prof(kClsNorm, s);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                         reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (dim % 4 == 0 && dim <= 4 * kNormThreads * kVec && aligned) {
+    if (dtype == MS_DTYPE_F32)
+      rmsnorm_vec_kernel<float><<<n_rows, kNormThreads, 0, s>>>(x, w, static_cast<float*>(y),
+                                                                row_idx, dim, eps);
+    else if (dtype == MS_DTYPE_BF16)
+      rmsnorm_vec_kernel<__nv_bfloat16><<<n_rows, kNormThreads, 0, s>>>(
+          x, w, static_cast<__nv_bfloat16*>(y), row_idx, dim, eps);
+    else
+      return fail(MS_ERR_UNSUPPORTED, "rmsnorm: dtype %d", dtype);
+    return check_launch("rmsnorm_vec_kernel");
+  }
   const int blocks = ceil_div(n_rows, 8);
   if (dtype == MS_DTYPE_F32)
     rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(x, w, static_cast<float*>(y), row_idx, n_rows, dim,

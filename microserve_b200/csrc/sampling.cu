@@ -49,7 +49,7 @@ struct Dist {
   int mode;
   bool divide;  // apply temperature when reading (row not pre-divided)
   float temp;
-  float m, thresh, z;
+  float m, thresh, z, inv_z;
   int argmax;
 
   __device__ __forceinline__ float x(int i) const {
@@ -61,13 +61,13 @@ struct Dist {
     if (mode == 1) return row[i];
     if (mode == 2) return i == argmax ? 1.f : 0.f;
     const float xv = x(i);
-    return xv >= thresh ? expf(xv - m) : 0.f;
+    return xv >= thresh ? __expf(xv - m) : 0.f;
   }
   __device__ __forceinline__ float prob(int i) const {
     if (mode == 1) return row[i];
     if (mode == 2) return i == argmax ? 1.f : 0.f;
     const float xv = x(i);
-    return xv >= thresh ? __fdiv_rn(expf(xv - m), z) : 0.f;
+    return xv >= thresh ? __expf(xv - m) * inv_z : 0.f;
   }
 };
 
@@ -119,6 +119,7 @@ __device__ void block_argmax(float v, int idx, RowSmem& sm, float& out_v, int& o
 __device__ void row_argmax(const Dist& d, int V, RowSmem& sm, float& m, int& am) {
   float best = -INFINITY;
   int bi = 0x7fffffff;
+#pragma unroll 4
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float v = d.x(i);
     if (v > best || (v == best && i < bi)) {
@@ -263,7 +264,7 @@ __device__ float radix_top_p(const Dist& d, int V, float top_p, RowSmem& sm) {
       if (xv < d.thresh) continue;
       const uint32_t key = fkey(xv);
       if ((key & mask) == prefix) {
-        const float p = __fdiv_rn(expf(xv - d.m), d.z);
+        const float p = __expf(xv - d.m) * d.inv_z;
         atomicAdd(reinterpret_cast<float*>(&h[(key >> shift) & 255u]), p);
       }
     }
@@ -280,37 +281,269 @@ __device__ float radix_top_p(const Dist& d, int V, float top_p, RowSmem& sm) {
   return kfloat(prefix);
 }
 
-// Fills d.m / d.thresh / d.z / d.argmax for a logits row (mode 0).
-__device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm) {
-  float m;
-  int am;
-  row_argmax(d, V, sm, m, am);
-  d.m = m;
-  d.argmax = am;
-  d.thresh = -INFINITY;
-  if (top_k > 0 && top_k < V) d.thresh = radix_kth_largest(d, V, top_k, sm);
-  float zl = 0.f;
+// ---- linear-bin selection -------------------------------------------------
+// Values are binned by their distance below the row maximum, bin =
+// floor((max - x) * 64) clamped to kLinBins-1: one pass with little atomic
+// contention (logits spread over many bins, unlike their exponent bits), a
+// block scan to find the bin holding the k-th largest value / the top-p
+// crossing value, then an exact choice among that bin's few candidates.  A
+// bin with more than kCand candidates (flat or tied rows) falls back to the
+// radix routines above.
+constexpr int kLinBins = 2048;
+constexpr int kCand = 512;
+constexpr float kBinsPerUnit = 64.f;
+
+__device__ __forceinline__ int lin_bin(float m, float x) {
+  const float t = (m - x) * kBinsPerUnit;
+  return t < (float)(kLinBins - 1) ? (int)t : kLinBins - 1;
+}
+
+// Block-wide search over the kLinBins histogram for the first bin whose
+// inclusive prefix reaches the target.  Returns the bin (-1 if none) and the
+// amount in the bins before it.
+template <bool kFloat>
+__device__ int lin_find(const uint32_t* H, float target_f, uint32_t target_u, RowSmem& sm,
+                        float& before_f, uint32_t& before_u) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = kLinBins / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  float lf = 0.f;
+  uint32_t lu = 0;
+  for (int j = 0; j < per; ++j) {
+    if (kFloat) lf += __uint_as_float(H[b0 + j]);
+    else lu += H[b0 + j];
+  }
+  float incf = lf;
+  uint32_t incu = lu;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float tf = __shfl_up_sync(0xffffffffu, incf, o);
+    const uint32_t tu = __shfl_up_sync(0xffffffffu, incu, o);
+    if (lane >= o) {
+      incf += tf;
+      incu += tu;
+    }
+  }
+  __syncthreads();
+  if (lane == 31) {
+    sm.red[warp] = incf;
+    sm.red_i[warp] = (int)incu;
+  }
+  if (threadIdx.x == 0) sm.red_i[48] = -1;
+  __syncthreads();
+  float wf = 0.f;
+  uint32_t wu = 0;
+  for (int w = 0; w < warp; ++w) {
+    wf += sm.red[w];
+    wu += (uint32_t)sm.red_i[w];
+  }
+  (void)nw;
+  const float exf = wf + incf - lf;  // before this thread's bins
+  const uint32_t exu = wu + incu - lu;
+  const bool hit = kFloat ? (exf < target_f && exf + lf >= target_f)
+                          : (exu < target_u && exu + lu >= target_u);
+  if (hit) {
+    float af = exf;
+    uint32_t au = exu;
+    for (int j = 0; j < per; ++j) {
+      const uint32_t h = H[b0 + j];
+      const bool hb = kFloat ? (af + __uint_as_float(h) >= target_f) : (au + h >= target_u);
+      if (hb) {
+        sm.red_i[48] = b0 + j;
+        sm.red[48] = af;
+        sm.red_i[49] = (int)au;
+        break;
+      }
+      if (kFloat) af += __uint_as_float(h);
+      else au += h;
+    }
+  }
+  __syncthreads();
+  const int bin = sm.red_i[48];
+  before_f = sm.red[48];
+  before_u = (uint32_t)sm.red_i[49];
+  __syncthreads();
+  return bin;
+}
+
+// Gathers (value, index) of the kept elements in `bin` into the candidate
+// lists; returns their number (may exceed kCand: caller falls back).
+__device__ int lin_gather(const Dist& d, int V, int bin, uint32_t* cv, uint32_t* ci, RowSmem& sm) {
+  if (threadIdx.x == 0) sm.red_i[50] = 0;
+  __syncthreads();
+#pragma unroll 4
   for (int i = threadIdx.x; i < V; i += blockDim.x) {
     const float xv = d.x(i);
-    if (xv >= d.thresh) zl += expf(xv - m);
+    if (xv >= d.thresh && lin_bin(d.m, xv) == bin) {
+      const int slot = atomicAdd(&sm.red_i[50], 1);
+      if (slot < kCand) {
+        cv[slot] = __float_as_uint(xv);
+        ci[slot] = (uint32_t)i;
+      }
+    }
+  }
+  __syncthreads();
+  const int n = sm.red_i[50];
+  __syncthreads();
+  return n;
+}
+
+// k-th largest value (ties keep more).  ok=false: use the radix routine.
+__device__ float linear_kth(const Dist& d, int V, int k, RowSmem& sm, bool& ok) {
+  uint32_t* H = sm.hist;
+  uint32_t* cv = H + kLinBins;
+  uint32_t* ci = cv + kCand;
+  for (int i = threadIdx.x; i < kLinBins; i += blockDim.x) H[i] = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&H[lin_bin(d.m, d.x(i))], 1u);
+  __syncthreads();
+  float bf;
+  uint32_t bu;
+  const int bin = lin_find<false>(H, 0.f, (uint32_t)k, sm, bf, bu);
+  ok = false;
+  if (bin < 0) return -INFINITY;
+  const int n = lin_gather(d, V, bin, cv, ci, sm);  // d.thresh is -inf here
+  if (n > kCand || n == 0) return -INFINITY;
+  const int kk = k - (int)bu;  // rank wanted inside the bin (1-based)
+  if (threadIdx.x == 0) sm.red_i[51] = -1;
+  __syncthreads();
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float vt = __uint_as_float(cv[t]);
+    int greater = 0, equal = 0;
+    for (int j = 0; j < n; ++j) {
+      const float vj = __uint_as_float(cv[j]);
+      greater += vj > vt;
+      equal += vj == vt;
+    }
+    if (greater < kk && kk <= greater + equal) sm.red_i[51] = (int)cv[t];
+  }
+  __syncthreads();
+  const int res = sm.red_i[51];
+  __syncthreads();
+  if (res == -1) return -INFINITY;
+  ok = true;
+  return __uint_as_float((uint32_t)res);
+}
+
+// Top-p on the histogram (already built by row_stats) of unnormalised
+// masses e = exp(x - m) of the kept elements, whose total is d.z: returns the
+// crossing value -- the first value in descending order whose inclusive mass
+// reaches top_p * z -- and the mass kept at and above it.  ok=false: use the
+// radix routine.
+__device__ float linear_top_p(const Dist& d, int V, float top_p, RowSmem& sm, bool& ok,
+                              float& z_keep) {
+  uint32_t* H = sm.hist;
+  uint32_t* cv = H + kLinBins;
+  uint32_t* ci = cv + kCand;
+  float* cm = reinterpret_cast<float*>(ci + kCand);
+  const float target = top_p * d.z;
+  float before;
+  uint32_t bu;
+  const int bin = lin_find<true>(H, target, 0u, sm, before, bu);
+  ok = false;
+  if (bin < 0) return -INFINITY;
+  const int n = lin_gather(d, V, bin, cv, ci, sm);
+  if (n > kCand || n == 0) return -INFINITY;
+  for (int t = threadIdx.x; t < n; t += blockDim.x) cm[t] = __expf(__uint_as_float(cv[t]) - d.m);
+  if (threadIdx.x == 0) sm.red_i[51] = -1;
+  __syncthreads();
+  for (int t = threadIdx.x; t < n; t += blockDim.x) {
+    const float vt = __uint_as_float(cv[t]);
+    const uint32_t it = ci[t];
+    float above = before;
+    for (int j = 0; j < n; ++j) {
+      const float vj = __uint_as_float(cv[j]);
+      if (vj > vt || (vj == vt && ci[j] < it)) above += cm[j];
+    }
+    if (above < target && above + cm[t] >= target) sm.red_i[51] = (int)cv[t];
+  }
+  __syncthreads();
+  const int res = sm.red_i[51];
+  __syncthreads();
+  if (res == -1) return -INFINITY;  // rounding found no crossing: radix fallback
+  const float cut = __uint_as_float((uint32_t)res);
+  float part = 0.f;
+  for (int t = threadIdx.x; t < n; t += blockDim.x)
+    if (__uint_as_float(cv[t]) >= cut) part += cm[t];
+  z_keep = before + block_sum_b(part, sm);
+  ok = true;
+  return cut;
+}
+
+__device__ __forceinline__ bool linear_ok(RowSmem& sm, int V) {
+  // histogram + candidate values, indices and masses fit the histogram area
+  return (int)(blockDim.x >> 5) * kHistBins >= kLinBins + 3 * kCand && V >= 4096 &&
+         kLinBins % blockDim.x == 0;
+}
+
+// Fills d.m / d.argmax (unless have_max), d.thresh, d.z, d.inv_z for a
+// logits row (mode 0).  The kept-mass total and the top-p histogram come out
+// of one pass; the top-p kept mass is derived from the bins, not re-summed.
+__device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, bool have_max) {
+  if (!have_max) {
+    float m0;
+    int am;
+    row_argmax(d, V, sm, m0, am);
+    d.m = m0;
+    d.argmax = am;
+  }
+  const float m = d.m;
+  d.thresh = -INFINITY;
+  const bool lin = linear_ok(sm, V);
+  if (top_k > 0 && top_k < V) {
+    bool ok = false;
+    float kth = -INFINITY;
+    if (lin) kth = linear_kth(d, V, top_k, sm, ok);
+    d.thresh = ok ? kth : radix_kth_largest(d, V, top_k, sm);
+  }
+  const bool want_p = top_p < 1.f;
+  const bool hist = want_p && lin;
+  float* Hf = reinterpret_cast<float*>(sm.hist);
+  if (hist) {
+    for (int i = threadIdx.x; i < kLinBins; i += blockDim.x) Hf[i] = 0.f;
+    __syncthreads();
+  }
+  float zl = 0.f;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float xv = d.x(i);
+    if (xv >= d.thresh) {
+      const float e = __expf(xv - m);
+      zl += e;
+      if (hist) atomicAdd(&Hf[lin_bin(m, xv)], e);
+    }
   }
   d.z = block_sum_b(zl, sm);
-  if (top_p < 1.f) {
-    float cut;
-    if (__fdiv_rn(1.f, d.z) >= top_p) {
-      cut = m;  // the maximum alone already covers top_p
-    } else {
-      cut = radix_top_p(d, V, top_p, sm);
-    }
-    if (cut > d.thresh) {
-      d.thresh = cut;
-      zl = 0.f;
-      for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float xv = d.x(i);
-        if (xv >= d.thresh) zl += expf(xv - m);
+  d.inv_z = 1.f / d.z;
+  if (!want_p) return;
+  float cut = -INFINITY;
+  bool done = false;
+  if (1.f >= top_p * d.z) {
+    cut = m;  // the maximum alone already covers top_p
+  } else if (hist) {
+    float z_keep = d.z;
+    bool ok = false;
+    const float c = linear_top_p(d, V, top_p, sm, ok, z_keep);
+    if (ok) {
+      if (c > d.thresh) {
+        d.thresh = c;
+        d.z = z_keep;
+        d.inv_z = 1.f / d.z;
       }
-      d.z = block_sum_b(zl, sm);
+      done = true;
     }
+  }
+  if (!done && cut == -INFINITY) cut = radix_top_p(d, V, top_p, sm);
+  if (!done && cut > d.thresh) {
+    d.thresh = cut;
+    zl = 0.f;
+#pragma unroll 4
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float xv = d.x(i);
+      if (xv >= d.thresh) zl += __expf(xv - m);
+    }
+    d.z = block_sum_b(zl, sm);
+    d.inv_z = 1.f / d.z;
   }
 }
 
@@ -326,6 +559,7 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
   // phase 1: segment totals and the last positive index
   float part = 0.f;
   int last = -1;
+#pragma unroll 4
   for (int i = s0 + lane; i < s1; i += 32) {
     const float v = w(i);
     part += v;
@@ -418,27 +652,85 @@ size_t smem_bytes(int threads, int V, bool stage) {
 }
 
 // Loads a logits row into a Dist: staged (pre-divided by T) when it fits.
-__device__ void load_logits(Dist& d, const float* row, int V, float temp, RowSmem& sm) {
+// Loads a logits row into a Dist: staged in shared memory (pre-divided by T)
+// when it fits, computing the row max and first argmax on the way (returns
+// true); otherwise the Dist reads global memory (returns false).
+__device__ bool load_logits(Dist& d, const float* row, int V, float temp, RowSmem& sm) {
   d.mode = 0;
   d.temp = temp;
-  if (sm.stage != nullptr) {
-    __syncthreads();  // previous users of the stage are done
-    const bool div = temp != 1.f;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-      const float v = __ldg(row + i);
-      sm.stage[i] = div ? __fdiv_rn(v, temp) : v;
-    }
-    __syncthreads();
-    d.row = sm.stage;
-    d.divide = false;
-  } else {
+  if (sm.stage == nullptr) {
     d.row = row;
     d.divide = temp != 1.f;
+    return false;
   }
+  __syncthreads();  // previous users of the stage are done
+  const bool div = temp != 1.f;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  auto note = [&](float v, int i) {
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  };
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    // float4 loads, 8 in flight per thread
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    float4* s4 = reinterpret_cast<float4*>(sm.stage);
+    const int n4 = V >> 2;
+    for (int base = threadIdx.x; base < n4; base += 8 * blockDim.x) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * blockDim.x;
+        v[u] = i < n4 ? __ldg(r4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * blockDim.x;
+        if (i < n4) {
+          float4 w = v[u];
+          if (div) {
+            w.x = __fdiv_rn(w.x, temp);
+            w.y = __fdiv_rn(w.y, temp);
+            w.z = __fdiv_rn(w.z, temp);
+            w.w = __fdiv_rn(w.w, temp);
+          }
+          s4[i] = w;
+          note(w.x, 4 * i);
+          note(w.y, 4 * i + 1);
+          note(w.z, 4 * i + 2);
+          note(w.w, 4 * i + 3);
+        }
+      }
+    }
+    for (int i = (n4 << 2) + threadIdx.x; i < V; i += blockDim.x) {
+      const float v = __ldg(row + i);
+      const float x = div ? __fdiv_rn(v, temp) : v;
+      sm.stage[i] = x;
+      note(x, i);
+    }
+  } else {
+#pragma unroll 8
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = __ldg(row + i);
+      const float x = div ? __fdiv_rn(v, temp) : v;
+      sm.stage[i] = x;
+      note(x, i);
+    }
+  }
+  d.row = sm.stage;
+  d.divide = false;
+  float m;
+  int am;
+  block_argmax(best, bi, sm, m, am);  // its barriers also publish the stage
+  d.m = m;
+  d.argmax = am == 0x7fffffff ? 0 : am;
+  return true;
 }
 
 // ---- K8: one draw per row ----------------------------------------------------
-__global__ void sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
+__global__ void __launch_bounds__(512) sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
                                    const ms_sampling_params* __restrict__ params,
                                    const int32_t* __restrict__ pidx, uint32_t lane_id,
                                    int32_t* __restrict__ tokens, float* __restrict__ probs,
@@ -466,8 +758,8 @@ __global__ void sample_rows_kernel(const float* __restrict__ logits, int64_t str
     d.z = 1.f;
     token = am;
   } else {
-    load_logits(d, row, V, P.temperature, sm);
-    row_stats(d, V, P.top_k, P.top_p < 1.f ? P.top_p : 1.f, sm);
+    const bool have_max = load_logits(d, row, V, P.temperature, sm);
+    row_stats(d, V, P.top_k, P.top_p < 1.f ? P.top_p : 1.f, sm, have_max);
     const float u = philox_uniform(P.seed, P.step, lane_id);
     token = inverse_cdf([&](int i) { return d.weight(i); }, V, u, sm);
   }
@@ -501,7 +793,7 @@ struct AcceptArgs {
   int* err;
 };
 
-__global__ void spec_accept_kernel(AcceptArgs a, int stage) {
+__global__ void __launch_bounds__(512) spec_accept_kernel(AcceptArgs a, int stage) {
   RowSmem sm;
   setup_smem(sm, a.V, stage != 0);
   const int b = blockIdx.x;
@@ -541,8 +833,8 @@ __global__ void spec_accept_kernel(AcceptArgs a, int stage) {
       p.argmax = am;
       return;
     }
-    load_logits(p, row, V, P.temperature, sm);
-    row_stats(p, V, P.top_k, top_p, sm);
+    const bool have_max = load_logits(p, row, V, P.temperature, sm);
+    row_stats(p, V, P.top_k, top_p, sm, have_max);
   };
   // Builds the draft distribution for position i (never staged).
   auto draft_dist = [&](int i, Dist& q) {
@@ -561,6 +853,7 @@ __global__ void spec_accept_kernel(AcceptArgs a, int stage) {
       q.m = s.max;
       q.thresh = s.thresh;
       q.z = s.z;
+      q.inv_z = 1.f / s.z;
       q.argmax = s.argmax;
       q.mode = greedy ? 2 : 0;
       return;
@@ -574,7 +867,7 @@ __global__ void spec_accept_kernel(AcceptArgs a, int stage) {
       q.argmax = am;
       return;
     }
-    row_stats(q, V, P.top_k, top_p, sm);
+    row_stats(q, V, P.top_k, top_p, sm, false);
   };
 
   for (int i = 0; i < G; ++i) {
@@ -597,6 +890,7 @@ __global__ void spec_accept_kernel(AcceptArgs a, int stage) {
     }
     // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0.
     float part = 0.f;
+#pragma unroll 4
     for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(p.prob(j) - q.prob(j), 0.f);
     const float total = block_sum_b(part, sm);
     const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
@@ -626,7 +920,7 @@ __global__ void spec_accept_kernel(AcceptArgs a, int stage) {
 int row_threads(int V) {
   int t = ((V / 16) + 31) & ~31;
   if (t < 128) t = 128;
-  if (t > 1024) t = 1024;
+  if (t > 512) t = 512;
   return t;
 }
 

@@ -114,14 +114,17 @@ def _accept_case(B: int, G: int, V: int, t: float, k, p, seed: int):
     return tl, dl, seeds, steps, qrows, props
 
 
-@pytest.mark.parametrize("setting", [(1.0, None, None), (1.0, 50, None), (1.0, None, 0.9),
-                                     (0.8, 20, 0.95), (0.0, None, None)])
-@pytest.mark.parametrize("draft_mode", ["logits", "stats", "probs"])
-def test_spec_accept_matches_oracle(setting, draft_mode: str) -> None:
+@pytest.mark.parametrize("setting,draft_mode,V", [
+    *[(s, m, 4000) for s in [(1.0, None, None), (1.0, 50, None), (1.0, None, 0.9),
+                             (0.8, 20, 0.95), (0.0, None, None)]
+      for m in ("logits", "stats", "probs")],
+    *[(s, "stats", 32000) for s in [(1.0, 50, None), (1.0, None, 0.9), (0.8, 50, 0.9)]],
+])
+def test_spec_accept_matches_oracle(setting, draft_mode: str, V: int) -> None:
     """config-1-shaped (rows x gamma=5 x vocab) at a reduced row count."""
     L = _lib()
     t, k, p = setting
-    B, G, V = 48, 5, 4000
+    B, G = 48, 5
     tl, dl, seeds, steps, qrows, props = _accept_case(B, G, V, t, k, p, 99)
     params = _params([(t, k, p)] * B, seeds.tolist(), steps.tolist())
     d_tl = torch.from_numpy(tl.reshape(B * (G + 1), V)).to(DEV)
