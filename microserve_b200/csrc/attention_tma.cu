@@ -1,17 +1,25 @@
 // Paged attention for bf16 caches with TMA tile loads (sm_100a).
 //
-// Same work decomposition and arithmetic as attention_tc.cu (one CTA per
-// (64-row query tile, kv head, sequence, KV range); the GQA query heads of a
-// kv head share M), but the K/V traffic is moved by the tensor memory
-// accelerator instead of per-thread cp.async:
-//   warp 4 lane 0  producer: for each 64-key chunk, looks up the chunk's
-//                  blocks in the block table and issues one 2-D TMA load per
-//                  (block, kv head, 64-column half) of K and of V into a
-//                  STAGES-deep ring, 128-byte swizzled, completing on the
-//                  stage's "full" mbarrier;
-//   warps 0-3      consumers: wait "full", S = Q K^T and O += P V with
-//                  ldmatrix (swizzle-aware addresses) + mma.sync m16n8k16,
-//                  online softmax, then arrive on the stage's "empty" barrier.
+// One CTA per (64-row query tile, kv head, sequence, KV range); the GQA query
+// heads of a kv head share the tile (row r = token * group + head-in-group),
+// so every K/V byte of a range is read once per kv head.
+//   producer warp, lane 0: for each chunk of kCh keys, looks up the chunk's
+//                  blocks in the block table (staged in shared memory) and
+//                  issues one 2-D TMA load per (block, kv head, 64-column
+//                  half) of K and of V into a kStages-deep ring, 128-byte
+//                  swizzled, completing on the stage's "full" mbarrier;
+//   consumer warps: warp w owns m-tile (w % MTP) of the query rows and key
+//                  slice (w / MTP) of every chunk, KW keys wide.  The slice
+//                  width is picked at launch from the batch's largest row
+//                  count, so a decode tile (8 rows, one m-tile) spreads each
+//                  chunk over all consumer warps instead of leaving all but
+//                  one idle.  Per slice: S = Q K^T and O += P V with ldmatrix
+//                  (swizzle-aware addresses) + mma.sync m16n8k16 bf16, online
+//                  softmax in base 2; then arrive on the stage's "empty"
+//                  barrier.
+// When a chunk is split over several warps, their (max, sum, O) states are
+// merged through shared memory at the end, with the same rescaling the
+// cross-CTA split-KV combine uses.
 // The pools are viewed as 2-D tensors [num_blocks * n_kv_heads * block_size
 // rows][d_head columns]; a (block, kv head) tile is block_size consecutive
 // rows.  No multicast; only this GPU's memory is read.  Every mbarrier wait
@@ -29,21 +37,26 @@ namespace ms {
 namespace {
 
 constexpr int kRows = 64;
-constexpr int kChunk = 64;
-constexpr int kConsumers = 4;
-constexpr int kThreads = (kConsumers + 1) * 32;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr long long kWaitCycles = 1ll << 32;
 constexpr int kErrTimeout = 5;
-constexpr int kTblCap = 64;  // block-table entries staged per refill (multiple of 8)
+constexpr int kErrRows = 6;  // a row tile wider than the launch's slice layout covers
+constexpr int kTblCap = 64;  // block-table entries staged per refill (multiple of 16)
 
 template <int DH> struct TmaCfg {
-  static constexpr int kHalves = DH / 64;                  // 128-byte column halves
-  static constexpr int kStages = DH == 64 ? 4 : 3;
-  static constexpr int kTileBytes = kChunk * DH * 2;       // one operand, one chunk
-  static constexpr int kStageBytes = 2 * kTileBytes;       // K + V
+  static constexpr int kCh = DH == 64 ? 128 : 64;   // keys per stage
+  static constexpr int kWarps = DH == 64 ? 8 : 4;   // consumer warps
+  static constexpr int kThreads = (kWarps + 1) * 32;
+  static constexpr int kHalves = DH / 64;           // 128-byte column halves
+  static constexpr int kStages = DH == 64 ? 3 : 2;
+  static constexpr int kTileBytes = kCh * DH * 2;   // one operand, one chunk
+  static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
   static constexpr int kLdQ = DH + 8;
   static constexpr int kQBytes = kRows * kLdQ * 2;
+  static constexpr int kLdPart = DH + 8;            // merge buffer row stride (floats)
+  static constexpr int kPartBytes = kWarps * 16 * (kLdPart * 4 + 8);
+  static_assert(kPartBytes <= kStages * kStageBytes, "merge buffer must fit in the ring");
+  static_assert(kTblCap % (kCh / 8) == 0, "table refill must hold whole chunks");
   static constexpr int kSmem =
       1024 + kStages * kStageBytes + kQBytes + kRows * 4 + 128 + kTblCap * 4;
 };
@@ -74,6 +87,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
+  if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (*abort_flag) return false;
@@ -117,12 +131,29 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
 }
+__device__ __forceinline__ void consumer_sync(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+// Named barrier 1 over the consumer warps; true when `pred` holds in any of them.
+__device__ __forceinline__ bool consumer_any(int threads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(threads)
+      : "memory");
+  return r != 0;
+}
 
-// Address of the 16-byte chunk `c` (0 .. DH/8-1) of key row `k` (0..63) in a
-// swizzled operand tile: half c/8, row k of 128 bytes, chunk (c%8) ^ (k%8).
+// Address of the 16-byte chunk `c` (0 .. DH/8-1) of key row `k` (0..kCh-1) in
+// a swizzled operand tile: half c/8, row k of 128 bytes, chunk (c%8) ^ (k%8).
 template <int DH>
 __device__ __forceinline__ uint32_t tile_addr(uint32_t tile, int k, int c) {
-  return tile + (uint32_t)((c >> 3) * (kChunk * 128) + k * 128 + (((c & 7) ^ (k & 7)) << 4));
+  return tile +
+         (uint32_t)((c >> 3) * (TmaCfg<DH>::kCh * 128) + k * 128 + (((c & 7) ^ (k & 7)) << 4));
 }
 
 struct TmaArgs {
@@ -140,14 +171,19 @@ struct TmaArgs {
   int* err;
 };
 
-template <int DH>
-__global__ void __launch_bounds__(kThreads)
+template <int DH, int KW>
+__global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
     attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     TmaArgs a) {
   using Cfg = TmaCfg<DH>;
   constexpr int S = Cfg::kStages;
+  constexpr int CH = Cfg::kCh;
+  constexpr int NW = Cfg::kWarps;
   constexpr int NT = DH / 8;
   constexpr int LDQ = Cfg::kLdQ;
+  constexpr int KS = CH / KW;   // key slices per chunk
+  constexpr int MTP = NW / KS;  // m-tiles the consumer warps cover
+  static_assert(KW % 16 == 0 && CH % KW == 0 && NW % KS == 0 && MTP * 16 <= kRows, "slice layout");
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const uint32_t raw = s_addr(smem_raw);
   unsigned char* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -167,14 +203,18 @@ __global__ void __launch_bounds__(kThreads)
   const int r0 = rt * kRows;
   if (r0 >= nrows) return;
   const int nr = min(kRows, nrows - r0);
+  if (nr > MTP * 16) {
+    if (threadIdx.x == 0) atomicCAS(a.err, 0, kErrRows);
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  for (int r = threadIdx.x; r < kRows; r += kThreads)
+  for (int r = threadIdx.x; r < kRows; r += Cfg::kThreads)
     rowpos[r] = r < nr ? a.positions[t0 + (r0 + r) / group] : -1;
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, kConsumers);
+      mbar_init(empty0 + 8 * s, NW);
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -182,10 +222,10 @@ __global__ void __launch_bounds__(kThreads)
   }
   // Stage tiles start zeroed: key rows a chunk never loads must hold finite
   // values (their probabilities are 0, and 0 * NaN would poison O).
-  for (int i = threadIdx.x; i < S * Cfg::kStageBytes / 16; i += kThreads)
+  for (int i = threadIdx.x; i < S * Cfg::kStageBytes / 16; i += Cfg::kThreads)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   // Q tile (zero rows past nr).
-  for (int idx = threadIdx.x; idx < kRows * (DH / 8); idx += kThreads) {
+  for (int idx = threadIdx.x; idx < kRows * (DH / 8); idx += Cfg::kThreads) {
     const int r = idx / (DH / 8), c = (idx % (DH / 8)) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < nr) {
@@ -197,19 +237,24 @@ __global__ void __launch_bounds__(kThreads)
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeros before TMA writes
   __syncthreads();
 
-  int kmax = 0;
-  for (int r = 0; r < nr; ++r) kmax = max(kmax, rowpos[r] + 1);
+  int kmax = 0, minpos = INT_MAX;
+  for (int r = 0; r < nr; ++r) {
+    kmax = max(kmax, rowpos[r] + 1);
+    minpos = min(minpos, rowpos[r]);
+  }
   kmax = min(kmax, a.context_lens[b]);
   const int splits_here = max(1, (kmax + a.split_len - 1) / a.split_len);
   if (split >= splits_here) return;
   const int kbeg = split * a.split_len;
   const int kend = min(kmax, kbeg + a.split_len);
-  const int nchunks = (kend - kbeg + kChunk - 1) / kChunk;
+  const int nchunks = (kend - kbeg + CH - 1) / CH;
+  // Keys below jfree are visible to every row of the tile: no mask needed.
+  const int jfree = min(kend, minpos + 1);
 
-  if (warp == kConsumers) {
+  if (warp == NW) {
     // ---- producer: block-table slice staged in smem, one lane issues TMA ----
     const int32_t* table = a.tables + (int64_t)b * a.max_blocks;
-    const int bpc = kChunk >> a.log2_bs;  // blocks per chunk
+    const int bpc = CH >> a.log2_bs;  // blocks per chunk
     const int first_blk = kbeg >> a.log2_bs;
     const int n_blk = (kend - kbeg + a.bs - 1) >> a.log2_bs;
     int issued = 0;
@@ -234,8 +279,8 @@ __global__ void __launch_bounds__(kThreads)
             stop = true;
             break;
           }
-          const int j0 = kbeg + ch * kChunk;
-          const int nb = (min(kend, j0 + kChunk) - j0 + a.bs - 1) >> a.log2_bs;
+          const int j0 = kbeg + ch * CH;
+          const int nb = (min(kend, j0 + CH) - j0 + a.bs - 1) >> a.log2_bs;
           mbar_expect_tx(full0 + 8 * s, (uint32_t)(nb * a.bs * DH * 2 * 2));
           const uint32_t kdst = stage0 + s * Cfg::kStageBytes;
           const uint32_t vdst = kdst + Cfg::kTileBytes;
@@ -245,8 +290,8 @@ __global__ void __launch_bounds__(kThreads)
             const uint32_t off = (uint32_t)(i * a.bs * 128);
 #pragma unroll
             for (int h = 0; h < Cfg::kHalves; ++h) {
-              tma_load_2d(kdst + h * kChunk * 128 + off, &kmap, full0 + 8 * s, h * 64, y);
-              tma_load_2d(vdst + h * kChunk * 128 + off, &vmap, full0 + 8 * s, h * 64, y);
+              tma_load_2d(kdst + h * CH * 128 + off, &kmap, full0 + 8 * s, h * 64, y);
+              tma_load_2d(vdst + h * CH * 128 + off, &vmap, full0 + 8 * s, h * 64, y);
             }
           }
           ++issued;
@@ -264,7 +309,8 @@ __global__ void __launch_bounds__(kThreads)
   }
 
   // ---- consumers ----
-  const int wr = warp * 16;
+  const int mi = warp % MTP, si = warp / MTP;
+  const int wr = mi * 16, kof = si * KW;
   const int ra = wr + (lane >> 2), rb = ra + 8;
   const int pos_a = rowpos[ra], pos_b = rowpos[rb];
   const bool live = wr < nr;
@@ -272,44 +318,75 @@ __global__ void __launch_bounds__(kThreads)
   float o[NT][4];
 #pragma unroll
   for (int i = 0; i < NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  // Q fragments stay in registers for the narrow slices; the 64-key slice
+  // (more live accumulators) re-reads them from shared memory per chunk.
+  constexpr bool kQRegs = KW <= 32;
+  const uint32_t q_lane = s_addr(Qs + (wr + (lane & 15)) * LDQ + (lane >> 4) * 8);
+  uint32_t qf[kQRegs ? DH / 16 : 1][4];
+  if constexpr (kQRegs) {
+#pragma unroll
+    for (int k = 0; k < DH / 16; ++k)
+      ldm_x4(q_lane + k * 32, qf[k][0], qf[k][1], qf[k][2], qf[k][3]);
+  }
 
   bool ok = true;
   for (int ch = 0; ch < nchunks && ok; ++ch) {
     const int s = ch % S;
     ok = mbar_wait(full0 + 8 * s, (ch / S) & 1, abort_flag, a.err);
     if (!ok) break;
-    if (live) {
+    const int jlo = kbeg + ch * CH + kof;  // first key of this warp's slice
+    if (live && jlo < kend) {
       const uint32_t Kt = stage0 + s * Cfg::kStageBytes;
       const uint32_t Vt = Kt + Cfg::kTileBytes;
-      float sc[8][4];
+      float sc[KW / 8][4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+      for (int i = 0; i < KW / 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
-      for (int k0 = 0; k0 < DH; k0 += 16) {
+      for (int k = 0; k < DH / 16; ++k) {
         uint32_t a0, a1, a2, a3;
-        ldm_x4(s_addr(Qs + (wr + (lane & 15)) * LDQ + k0 + (lane >> 4) * 8), a0, a1, a2, a3);
+        if constexpr (kQRegs) {
+          a0 = qf[k][0];
+          a1 = qf[k][1];
+          a2 = qf[k][2];
+          a3 = qf[k][3];
+        } else {
+          ldm_x4(q_lane + k * 32, a0, a1, a2, a3);
+        }
 #pragma unroll
-        for (int nt = 0; nt < 8; nt += 2) {
+        for (int nt = 0; nt < KW / 8; nt += 2) {
           uint32_t b0, b1, b2, b3;
-          const int key = nt * 8 + (lane & 7) + ((lane >> 4) << 3);
-          const int c = (k0 >> 3) + ((lane >> 3) & 1);
+          const int key = kof + nt * 8 + (lane & 7) + ((lane >> 4) << 3);
+          const int c = 2 * k + ((lane >> 3) & 1);
           ldm_x4(tile_addr<DH>(Kt, key, c), b0, b1, b2, b3);
           mma_bf16(sc[nt], a0, a1, a2, a3, b0, b1);
           mma_bf16(sc[nt + 1], a0, a1, a2, a3, b2, b3);
         }
       }
-      const int jbase = kbeg + ch * kChunk + 2 * (lane & 3);
       float mx_a = -INFINITY, mx_b = -INFINITY;
+      if (jlo + KW <= jfree) {
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < KW / 8; ++nt) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int j = jbase + nt * 8 + e;
-          const bool va = j < kend && j <= pos_a, vb = j < kend && j <= pos_b;
-          sc[nt][e] = va ? sc[nt][e] * a.scale_log2 : -INFINITY;
-          sc[nt][2 + e] = vb ? sc[nt][2 + e] * a.scale_log2 : -INFINITY;
-          mx_a = fmaxf(mx_a, sc[nt][e]);
-          mx_b = fmaxf(mx_b, sc[nt][2 + e]);
+          for (int e = 0; e < 2; ++e) {
+            sc[nt][e] *= a.scale_log2;
+            sc[nt][2 + e] *= a.scale_log2;
+            mx_a = fmaxf(mx_a, sc[nt][e]);
+            mx_b = fmaxf(mx_b, sc[nt][2 + e]);
+          }
+        }
+      } else {
+        const int jbase = jlo + 2 * (lane & 3);
+#pragma unroll
+        for (int nt = 0; nt < KW / 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int j = jbase + nt * 8 + e;
+            const bool va = j < kend && j <= pos_a, vb = j < kend && j <= pos_b;
+            sc[nt][e] = va ? sc[nt][e] * a.scale_log2 : -INFINITY;
+            sc[nt][2 + e] = vb ? sc[nt][2 + e] * a.scale_log2 : -INFINITY;
+            mx_a = fmaxf(mx_a, sc[nt][e]);
+            mx_b = fmaxf(mx_b, sc[nt][2 + e]);
+          }
         }
       }
 #pragma unroll
@@ -320,13 +397,15 @@ __global__ void __launch_bounds__(kThreads)
       const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
       const float al_a = mn_a == -INFINITY ? 1.f : exp2f(m_a - mn_a);
       const float al_b = mn_b == -INFINITY ? 1.f : exp2f(m_b - mn_b);
+      const float sub_a = mn_a == -INFINITY ? 0.f : mn_a;
+      const float sub_b = mn_b == -INFINITY ? 0.f : mn_b;
       float ps_a = 0.f, ps_b = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < KW / 8; ++nt) {
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          sc[nt][e] = mn_a == -INFINITY ? 0.f : exp2f(sc[nt][e] - mn_a);
-          sc[nt][2 + e] = mn_b == -INFINITY ? 0.f : exp2f(sc[nt][2 + e] - mn_b);
+          sc[nt][e] = exp2f(sc[nt][e] - sub_a);
+          sc[nt][2 + e] = exp2f(sc[nt][2 + e] - sub_b);
           ps_a += sc[nt][e];
           ps_b += sc[nt][2 + e];
         }
@@ -343,12 +422,12 @@ __global__ void __launch_bounds__(kThreads)
         o[i][3] *= al_b;
       }
 #pragma unroll
-      for (int kt = 0; kt < 4; ++kt) {
+      for (int kt = 0; kt < KW / 16; ++kt) {
         const uint32_t p0 = pack2(sc[2 * kt][0], sc[2 * kt][1]);
         const uint32_t p1 = pack2(sc[2 * kt][2], sc[2 * kt][3]);
         const uint32_t p2 = pack2(sc[2 * kt + 1][0], sc[2 * kt + 1][1]);
         const uint32_t p3 = pack2(sc[2 * kt + 1][2], sc[2 * kt + 1][3]);
-        const int key = kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int key = kof + kt * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
 #pragma unroll
         for (int nt = 0; nt < NT; nt += 2) {
           uint32_t b0, b1, b2, b3;
@@ -361,43 +440,92 @@ __global__ void __launch_bounds__(kThreads)
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
   }
-  if (!live || !ok) return;
-
 #pragma unroll
   for (int o_ = 1; o_ <= 2; o_ <<= 1) {
     l_a += __shfl_xor_sync(0xffffffffu, l_a, o_);
     l_b += __shfl_xor_sync(0xffffffffu, l_b, o_);
   }
   const int col = 2 * (lane & 3);
-  if (splits_here == 1) {
-    const float ia = l_a > 0.f ? 1.f / l_a : 0.f, ib = l_b > 0.f ? 1.f / l_b : 0.f;
+
+  if constexpr (KS == 1) {
+    if (!live || !ok) return;
+    if (splits_here == 1) {
+      const float ia = l_a > 0.f ? 1.f / l_a : 0.f, ib = l_b > 0.f ? 1.f / l_b : 0.f;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = half ? rb : ra;
-      if (r >= nr) continue;
-      const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
-      __nv_bfloat16* dst = a.out + ((int64_t)(t0 + t) * a.hq + h) * DH + col;
-      const float inv = half ? ib : ia;
+      for (int half = 0; half < 2; ++half) {
+        const int r = half ? rb : ra;
+        if (r >= nr) continue;
+        const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+        __nv_bfloat16* dst = a.out + ((int64_t)(t0 + t) * a.hq + h) * DH + col;
+        const float inv = half ? ib : ia;
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<uint32_t*>(dst + nt * 8) =
-            pack2(o[nt][2 * half] * inv, o[nt][2 * half + 1] * inv);
+        for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<uint32_t*>(dst + nt * 8) =
+              pack2(o[nt][2 * half] * inv, o[nt][2 * half + 1] * inv);
+      }
+    } else {
+      const int64_t unit = (((int64_t)b * a.hkv + g) * a.row_tiles + rt) * a.n_splits + split;
+      float* po = a.part_o + unit * kRows * DH;
+      float* pml = a.part_ml + unit * kRows * 2;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int r = half ? rb : ra;
+        if (r >= nr) continue;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+          *reinterpret_cast<float2*>(po + r * DH + nt * 8 + col) =
+              make_float2(o[nt][2 * half], o[nt][2 * half + 1]);
+        if ((lane & 3) == 0) {
+          pml[r * 2] = half ? m_b : m_a;
+          pml[r * 2 + 1] = half ? l_b : l_a;
+        }
+      }
     }
   } else {
-    const int64_t unit = (((int64_t)b * a.hkv + g) * a.row_tiles + rt) * a.n_splits + split;
-    float* po = a.part_o + unit * kRows * DH;
-    float* pml = a.part_ml + unit * kRows * 2;
+    // ---- merge the KS key slices of each row through the (drained) ring ----
+    // Every slice has finished reading the ring; leave together if any wait
+    // gave up (bar.red makes the decision uniform across the consumers).
+    if (consumer_any(NW * 32, !ok || *abort_flag)) return;
+    constexpr int LP = Cfg::kLdPart;
+    float* part = reinterpret_cast<float*>(smem);
+    float2* pml = reinterpret_cast<float2*>(part + NW * 16 * LP);
+    if (live) {
+      // partial row p = si * (MTP * 16) + r, for tile row r = wr + (0..15)
+      const int pa = si * (MTP * 16) + ra, pb = pa + 8;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = half ? rb : ra;
-      if (r >= nr) continue;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float2*>(po + r * DH + nt * 8 + col) =
-            make_float2(o[nt][2 * half], o[nt][2 * half + 1]);
+      for (int nt = 0; nt < NT; ++nt) {
+        *reinterpret_cast<float2*>(part + pa * LP + nt * 8 + col) = make_float2(o[nt][0], o[nt][1]);
+        *reinterpret_cast<float2*>(part + pb * LP + nt * 8 + col) = make_float2(o[nt][2], o[nt][3]);
+      }
       if ((lane & 3) == 0) {
-        pml[r * 2] = half ? m_b : m_a;
-        pml[r * 2 + 1] = half ? l_b : l_a;
+        pml[pa] = make_float2(m_a, l_a);
+        pml[pb] = make_float2(m_b, l_b);
+      }
+    }
+    consumer_sync(NW * 32);
+    const int64_t unit = (((int64_t)b * a.hkv + g) * a.row_tiles + rt) * a.n_splits + split;
+    for (int idx = threadIdx.x; idx < nr * DH; idx += NW * 32) {
+      const int r = idx / DH, d = idx % DH;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) mx = fmaxf(mx, pml[k * (MTP * 16) + r].x);
+      float l = 0.f, acc = 0.f;
+#pragma unroll
+      for (int k = 0; k < KS; ++k) {
+        const float2 ml = pml[k * (MTP * 16) + r];
+        const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - mx);
+        l += w * ml.y;
+        acc += w * part[(k * (MTP * 16) + r) * LP + d];
+      }
+      if (splits_here == 1) {
+        const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+        a.out[((int64_t)(t0 + t) * a.hq + h) * DH + d] = __float2bfloat16_rn(l > 0.f ? acc / l : 0.f);
+      } else {
+        a.part_o[unit * kRows * DH + r * DH + d] = acc;
+        if (d == 0) {
+          a.part_ml[unit * kRows * 2 + r * 2] = mx;
+          a.part_ml[unit * kRows * 2 + r * 2 + 1] = l;
+        }
       }
     }
   }
@@ -499,25 +627,40 @@ __global__ void attn_tma_combine_kernel(TmaArgs a, int dh) {
   }
 }
 
-template <int DH>
+template <int DH, int KW>
 int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
                cudaStream_t s) {
   using Cfg = TmaCfg<DH>;
-  static bool attr = false;
-  if (!attr) {
+  // The shared-memory opt-in is per device; remember it per device.
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(attr_set & bit)) {
     const cudaError_t e = cudaFuncSetAttribute(
-        attn_tma_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+        attn_tma_kernel<DH, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "attn_tma: smem attribute: %s", cudaGetErrorString(e));
-    attr = true;
+    attr_set |= bit;
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
-  attn_tma_kernel<DH><<<grid, kThreads, Cfg::kSmem, s>>>(km, vm, a);
+  attn_tma_kernel<DH, KW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
   MS_TRY(check_launch("attn_tma_kernel"));
   if (a.n_splits > 1) {
     attn_tma_combine_kernel<<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a, DH);
     MS_TRY(check_launch("attn_tma_combine_kernel"));
   }
   return MS_OK;
+}
+
+// Slice width: the fewest m-tiles that cover the batch's widest row tile,
+// and the remaining consumer warps split each chunk's keys.
+template <int DH>
+int launch_by_rows(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
+                   int max_rows, cudaStream_t s) {
+  const int mt = (min(max_rows, kRows) + 15) / 16;
+  if (mt <= 1) return launch_tma<DH, TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
+  if (mt == 2) return launch_tma<DH, 2 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
+  return launch_tma<DH, 4 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
 }
 
 }  // namespace
@@ -548,8 +691,9 @@ int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int l
   a.num_blocks = c.num_blocks;
   a.hq = hq;
   a.hkv = c.n_kv_heads;
-  attn_tc_plan(bt.max_q_len, hq / c.n_kv_heads, max_context, bt.n_seqs, c.n_kv_heads,
-               &a.row_tiles, &a.n_splits, &a.split_len);
+  const int group = hq / c.n_kv_heads;
+  attn_tc_plan(bt.max_q_len, group, max_context, bt.n_seqs, c.n_kv_heads, &a.row_tiles,
+               &a.n_splits, &a.split_len);
   a.scale_log2 = kLog2e / sqrtf((float)c.d_head);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.err = device_error_word();
@@ -557,8 +701,8 @@ int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int l
       attn_tc_scratch_bytes(bt.n_seqs, c.n_kv_heads, c.d_head, a.row_tiles, a.n_splits);
   if (need > scratch_bytes) {
     a.n_splits = 1;
-    a.split_len = ((max_context + kChunk - 1) / kChunk) * kChunk;
-    if (a.split_len <= 0) a.split_len = kChunk;
+    a.split_len = ((max_context + 63) / 64) * 64;
+    if (a.split_len <= 0) a.split_len = 64;
   } else if (need > 0) {
     const size_t units = (size_t)bt.n_seqs * a.hkv * a.row_tiles * a.n_splits;
     a.part_o = static_cast<float*>(scratch);
@@ -568,8 +712,9 @@ int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int l
   CUtensorMap km, vm;
   MS_TRY(pool_map(c.k_pool[layer], rows, c.d_head, c.block_size, &km));
   MS_TRY(pool_map(c.v_pool[layer], rows, c.d_head, c.block_size, &vm));
-  if (c.d_head == 64) return launch_tma<64>(a, km, vm, bt.n_seqs, s);
-  return launch_tma<128>(a, km, vm, bt.n_seqs, s);
+  const int max_rows = bt.max_q_len * group;
+  if (c.d_head == 64) return launch_by_rows<64>(a, km, vm, bt.n_seqs, max_rows, s);
+  return launch_by_rows<128>(a, km, vm, bt.n_seqs, max_rows, s);
 }
 
 }  // namespace ms

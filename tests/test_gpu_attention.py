@@ -78,6 +78,18 @@ def test_tensor_core_attention_decode_and_verify(hq, hkv, dh, bs) -> None:
     torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("dh", [64, 128])
+@pytest.mark.parametrize("qlen", [1, 2, 5])
+def test_tensor_core_attention_key_slices(dh: int, qlen: int) -> None:
+    """Uniform decode (8 rows: every consumer warp takes a key slice of each
+    chunk), two-token (16 rows) and verify (40 rows) batches, with contexts
+    that end mid-chunk, mid-slice and on a chunk boundary."""
+    ctx = [1, 16, 127, 128, 129, 700, 2049, 40]
+    got, ref = _case("bfloat16", 32, 4, dh, 16, [max(c, qlen) for c in ctx], [qlen] * len(ctx),
+                     seed=dh + qlen)
+    torch.testing.assert_close(got, ref, rtol=2e-2, atol=2e-2)
+
+
 @pytest.mark.parametrize("hq,hkv,dh", [(16, 4, 64), (8, 2, 128)])
 def test_tensor_core_attention_prefill_tiles(hq, hkv, dh) -> None:
     """Long query runs span several 64-row tiles with a causal staircase."""
