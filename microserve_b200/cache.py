@@ -93,9 +93,21 @@ class BlockAllocator:
         if self._refcount[block] == 0:
             self._free.append(block)
 
-    def free_many(self, blocks: Sequence[int]) -> None:
-        for b in blocks:
-            self.free(int(b))
+    def free_many(self, blocks: Sequence[int] | np.ndarray) -> None:
+        """``free`` each block in order (blocks reaching zero refs rejoin the
+        free list in that order)."""
+        arr = np.asarray(blocks, dtype=np.int64).reshape(-1)
+        if arr.size == 0:
+            return
+        if np.unique(arr).size != arr.size:
+            for b in arr.tolist():
+                self.free(b)
+            return
+        if np.any(self._refcount[arr] == 0):
+            bad = int(arr[self._refcount[arr] == 0][0])
+            raise ValueError(f"double free of block {bad}")
+        self._refcount[arr] -= 1
+        self._free.extend(arr[self._refcount[arr] == 0].tolist())
 
     def check_invariants(self) -> None:
         """Assert internal consistency; used by tests."""
@@ -289,7 +301,27 @@ class PagedKVCache:
         return row
 
     def rows_of(self, seq_ids: Sequence[int]) -> np.ndarray:
-        return np.fromiter((self._row_of(s) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        """Dense-table rows of ``seq_ids`` (new sequences get a row)."""
+        try:
+            return np.fromiter(map(self._rows.__getitem__, seq_ids), dtype=np.int64,
+                               count=len(seq_ids))
+        except KeyError:
+            return np.fromiter((self._row_of(s) for s in seq_ids), dtype=np.int64,
+                               count=len(seq_ids))
+
+    def _existing_rows(self, seq_ids: Sequence[int]) -> np.ndarray:
+        """Rows of sequences that must already exist (KeyError otherwise)."""
+        return np.fromiter(map(self._rows.__getitem__, seq_ids), dtype=np.int64,
+                           count=len(seq_ids))
+
+    def num_tokens_many(self, seq_ids: Sequence[int]) -> np.ndarray:
+        """``num_tokens`` of each sequence (0 for unknown ones), int64."""
+        get = self._rows.get
+        rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        out = np.zeros(len(seq_ids), dtype=np.int64)
+        known = rows >= 0
+        out[known] = self._ntok[rows[known]]
+        return out
 
     def _ensure_columns(self, n: int) -> None:
         if n > self._table.shape[1]:
@@ -325,13 +357,10 @@ class PagedKVCache:
         if total:
             self._ensure_columns(int((nblk + need).max()))
             blocks = self.allocator.allocate_many(total)
-            pos = 0
-            for i in np.nonzero(need)[0]:
-                k = int(need[i])
-                r = int(rows[i])
-                nb = int(nblk[i])
-                self._table[r, nb : nb + k] = blocks[pos : pos + k]
-                pos += k
+            # sequence i takes the next need[i] blocks, in batch order
+            owner = np.repeat(np.arange(len(rows)), need)
+            first = np.repeat(np.cumsum(need) - need, need)
+            self._table[rows[owner], nblk[owner] + (np.arange(total) - first)] = blocks
             self._nblk[rows] = (nblk + need).astype(np.int32)
         # positions ntok .. ntok+count-1 of each sequence, flattened
         n_total = int(counts.sum())
@@ -361,15 +390,20 @@ class PagedKVCache:
 
     def truncate_many(self, seq_ids: Sequence[int], num_tokens: Sequence[int] | np.ndarray) -> None:
         """Vectorised ``truncate`` (speculative rollback, reference cache.py:210-222)."""
-        rows = np.fromiter((self._rows[s] for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        rows = self._existing_rows(seq_ids)
         n = np.asarray(num_tokens, dtype=np.int64)
         if np.any(n > self._ntok[rows]):
             raise ValueError("truncate cannot grow a sequence")
         keep = (n + self.block_size - 1) // self.block_size
         nblk = self._nblk[rows].astype(np.int64)
-        for i in np.nonzero(keep < nblk)[0]:
-            r = int(rows[i])
-            self.allocator.free_many(self._table[r, int(keep[i]) : int(nblk[i])].tolist())
+        drop = np.maximum(nblk - keep, 0)
+        total = int(drop.sum())
+        if total:
+            # blocks past the new end, sequence by sequence, in table order
+            owner = np.repeat(np.arange(len(rows)), drop)
+            first = np.repeat(np.cumsum(drop) - drop, drop)
+            cols = keep[owner] + (np.arange(total) - first)
+            self.allocator.free_many(self._table[rows[owner], cols])
         self._nblk[rows] = np.minimum(nblk, keep).astype(np.int32)
         self._ntok[rows] = n
 
@@ -381,7 +415,7 @@ class PagedKVCache:
     # -- batch tables --------------------------------------------------------
     def table_rows(self, seq_ids: Sequence[int]) -> tuple[np.ndarray, np.ndarray, int]:
         """Host ``(B, max_blocks)`` int32 tables, ``(B,)`` token counts and the width."""
-        rows = np.fromiter((self._rows[s] for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        rows = self._existing_rows(seq_ids)
         width = max(1, int(self._nblk[rows].max())) if len(rows) else 1
         return self._table[rows, :width], self._ntok[rows].copy(), width
 

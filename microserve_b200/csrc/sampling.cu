@@ -550,79 +550,67 @@ __device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, b
 // Inverse-CDF draw over weights w(i) in vocabulary order: the first index
 // whose running sum exceeds u * total.  Falls back to the last positive
 // weight when rounding leaves the target past the end.
+//
+// Every thread owns a contiguous segment of the row: it sums its segment (in
+// double), a block scan places the segments, and the one thread whose
+// segment holds the target walks it.  Two passes over the row and three
+// barriers, with no serial warp-wide walk.
 template <typename W>
 __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  int seg = (V + nw - 1) / nw;
-  seg = (seg + 31) & ~31;
-  const int s0 = min(V, warp * seg), s1 = min(V, s0 + seg);
-  // phase 1: segment totals and the last positive index
-  float part = 0.f;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int seg = (V + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int s0 = min(V, tid * seg), s1 = min(V, s0 + seg);
+  double part = 0.0;
   int last = -1;
-#pragma unroll 4
-  for (int i = s0 + lane; i < s1; i += 32) {
+  for (int i = s0; i < s1; ++i) {
     const float v = w(i);
-    part += v;
+    part += (double)v;
     if (v > 0.f) last = i;
   }
-  part = warp_sum(part);
+  // block exclusive scan of the segment sums (lanes, then warps)
+  double inc = part;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
-  __syncthreads();
-  if (lane == 0) {
-    sm.red_d[warp] = (double)part;
-    sm.red_i[warp] = last;
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
   }
+  int lp = last;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+  __syncthreads();  // earlier users of red_* are done
+  if (lane == 31) sm.red_d[warp] = inc;
+  if (lane == 0) sm.red_i[warp] = lp;
+  if (tid == 0) sm.red_i[40] = -1;
   __syncthreads();
-  // phase 2: warp 0 scans the segment totals in double
-  if (warp == 0) {
-    double v = lane < nw ? sm.red_d[lane] : 0.0;
-    int lp = lane < nw ? sm.red_i[lane] : -1;
-    double inc = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double t = __shfl_up_sync(0xffffffffu, inc, o);
-      if (lane >= o) inc += t;
-    }
-    const double total = __shfl_sync(0xffffffffu, inc, 31);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
-    const double target = (double)u * total;
-    const unsigned hit = __ballot_sync(0xffffffffu, lane < nw && inc > target && v > 0.0);
-    if (lane == 0) {
-      sm.red_i[32] = hit ? (__ffs(hit) - 1) : -1;  // target warp
-      sm.red_i[33] = lp;                            // global last positive
-      sm.red_d[32] = target;
-    }
-    if (hit) {
-      const int tw = __ffs(hit) - 1;
-      const double base = __shfl_sync(0xffffffffu, inc - v, tw);
-      if (lane == 0) sm.red_d[33] = base;
-    }
+  double before = 0.0, total = 0.0;
+  int glast = -1;
+  for (int k = 0; k < nw; ++k) {
+    const double t = sm.red_d[k];
+    if (k < warp) before += t;
+    total += t;
+    glast = max(glast, sm.red_i[k]);
   }
-  __syncthreads();
-  const int tw = sm.red_i[32];
-  if (tw >= 0 && warp == tw) {
-    const double target = sm.red_d[32];
-    double run = sm.red_d[33];
-    int found = -1;
-    for (int b0 = s0; b0 < s1 && found < 0; b0 += 32) {
-      const int i = b0 + lane;
-      const float v = i < s1 ? w(i) : 0.f;
-      float inc = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float t = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += t;
+  // Segment t covers [E_t, E_t+1) with both ends computed the same way by
+  // the two threads that share them, so exactly one segment claims a target.
+  const double up = __shfl_up_sync(0xffffffffu, inc, 1);
+  const double e0 = before + (lane == 0 ? 0.0 : up), e1 = before + inc;
+  const double target = (double)u * total;
+  if (part > 0.0 && e0 <= target && target < e1) {
+    double run = e0;
+    int found = last;  // rounding inside the segment: its last positive weight
+    for (int i = s0; i < s1; ++i) {
+      const float v = w(i);
+      run += (double)v;
+      if (v > 0.f && run > target) {
+        found = i;
+        break;
       }
-      const unsigned hit = __ballot_sync(0xffffffffu, i < s1 && v > 0.f && run + (double)inc > target);
-      if (hit) found = b0 + __ffs(hit) - 1;
-      run += (double)__shfl_sync(0xffffffffu, inc, 31);
     }
-    if (lane == 0) sm.red_i[34] = found >= 0 ? found : sm.red_i[warp];
+    sm.red_i[40] = found;
   }
   __syncthreads();
-  int res = tw >= 0 ? sm.red_i[34] : sm.red_i[33];
+  int res = sm.red_i[40];
+  if (res < 0) res = glast;
   if (res < 0) res = 0;
   __syncthreads();
   return res;

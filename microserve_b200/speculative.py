@@ -26,6 +26,7 @@ lane j, accept roll i on lane 64+i, the residual/bonus draw on lane 128.
 from __future__ import annotations
 
 import ctypes
+import itertools
 from dataclasses import dataclass
 
 import numpy as np
@@ -47,6 +48,18 @@ class VerificationResult:
     tokens: list[int]  # accepted drafts followed by exactly one extra token
     num_accepted: int
     num_proposed: int
+
+
+def _tails(requests: list[Request], counts: np.ndarray) -> list[list[int]]:
+    """The last ``counts[b]`` token ids of each request (its uncached suffix)."""
+    out = []
+    for r, k in zip(requests, counts.tolist(), strict=True):
+        o = r.output_ids
+        if k <= len(o):
+            out.append(o[len(o) - k :] if k else [])
+        else:
+            out.append(r.prompt_ids[len(r.prompt_ids) - (k - len(o)) :] + o)
+    return out
 
 
 def _u64_tensor(values: list[int], device: torch.device) -> torch.Tensor:
@@ -172,8 +185,8 @@ class SpeculativeDecoder:
         if not requests:
             return []
         G, B, V = self.gamma, len(requests), self.target.cfg.vocab_size
-        for r in requests:
-            validate(r.sampling)
+        for cfg in {id(r.sampling): r.sampling for r in requests}.values():
+            validate(cfg)
         plan = self._plan(requests, target_cache, generators)
         launches0 = _lib.launch_count()
         self._launch(plan, target_cache)
@@ -197,14 +210,15 @@ class SpeculativeDecoder:
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
         dcache = self.draft_cache
-        d_cached = np.fromiter((dcache.num_tokens(i) for i in ids), np.int64, B)
-        t_cached = np.fromiter((target_cache.num_tokens(i) for i in ids), np.int64, B)
-        pending = [r.tail(int(c)) for r, c in zip(requests, d_cached, strict=True)]
-        prefix = [r.tail(int(c)) for r, c in zip(requests, t_cached, strict=True)]
-        n0 = np.fromiter((len(p) for p in pending), np.int64, B)
-        npre = np.fromiter((len(p) for p in prefix), np.int64, B)
+        d_cached = dcache.num_tokens_many(ids)
+        t_cached = target_cache.num_tokens_many(ids)
+        n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests), np.int64, B)
+        n0 = n_tok - d_cached
+        npre = n_tok - t_cached
         if np.any(npre < 1):
             raise ValueError("every request needs at least one uncomputed token")
+        pending = _tails(requests, n0)
+        prefix = _tails(requests, npre)
 
         # Slots for the whole round, reserved up front (all-or-nothing).
         dslots = dcache.append_many(ids, n0 + (G - 1))
@@ -220,7 +234,7 @@ class SpeculativeDecoder:
         T0 = int(q0[-1])
         seg0 = np.repeat(np.arange(B), n0)
         within0 = np.arange(T0) - q0[:-1][seg0]
-        ids0 = np.fromiter((t for p in pending for t in p), np.int32, T0)
+        ids0 = np.fromiter(itertools.chain.from_iterable(pending), np.int32, T0)
         pos0 = d_cached[seg0] + within0
         slots0 = dslots[dstart[:-1][seg0] + within0]
         ctx0 = d_cached + n0
@@ -240,7 +254,8 @@ class SpeculativeDecoder:
         withinv = np.arange(Tv) - qv[:-1][segv]
         idsv = np.zeros(Tv, np.int32)
         is_prefix = withinv < npre[segv]
-        idsv[is_prefix] = np.fromiter((t for p in prefix for t in p), np.int32, int(npre.sum()))
+        idsv[is_prefix] = np.fromiter(itertools.chain.from_iterable(prefix), np.int32,
+                                      int(npre.sum()))
         posv = t_cached[segv] + withinv
         ctxv = t_cached + npre + G
         rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
@@ -249,6 +264,7 @@ class SpeculativeDecoder:
         seeds = [generators[i].initial_seed() for i in ids]
         steps = [r.rng_step for r in requests]
         params = make_params([r.sampling for r in requests], seeds, steps)
+        params_n_tok = n_tok
         pwords = params.view(np.int32)
 
         parts = [
@@ -271,6 +287,7 @@ class SpeculativeDecoder:
             "ctx0": int(ctx0.max()), "ctxv": int(ctxv.max()),
             "ctx_j": [int(c.max()) for c in ctx_j],
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
+            "n_tok": params_n_tok,
         }
 
     def _launch(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
@@ -347,19 +364,22 @@ class SpeculativeDecoder:
     ) -> list[list[int]]:
         G = self.gamma
         ids: list[int] = plan["ids"]  # type: ignore[assignment]
-        n_tok = np.fromiter((r.num_tokens for r in requests), np.int64, len(requests))
+        n_tok: np.ndarray = plan["n_tok"]  # type: ignore[assignment]
         keep = n_tok + nacc
         target_cache.truncate_many(ids, keep)
         d_len = plan["d_cached"] + plan["n0"] + (G - 1)  # type: ignore[operator]
         self.draft_cache.truncate_many(ids, np.minimum(d_len, keep))
+        rows = tokens.tolist()
+        nacc_l = nacc.tolist()
+        keep_l = keep.tolist()
         results: list[list[int]] = []
-        for b, r in enumerate(requests):
-            n = int(nacc[b])
-            r.num_computed = int(keep[b])
+        for r, row, n, kp in zip(requests, rows, nacc_l, keep_l, strict=True):
+            r.num_computed = kp
             r.num_draft_proposed += G
             r.num_draft_accepted += n
             r.rng_step += 1
-            results.append(tokens[b, : n + 1].tolist())
+            del row[n + 1 :]
+            results.append(row)
         self.num_proposed += G * len(requests)
         self.num_accepted += int(nacc.sum())
         return results
