@@ -116,7 +116,7 @@ __device__ void block_argmax(float v, int idx, RowSmem& sm, float& out_v, int& o
 }
 
 // Pass over the row computing max and first argmax of x.
-__device__ void row_argmax(const Dist& d, int V, RowSmem& sm, float& m, int& am) {
+__device__ void row_argmax(const Dist d, int V, RowSmem& sm, float& m, int& am) {
   float best = -INFINITY;
   int bi = 0x7fffffff;
 #pragma unroll 4
@@ -225,7 +225,7 @@ __device__ void hist_find_from_top(RowSmem& sm, float target_f, uint32_t target_
 }
 
 // k-th largest x over the row (1 <= k <= V), exact.
-__device__ float radix_kth_largest(const Dist& d, int V, int k, RowSmem& sm) {
+__device__ float radix_kth_largest(const Dist d, int V, int k, RowSmem& sm) {
   uint32_t prefix = 0, mask = 0;
   uint32_t k_rem = (uint32_t)k;
   const int warp = threadIdx.x >> 5;
@@ -252,7 +252,7 @@ __device__ float radix_kth_largest(const Dist& d, int V, int k, RowSmem& sm) {
 
 // The top-p crossing value: first x in descending order whose inclusive
 // cumulative probability reaches top_p.  Returns -inf if it never does.
-__device__ float radix_top_p(const Dist& d, int V, float top_p, RowSmem& sm) {
+__device__ float radix_top_p(const Dist d, int V, float top_p, RowSmem& sm) {
   uint32_t prefix = 0, mask = 0;
   float above_total = 0.f;
   const int warp = threadIdx.x >> 5;
@@ -286,101 +286,108 @@ __device__ float radix_top_p(const Dist& d, int V, float top_p, RowSmem& sm) {
 // floor((max - x) * 64) clamped to kLinBins-1: one pass with little atomic
 // contention (logits spread over many bins, unlike their exponent bits), a
 // block scan to find the bin holding the k-th largest value / the top-p
-// crossing value, then an exact choice among that bin's few candidates.  A
-// bin with more than kCand candidates (flat or tied rows) falls back to the
-// radix routines above.
+// crossing value, then an exact choice among that bin's candidates, ranked
+// in shared memory (value descending, index ascending).  A bin with more
+// than kCand candidates (flat or tied rows) falls back to the radix
+// routines above.
+//
+// Top-p bin masses use two 32-bit integer atomics per element (shared-memory
+// float and 64-bit atomics are much slower): a count, and the deficit
+// 1 - e * 2^(b/64 log2 e) of the element's mass e = exp(x - max) against the
+// bin's upper edge, in 2^-22 fixed point.  A bin's mass is then
+// exp(-b/64) * (count - deficit * 2^-22), exact to about 2^-22 per element,
+// and every sum fits 32 bits for up to 65536 elements per bin.
 constexpr int kLinBins = 2048;
 constexpr int kCand = 512;
 constexpr float kBinsPerUnit = 64.f;
+constexpr float kDefScale = 4194304.f;  // 2^22
+// shared words: counts, deficits, candidate keys (u64), ranked keys (u64)
+constexpr int kLinWords = 2 * kLinBins + 4 * kCand;
 
 __device__ __forceinline__ int lin_bin(float m, float x) {
   const float t = (m - x) * kBinsPerUnit;
   return t < (float)(kLinBins - 1) ? (int)t : kLinBins - 1;
 }
+// The element's deficit against its bin's upper edge, fixed point.
+__device__ __forceinline__ uint32_t lin_deficit(float m, float x, int b) {
+  if (b >= kLinBins - 1) return 0u;
+  const float r = __expf((x - m) + (float)b * (1.f / kBinsPerUnit));
+  return __float2uint_rn(fmaxf(1.f - r, 0.f) * kDefScale);
+}
+__device__ __forceinline__ float lin_bin_mass(const uint32_t* Hc, const uint32_t* Hd, int b) {
+  const float cnt = (float)Hc[b] - (float)Hd[b] * (1.f / kDefScale);
+  return cnt * __expf(-(float)b * (1.f / kBinsPerUnit));
+}
 
-// Block-wide search over the kLinBins histogram for the first bin whose
-// inclusive prefix reaches the target.  Returns the bin (-1 if none) and the
-// amount in the bins before it.
-template <bool kFloat>
-__device__ int lin_find(const uint32_t* H, float target_f, uint32_t target_u, RowSmem& sm,
-                        float& before_f, uint32_t& before_u) {
+// Block-wide search over the kLinBins bins for the first bin whose inclusive
+// prefix (counts when Hd is null, masses otherwise) reaches `target`.
+// Returns the bin (-1 if none) and the amount in the bins before it.
+__device__ int lin_find(const uint32_t* Hc, const uint32_t* Hd, double target, RowSmem& sm,
+                        double& before) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int per = kLinBins / blockDim.x;
   const int b0 = threadIdx.x * per;
-  float lf = 0.f;
-  uint32_t lu = 0;
-  for (int j = 0; j < per; ++j) {
-    if (kFloat) lf += __uint_as_float(H[b0 + j]);
-    else lu += H[b0 + j];
-  }
-  float incf = lf;
-  uint32_t incu = lu;
+  double own = 0.0;
+  for (int j = 0; j < per; ++j)
+    own += Hd ? (double)lin_bin_mass(Hc, Hd, b0 + j) : (double)Hc[b0 + j];
+  double inc = own;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const float tf = __shfl_up_sync(0xffffffffu, incf, o);
-    const uint32_t tu = __shfl_up_sync(0xffffffffu, incu, o);
-    if (lane >= o) {
-      incf += tf;
-      incu += tu;
-    }
+    const double t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
   }
   __syncthreads();
-  if (lane == 31) {
-    sm.red[warp] = incf;
-    sm.red_i[warp] = (int)incu;
-  }
+  if (lane == 31) sm.red_d[warp] = inc;
   if (threadIdx.x == 0) sm.red_i[48] = -1;
   __syncthreads();
-  float wf = 0.f;
-  uint32_t wu = 0;
-  for (int w = 0; w < warp; ++w) {
-    wf += sm.red[w];
-    wu += (uint32_t)sm.red_i[w];
-  }
-  (void)nw;
-  const float exf = wf + incf - lf;  // before this thread's bins
-  const uint32_t exu = wu + incu - lu;
-  const bool hit = kFloat ? (exf < target_f && exf + lf >= target_f)
-                          : (exu < target_u && exu + lu >= target_u);
-  if (hit) {
-    float af = exf;
-    uint32_t au = exu;
+  double wb = 0.0;
+  for (int w = 0; w < warp && w < nw; ++w) wb += sm.red_d[w];
+  const double ex = wb + inc - own;  // before this thread's bins
+  if (ex < target && ex + own >= target) {
+    double a = ex;
     for (int j = 0; j < per; ++j) {
-      const uint32_t h = H[b0 + j];
-      const bool hb = kFloat ? (af + __uint_as_float(h) >= target_f) : (au + h >= target_u);
-      if (hb) {
+      const double h = Hd ? (double)lin_bin_mass(Hc, Hd, b0 + j) : (double)Hc[b0 + j];
+      if (a + h >= target) {
         sm.red_i[48] = b0 + j;
-        sm.red[48] = af;
-        sm.red_i[49] = (int)au;
+        sm.red_d[48] = a;
         break;
       }
-      if (kFloat) af += __uint_as_float(h);
-      else au += h;
+      a += h;
     }
   }
   __syncthreads();
   const int bin = sm.red_i[48];
-  before_f = sm.red[48];
-  before_u = (uint32_t)sm.red_i[49];
+  before = sm.red_d[48];
   __syncthreads();
   return bin;
 }
 
-// Gathers (value, index) of the kept elements in `bin` into the candidate
-// lists; returns their number (may exceed kCand: caller falls back).
-__device__ int lin_gather(const Dist& d, int V, int bin, uint32_t* cv, uint32_t* ci, RowSmem& sm) {
+// Gathers the sort keys (value descending, index ascending) of the kept
+// elements in `bin`; returns their number (may exceed kCand: caller falls
+// back).
+__device__ int lin_gather(const Dist d, int V, int bin, unsigned long long* keys, RowSmem& sm) {
   if (threadIdx.x == 0) sm.red_i[50] = 0;
   __syncthreads();
-#pragma unroll 4
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float xv = d.x(i);
+  auto note = [&](float xv, int i) {
     if (xv >= d.thresh && lin_bin(d.m, xv) == bin) {
       const int slot = atomicAdd(&sm.red_i[50], 1);
-      if (slot < kCand) {
-        cv[slot] = __float_as_uint(xv);
-        ci[slot] = (uint32_t)i;
-      }
+      if (slot < kCand) keys[slot] = ((unsigned long long)fkey(xv) << 32) | (uint32_t)~(uint32_t)i;
     }
+  };
+  if (!d.divide && (reinterpret_cast<uintptr_t>(d.row) & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(d.row);
+    const int n4 = V >> 2;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) {
+      const float4 v = r4[i];
+      note(v.x, 4 * i);
+      note(v.y, 4 * i + 1);
+      note(v.z, 4 * i + 2);
+      note(v.w, 4 * i + 3);
+    }
+    for (int i = (n4 << 2) + threadIdx.x; i < V; i += blockDim.x) note(d.row[i], i);
+  } else {
+#pragma unroll 4
+    for (int i = threadIdx.x; i < V; i += blockDim.x) note(d.x(i), i);
   }
   __syncthreads();
   const int n = sm.red_i[50];
@@ -388,98 +395,110 @@ __device__ int lin_gather(const Dist& d, int V, int bin, uint32_t* cv, uint32_t*
   return n;
 }
 
-// k-th largest value (ties keep more).  ok=false: use the radix routine.
-__device__ float linear_kth(const Dist& d, int V, int k, RowSmem& sm, bool& ok) {
-  uint32_t* H = sm.hist;
-  uint32_t* cv = H + kLinBins;
-  uint32_t* ci = cv + kCand;
-  for (int i = threadIdx.x; i < kLinBins; i += blockDim.x) H[i] = 0u;
-  __syncthreads();
-  for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&H[lin_bin(d.m, d.x(i))], 1u);
-  __syncthreads();
-  float bf;
-  uint32_t bu;
-  const int bin = lin_find<false>(H, 0.f, (uint32_t)k, sm, bf, bu);
-  ok = false;
-  if (bin < 0) return -INFINITY;
-  const int n = lin_gather(d, V, bin, cv, ci, sm);  // d.thresh is -inf here
-  if (n > kCand || n == 0) return -INFINITY;
-  const int kk = k - (int)bu;  // rank wanted inside the bin (1-based)
-  if (threadIdx.x == 0) sm.red_i[51] = -1;
-  __syncthreads();
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const float vt = __uint_as_float(cv[t]);
-    int greater = 0, equal = 0;
-    for (int j = 0; j < n; ++j) {
-      const float vj = __uint_as_float(cv[j]);
-      greater += vj > vt;
-      equal += vj == vt;
+// Ranks keys[0, n) (distinct) and writes them to `sorted` in descending
+// order: rank = number of larger keys, one candidate per thread.
+__device__ void rank_keys_desc(const unsigned long long* keys, unsigned long long* sorted, int n) {
+  for (int c = threadIdx.x; c < n; c += blockDim.x) {
+    const unsigned long long kc = keys[c];
+    int r0 = 0, r1 = 0, r2 = 0, r3 = 0;
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+      r0 += keys[j] > kc;
+      r1 += keys[j + 1] > kc;
+      r2 += keys[j + 2] > kc;
+      r3 += keys[j + 3] > kc;
     }
-    if (greater < kk && kk <= greater + equal) sm.red_i[51] = (int)cv[t];
+    for (; j < n; ++j) r0 += keys[j] > kc;
+    sorted[(r0 + r1) + (r2 + r3)] = kc;
   }
   __syncthreads();
-  const int res = sm.red_i[51];
-  __syncthreads();
-  if (res == -1) return -INFINITY;
-  ok = true;
-  return __uint_as_float((uint32_t)res);
 }
 
-// Top-p on the histogram (already built by row_stats) of unnormalised
-// masses e = exp(x - m) of the kept elements, whose total is d.z: returns the
-// crossing value -- the first value in descending order whose inclusive mass
-// reaches top_p * z -- and the mass kept at and above it.  ok=false: use the
-// radix routine.
-__device__ float linear_top_p(const Dist& d, int V, float top_p, RowSmem& sm, bool& ok,
-                              float& z_keep) {
-  uint32_t* H = sm.hist;
-  uint32_t* cv = H + kLinBins;
-  uint32_t* ci = cv + kCand;
-  float* cm = reinterpret_cast<float*>(ci + kCand);
-  const float target = top_p * d.z;
-  float before;
-  uint32_t bu;
-  const int bin = lin_find<true>(H, target, 0u, sm, before, bu);
+// k-th largest value (ties keep more).  ok=false: use the radix routine.
+__device__ float linear_kth(const Dist d, int V, int k, RowSmem& sm, bool& ok) {
+  uint32_t* Hc = sm.hist;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(sm.hist + 2 * kLinBins);
+  unsigned long long* sorted = keys + kCand;
+  for (int i = threadIdx.x; i < kLinBins; i += blockDim.x) Hc[i] = 0u;
+  __syncthreads();
+  for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&Hc[lin_bin(d.m, d.x(i))], 1u);
+  __syncthreads();
+  double before;
+  const int bin = lin_find(Hc, nullptr, (double)k, sm, before);
   ok = false;
   if (bin < 0) return -INFINITY;
-  const int n = lin_gather(d, V, bin, cv, ci, sm);
+  const int n = lin_gather(d, V, bin, keys, sm);  // d.thresh is -inf here
   if (n > kCand || n == 0) return -INFINITY;
-  for (int t = threadIdx.x; t < n; t += blockDim.x) cm[t] = __expf(__uint_as_float(cv[t]) - d.m);
+  const int rank = k - (int)before;  // 1-based rank wanted inside the bin
+  if (rank < 1 || rank > n) return -INFINITY;
+  rank_keys_desc(keys, sorted, n);
+  const float v = kfloat((uint32_t)(sorted[rank - 1] >> 32));
+  __syncthreads();
+  ok = true;
+  return v;
+}
+
+// Top-p on the mass bins built by row_stats: returns the crossing value --
+// the first value in descending order whose inclusive mass reaches `target`
+// (top_p times the kept total) -- and the mass kept at and above it.
+// ok=false: use the radix routine.
+__device__ float linear_top_p(const Dist d, int V, double target, RowSmem& sm, bool& ok,
+                              double& z_keep) {
+  const uint32_t* Hc = sm.hist;
+  const uint32_t* Hd = sm.hist + kLinBins;
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(sm.hist + 2 * kLinBins);
+  unsigned long long* sorted = keys + kCand;
+  double before;
+  const int bin = lin_find(Hc, Hd, target, sm, before);
+  ok = false;
+  if (bin < 0 || bin >= kLinBins - 1 || Hc[bin] > 65536u) return -INFINITY;
+  const int n = lin_gather(d, V, bin, keys, sm);
+  if (n > kCand || n == 0) return -INFINITY;
+  rank_keys_desc(keys, sorted, n);
+  // inclusive prefix of the ranked candidates' exact masses, one per thread
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int c = threadIdx.x;
+  const float xc = c < n ? kfloat((uint32_t)(sorted[c] >> 32)) : -INFINITY;
+  const double e = c < n ? (double)__expf(xc - d.m) : 0.0;
+  double inc = e;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  if (lane == 31) sm.red_d[warp] = inc;
   if (threadIdx.x == 0) sm.red_i[51] = -1;
   __syncthreads();
-  for (int t = threadIdx.x; t < n; t += blockDim.x) {
-    const float vt = __uint_as_float(cv[t]);
-    const uint32_t it = ci[t];
-    float above = before;
-    for (int j = 0; j < n; ++j) {
-      const float vj = __uint_as_float(cv[j]);
-      if (vj > vt || (vj == vt && ci[j] < it)) above += cm[j];
-    }
-    if (above < target && above + cm[t] >= target) sm.red_i[51] = (int)cv[t];
+  double wb = before;
+  for (int w = 0; w < warp && w < nw; ++w) wb += sm.red_d[w];
+  const double cum = wb + inc;  // mass at and above candidate c
+  if (c < n && cum - e < target && cum >= target) sm.red_i[51] = c;
+  __syncthreads();
+  const int cross = sm.red_i[51];
+  if (cross < 0) {  // rounding found no crossing: radix fallback
+    __syncthreads();
+    return -INFINITY;
   }
+  const float cut = kfloat((uint32_t)(sorted[cross] >> 32));
+  // kept mass: through the last candidate equal to the cut (ties kept)
+  if (c < n && xc == cut && (c + 1 == n || kfloat((uint32_t)(sorted[c + 1] >> 32)) < cut))
+    sm.red_d[49] = cum;
   __syncthreads();
-  const int res = sm.red_i[51];
+  z_keep = sm.red_d[49];
   __syncthreads();
-  if (res == -1) return -INFINITY;  // rounding found no crossing: radix fallback
-  const float cut = __uint_as_float((uint32_t)res);
-  float part = 0.f;
-  for (int t = threadIdx.x; t < n; t += blockDim.x)
-    if (__uint_as_float(cv[t]) >= cut) part += cm[t];
-  z_keep = before + block_sum_b(part, sm);
   ok = true;
   return cut;
 }
 
-__device__ __forceinline__ bool linear_ok(RowSmem& sm, int V) {
-  // histogram + candidate values, indices and masses fit the histogram area
-  return (int)(blockDim.x >> 5) * kHistBins >= kLinBins + 3 * kCand && V >= 4096 &&
-         kLinBins % blockDim.x == 0;
+__device__ __forceinline__ bool linear_ok(int V) {
+  return V >= 4096 && kLinBins % blockDim.x == 0 && (int)blockDim.x >= kCand;
 }
 
 // Fills d.m / d.argmax (unless have_max), d.thresh, d.z, d.inv_z for a
-// logits row (mode 0).  The kept-mass total and the top-p histogram come out
-// of one pass; the top-p kept mass is derived from the bins, not re-summed.
-__device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, bool have_max) {
+// logits row (mode 0).  The kept-mass total and the top-p mass bins come out
+// of one pass; the top-p kept mass is derived from the bins and candidates.
+__device__ void row_stats(Dist& dref, int V, int top_k, float top_p, RowSmem& sm, bool have_max) {
+  Dist d = dref;  // register copy for the hot loops
   if (!have_max) {
     float m0;
     int am;
@@ -489,7 +508,7 @@ __device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, b
   }
   const float m = d.m;
   d.thresh = -INFINITY;
-  const bool lin = linear_ok(sm, V);
+  const bool lin = linear_ok(V);
   if (top_k > 0 && top_k < V) {
     bool ok = false;
     float kth = -INFINITY;
@@ -498,36 +517,72 @@ __device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, b
   }
   const bool want_p = top_p < 1.f;
   const bool hist = want_p && lin;
-  float* Hf = reinterpret_cast<float*>(sm.hist);
+  uint32_t* Hc = sm.hist;
+  uint32_t* Hd = sm.hist + kLinBins;
   if (hist) {
-    for (int i = threadIdx.x; i < kLinBins; i += blockDim.x) Hf[i] = 0.f;
+    for (int i = threadIdx.x; i < 2 * kLinBins; i += blockDim.x) Hc[i] = 0u;
     __syncthreads();
   }
   float zl = 0.f;
+  {
+    const float thresh = d.thresh;
+    auto note = [&](float xv) {
+      if (xv >= thresh) {
+        zl += __expf(xv - m);
+        if (hist) {
+          const int b = lin_bin(m, xv);
+          atomicAdd(&Hc[b], 1u);
+          atomicAdd(&Hd[b], lin_deficit(m, xv, b));
+        }
+      }
+    };
+    if (!d.divide && (reinterpret_cast<uintptr_t>(d.row) & 15) == 0) {
+      // staged / pre-divided rows: two float4 loads ahead of the atomics
+      const float4* r4 = reinterpret_cast<const float4*>(d.row);
+      const int n4 = V >> 2;
+      int i = threadIdx.x;
+      for (; i + (int)blockDim.x < n4; i += 2 * blockDim.x) {
+        const float4 a = r4[i], b = r4[i + blockDim.x];
+        note(a.x);
+        note(a.y);
+        note(a.z);
+        note(a.w);
+        note(b.x);
+        note(b.y);
+        note(b.z);
+        note(b.w);
+      }
+      for (; i < n4; i += blockDim.x) {
+        const float4 a = r4[i];
+        note(a.x);
+        note(a.y);
+        note(a.z);
+        note(a.w);
+      }
+      for (int j = (n4 << 2) + threadIdx.x; j < V; j += blockDim.x) note(d.row[j]);
+    } else {
 #pragma unroll 4
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float xv = d.x(i);
-    if (xv >= d.thresh) {
-      const float e = __expf(xv - m);
-      zl += e;
-      if (hist) atomicAdd(&Hf[lin_bin(m, xv)], e);
+      for (int j = threadIdx.x; j < V; j += blockDim.x) note(d.x(j));
     }
   }
   d.z = block_sum_b(zl, sm);
   d.inv_z = 1.f / d.z;
-  if (!want_p) return;
+  if (!want_p) {
+    dref = d;
+    return;
+  }
   float cut = -INFINITY;
   bool done = false;
   if (1.f >= top_p * d.z) {
     cut = m;  // the maximum alone already covers top_p
   } else if (hist) {
-    float z_keep = d.z;
+    double z_keep = d.z;
     bool ok = false;
-    const float c = linear_top_p(d, V, top_p, sm, ok, z_keep);
+    const float c = linear_top_p(d, V, (double)top_p * (double)d.z, sm, ok, z_keep);
     if (ok) {
       if (c > d.thresh) {
         d.thresh = c;
-        d.z = z_keep;
+        d.z = (float)z_keep;
         d.inv_z = 1.f / d.z;
       }
       done = true;
@@ -545,42 +600,57 @@ __device__ void row_stats(Dist& d, int V, int top_k, float top_p, RowSmem& sm, b
     d.z = block_sum_b(zl, sm);
     d.inv_z = 1.f / d.z;
   }
+  dref = d;
 }
 
 // Inverse-CDF draw over weights w(i) in vocabulary order: the first index
 // whose running sum exceeds u * total.  Falls back to the last positive
 // weight when rounding leaves the target past the end.
 //
-// Every thread owns a contiguous segment of the row: it sums its segment (in
-// double), a block scan places the segments, and the one thread whose
-// segment holds the target walks it.  Two passes over the row and three
-// barriers, with no serial warp-wide walk.
+// Warp w owns a contiguous segment of the row, walked in chunks of 4 * 32
+// elements (element c0 + 32k + lane in slot k of a lane, so loads are
+// conflict-free).  Pass 1: every chunk's total (a fixed
+// butterfly, so both passes round it identically) and the warp's total; a
+// block scan places the warps.  Pass 2: only the warp holding the target
+// re-walks its chunks, skipping whole chunks by their totals, and scans
+// inside the one chunk that crosses.
 template <typename W>
 __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-  const int seg = (V + (int)blockDim.x - 1) / (int)blockDim.x;
-  const int s0 = min(V, tid * seg), s1 = min(V, s0 + seg);
-  double part = 0.0;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int seg = (V + nw - 1) / nw;
+  seg = (seg + 127) & ~127;
+  const int s0 = min(V, warp * seg), s1 = min(V, s0 + seg);
+  auto chunk = [&](int c0, float (&v)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = c0 + 32 * k + lane;
+      v[k] = i < s1 ? w(i) : 0.f;
+    }
+  };
+  auto chunk_total = [&](const float (&v)[4]) {
+    float t = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+  };
+  double wtot = 0.0;
   int last = -1;
-  for (int i = s0; i < s1; ++i) {
-    const float v = w(i);
-    part += (double)v;
-    if (v > 0.f) last = i;
-  }
-  // block exclusive scan of the segment sums (lanes, then warps)
-  double inc = part;
+  for (int c0 = s0; c0 < s1; c0 += 128) {
+    float v[4];
+    chunk(c0, v);
+    wtot += (double)chunk_total(v);
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += t;
+    for (int k = 0; k < 4; ++k)
+      if (v[k] > 0.f) last = max(last, c0 + 32 * k + lane);
   }
-  int lp = last;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+  for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
   __syncthreads();  // earlier users of red_* are done
-  if (lane == 31) sm.red_d[warp] = inc;
-  if (lane == 0) sm.red_i[warp] = lp;
-  if (tid == 0) sm.red_i[40] = -1;
+  if (lane == 0) {
+    sm.red_d[warp] = wtot;
+    sm.red_i[warp] = last;
+  }
+  if (threadIdx.x == 0) sm.red_i[40] = -1;
   __syncthreads();
   double before = 0.0, total = 0.0;
   int glast = -1;
@@ -590,23 +660,41 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
     total += t;
     glast = max(glast, sm.red_i[k]);
   }
-  // Segment t covers [E_t, E_t+1) with both ends computed the same way by
-  // the two threads that share them, so exactly one segment claims a target.
-  const double up = __shfl_up_sync(0xffffffffu, inc, 1);
-  const double e0 = before + (lane == 0 ? 0.0 : up), e1 = before + inc;
   const double target = (double)u * total;
-  if (part > 0.0 && e0 <= target && target < e1) {
-    double run = e0;
-    int found = last;  // rounding inside the segment: its last positive weight
-    for (int i = s0; i < s1; ++i) {
-      const float v = w(i);
-      run += (double)v;
-      if (v > 0.f && run > target) {
-        found = i;
-        break;
+  if (wtot > 0.0 && before <= target && target < before + wtot) {
+    double run = before;
+    int found = last;  // rounding: the segment's last positive weight
+    for (int c0 = s0; c0 < s1; c0 += 128) {
+      float v[4];
+      chunk(c0, v);
+      const float t = chunk_total(v);
+      if (run + (double)t <= target) {
+        run += (double)t;
+        continue;
       }
+      // crossing chunk: slot by slot, an inclusive lane scan of each
+      int hit = -1, lp = -1;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float incl = v[k];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const unsigned hb =
+            __ballot_sync(0xffffffffu, v[k] > 0.f && run + (double)incl > target);
+        if (v[k] > 0.f) lp = c0 + 32 * k + lane;
+        if (hit < 0 && hb) hit = c0 + 32 * k + (__ffs(hb) - 1);
+        run += (double)__shfl_sync(0xffffffffu, incl, 31);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+      // rounding inside the chunk: its last positive weight
+      found = hit >= 0 ? hit : (lp >= 0 ? lp : found);
+      break;
     }
-    sm.red_i[40] = found;
+    if (lane == 0) sm.red_i[40] = found;
   }
   __syncthreads();
   int res = sm.red_i[40];
@@ -614,6 +702,12 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
   if (res < 0) res = 0;
   __syncthreads();
   return res;
+}
+
+// Histogram area (32-bit words): per-warp radix histograms or the linear
+// bins and candidate keys, whichever is larger.
+__host__ __device__ constexpr int hist_words(int nw) {
+  return nw * kHistBins > kLinWords ? nw * kHistBins : kLinWords;
 }
 
 __device__ void setup_smem(RowSmem& sm, int V, bool stage) {
@@ -627,14 +721,14 @@ __device__ void setup_smem(RowSmem& sm, int V, bool stage) {
   sm.red_i = reinterpret_cast<int*>(p);
   p += 64 * sizeof(int);
   sm.hist = reinterpret_cast<uint32_t*>(p);
-  p += (size_t)nw * kHistBins * sizeof(uint32_t);
+  p += (size_t)hist_words(nw) * sizeof(uint32_t);
   sm.stage = stage ? reinterpret_cast<float*>(p) : nullptr;
   (void)V;
 }
 
 size_t smem_bytes(int threads, int V, bool stage) {
   size_t b = 64 * sizeof(double) + 64 * sizeof(float) + 64 * sizeof(int) +
-             (size_t)(threads / 32) * kHistBins * sizeof(uint32_t);
+             (size_t)hist_words(threads / 32) * sizeof(uint32_t);
   if (stage) b += (size_t)V * sizeof(float);
   return b;
 }
@@ -718,7 +812,7 @@ __device__ bool load_logits(Dist& d, const float* row, int V, float temp, RowSme
 }
 
 // ---- K8: one draw per row ----------------------------------------------------
-__global__ void __launch_bounds__(512) sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
+__global__ void __launch_bounds__(512, 1) sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
                                    const ms_sampling_params* __restrict__ params,
                                    const int32_t* __restrict__ pidx, uint32_t lane_id,
                                    int32_t* __restrict__ tokens, float* __restrict__ probs,
@@ -749,7 +843,8 @@ __global__ void __launch_bounds__(512) sample_rows_kernel(const float* __restric
     const bool have_max = load_logits(d, row, V, P.temperature, sm);
     row_stats(d, V, P.top_k, P.top_p < 1.f ? P.top_p : 1.f, sm, have_max);
     const float u = philox_uniform(P.seed, P.step, lane_id);
-    token = inverse_cdf([&](int i) { return d.weight(i); }, V, u, sm);
+    const Dist dv = d;
+    token = inverse_cdf([dv](int i) { return dv.weight(i); }, V, u, sm);
   }
   if (threadIdx.x == 0) {
     tokens[r] = token;
@@ -781,7 +876,7 @@ struct AcceptArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(512) spec_accept_kernel(AcceptArgs a, int stage) {
+__global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int stage) {
   RowSmem sm;
   setup_smem(sm, a.V, stage != 0);
   const int b = blockIdx.x;
@@ -878,15 +973,19 @@ __global__ void __launch_bounds__(512) spec_accept_kernel(AcceptArgs a, int stag
     }
     // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0.
     float part = 0.f;
+    {
+      const Dist pv = p, qv = q;
 #pragma unroll 4
-    for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(p.prob(j) - q.prob(j), 0.f);
+      for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(pv.prob(j) - qv.prob(j), 0.f);
+    }
     const float total = block_sum_b(part, sm);
     const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
     int tok;
+    const Dist pv = p, qv = q;
     if (total <= 1e-9f) {
-      tok = inverse_cdf([&](int j) { return p.prob(j); }, V, u2, sm);
+      tok = inverse_cdf([pv](int j) { return pv.prob(j); }, V, u2, sm);
     } else {
-      tok = inverse_cdf([&](int j) { return fmaxf(p.prob(j) - q.prob(j), 0.f); }, V, u2, sm);
+      tok = inverse_cdf([pv, qv](int j) { return fmaxf(pv.prob(j) - qv.prob(j), 0.f); }, V, u2, sm);
     }
     if (threadIdx.x == 0) {
       out[i] = tok;
@@ -898,7 +997,8 @@ __global__ void __launch_bounds__(512) spec_accept_kernel(AcceptArgs a, int stag
   Dist p;
   target_dist(G, p);
   const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
-  const int tok = inverse_cdf([&](int j) { return p.weight(j); }, V, u2, sm);
+  const Dist pv = p;
+  const int tok = inverse_cdf([pv](int j) { return pv.weight(j); }, V, u2, sm);
   if (threadIdx.x == 0) {
     out[G] = tok;
     a.out_nacc[b] = G;
