@@ -609,11 +609,10 @@ __device__ void row_stats(Dist& dref, int V, int top_k, float top_p, RowSmem& sm
 //
 // Warp w owns a contiguous segment of the row, walked in chunks of 4 * 32
 // elements (element c0 + 32k + lane in slot k of a lane, so loads are
-// conflict-free).  Pass 1: every chunk's total (a fixed
-// butterfly, so both passes round it identically) and the warp's total; a
-// block scan places the warps.  Pass 2: only the warp holding the target
-// re-walks its chunks, skipping whole chunks by their totals, and scans
-// inside the one chunk that crosses.
+// conflict-free).  Pass 1: each lane sums its elements, one butterfly gives
+// the warp's total, and a block scan places the warps.  Pass 2: only the
+// warp holding the target re-walks its segment, skipping whole chunks by
+// their totals, and scans inside the one chunk that crosses.
 template <typename W>
 __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -627,22 +626,24 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
       v[k] = i < s1 ? w(i) : 0.f;
     }
   };
-  auto chunk_total = [&](const float (&v)[4]) {
-    float t = (v[0] + v[1]) + (v[2] + v[3]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-    return t;
-  };
-  double wtot = 0.0;
+  // pass 1: lane sums (four independent chunks at a time), one butterfly
+  float lsum = 0.f;
   int last = -1;
-  for (int c0 = s0; c0 < s1; c0 += 128) {
-    float v[4];
-    chunk(c0, v);
-    wtot += (double)chunk_total(v);
+  for (int c0 = s0; c0 < s1; c0 += 4 * 128) {
+    float v[4][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-      if (v[k] > 0.f) last = max(last, c0 + 32 * k + lane);
+    for (int q = 0; q < 4; ++q) chunk(c0 + 128 * q, v[q]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      lsum += (v[q][0] + v[q][1]) + (v[q][2] + v[q][3]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (v[q][k] > 0.f) last = max(last, c0 + 128 * q + 32 * k + lane);
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+  const double wtot = (double)lsum;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
   __syncthreads();  // earlier users of red_* are done
@@ -662,37 +663,52 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
   }
   const double target = (double)u * total;
   if (wtot > 0.0 && before <= target && target < before + wtot) {
+    // pass 2 (the target's warp): chunk totals four at a time, skip whole
+    // chunks, scan inside the one that crosses
     double run = before;
     int found = last;  // rounding: the segment's last positive weight
-    for (int c0 = s0; c0 < s1; c0 += 128) {
-      float v[4];
-      chunk(c0, v);
-      const float t = chunk_total(v);
-      if (run + (double)t <= target) {
-        run += (double)t;
-        continue;
+    bool done = false;
+    for (int c0 = s0; c0 < s1 && !done; c0 += 4 * 128) {
+      float v[4][4], t[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        chunk(c0 + 128 * q, v[q]);
+        t[q] = (v[q][0] + v[q][1]) + (v[q][2] + v[q][3]);
       }
-      // crossing chunk: slot by slot, an inclusive lane scan of each
-      int hit = -1, lp = -1;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float incl = v[k];
+      for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
+        for (int q = 0; q < 4; ++q) t[q] += __shfl_xor_sync(0xffffffffu, t[q], o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (done) break;
+        if (run + (double)t[q] <= target) {
+          run += (double)t[q];
+          continue;
         }
-        const unsigned hb =
-            __ballot_sync(0xffffffffu, v[k] > 0.f && run + (double)incl > target);
-        if (v[k] > 0.f) lp = c0 + 32 * k + lane;
-        if (hit < 0 && hb) hit = c0 + 32 * k + (__ffs(hb) - 1);
-        run += (double)__shfl_sync(0xffffffffu, incl, 31);
-      }
+        // crossing chunk: slot by slot, an inclusive lane scan of each
+        const int cq = c0 + 128 * q;
+        int hit = -1, lp = -1;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
-      // rounding inside the chunk: its last positive weight
-      found = hit >= 0 ? hit : (lp >= 0 ? lp : found);
-      break;
+        for (int k = 0; k < 4; ++k) {
+          float incl = v[q][k];
+#pragma unroll
+          for (int o = 1; o < 32; o <<= 1) {
+            const float y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+          }
+          const unsigned hb =
+              __ballot_sync(0xffffffffu, v[q][k] > 0.f && run + (double)incl > target);
+          if (v[q][k] > 0.f) lp = cq + 32 * k + lane;
+          if (hit < 0 && hb) hit = cq + 32 * k + (__ffs(hb) - 1);
+          run += (double)__shfl_sync(0xffffffffu, incl, 31);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lp = max(lp, __shfl_xor_sync(0xffffffffu, lp, o));
+        // rounding inside the chunk: its last positive weight
+        found = hit >= 0 ? hit : (lp >= 0 ? lp : found);
+        done = true;
+      }
     }
     if (lane == 0) sm.red_i[40] = found;
   }
