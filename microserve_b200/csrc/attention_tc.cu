@@ -348,12 +348,15 @@ __global__ void attn_combine_kernel(AttnArgs a) {
 template <int DH>
 int launch(AttnArgs& a, int n_seqs, cudaStream_t s) {
   using Cfg = AttnCfg<DH>;
-  static bool attr = false;
-  if (!attr) {
+  // the shared-memory opt-in is per device
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << (dev & 63)))) {
     const cudaError_t e = cudaFuncSetAttribute(
         attn_tc_kernel<DH>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "attn_tc: smem attribute: %s", cudaGetErrorString(e));
-    attr = true;
+    attr_set |= 1ull << (dev & 63);
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
   attn_tc_kernel<DH><<<grid, kThreads, Cfg::kSmem, s>>>(a);

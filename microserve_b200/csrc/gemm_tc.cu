@@ -482,12 +482,15 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
   MS_TRY(tensor_map(B, N, K, BN, &tb));
   using Cfg = TileCfg<BN>;
   auto kern = gemm_tc_kernel<BN, EPI, TC>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // the shared-memory opt-in is per device
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << (dev & 63)))) {
     const cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "gemm_tc: smem attribute: %s", cudaGetErrorString(e));
-    attr_set = true;
+    attr_set |= 1ull << (dev & 63);
   }
   const int tiles = ((M + BM - 1) / BM) * (N / BN);
   const int kiters = (K + BK - 1) / BK;
