@@ -171,6 +171,79 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ 
   }
 }
 
+// Vectorised rope_kv for bf16 with d_head % 16 == 0: a task is 8 rotation
+// pairs of one q/k head (two 16-byte loads, cos/sin as float4) or 8 values of
+// one v head; kRopeTokens tokens per CTA.  Same arithmetic as rope_kv_kernel.
+constexpr int kRopeTokens = 4;
+__global__ void __launch_bounds__(128)
+    rope_kv_vec_kernel(__nv_bfloat16* __restrict__ qkv, const int32_t* __restrict__ positions,
+                       const int32_t* __restrict__ slots, const float* __restrict__ cos_t,
+                       const float* __restrict__ sin_t, int max_pos, int n_tokens, int hq, int hkv,
+                       int dh, int bs, int num_blocks, __nv_bfloat16* __restrict__ kpool,
+                       __nv_bfloat16* __restrict__ vpool, int* __restrict__ err) {
+  const int width = (hq + 2 * hkv) * dh;
+  const int half = dh / 2, hc = half / 8, vc = dh / 8;
+  const int n_rot = (hq + hkv) * hc, per_token = n_rot + hkv * vc;
+  for (int idx = threadIdx.x; idx < kRopeTokens * per_token; idx += blockDim.x) {
+    const int tl = idx / per_token, task = idx - tl * per_token;
+    const int t = blockIdx.x * kRopeTokens + tl;
+    if (t >= n_tokens) break;
+    __nv_bfloat16* row = qkv + (int64_t)t * width;
+    const int slot = slots[t];
+    if (task < n_rot) {
+      int pos = positions[t];
+      if (pos < 0 || pos >= max_pos) {
+        raise_device_error(err, kErrPosition);
+        pos = 0;
+      }
+      const int h = task / hc, i0 = (task - h * hc) * 8;
+      __nv_bfloat16* hp = row + h * dh;
+      const uint4 a = *reinterpret_cast<const uint4*>(hp + i0);
+      const uint4 b = *reinterpret_cast<const uint4*>(hp + half + i0);
+      const float4* c4 = reinterpret_cast<const float4*>(cos_t + (int64_t)pos * half + i0);
+      const float4* s4 = reinterpret_cast<const float4*>(sin_t + (int64_t)pos * half + i0);
+      const float4 ca = c4[0], cb = c4[1], sa = s4[0], sb = s4[1];
+      const float c[8] = {ca.x, ca.y, ca.z, ca.w, cb.x, cb.y, cb.z, cb.w};
+      const float sn[8] = {sa.x, sa.y, sa.z, sa.w, sb.x, sb.y, sb.z, sb.w};
+      const __nv_bfloat162* x1 = reinterpret_cast<const __nv_bfloat162*>(&a);
+      const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&b);
+      uint4 o1, o2;
+      __nv_bfloat162* r1 = reinterpret_cast<__nv_bfloat162*>(&o1);
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&o2);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 p = __bfloat1622float2(x1[j]), q = __bfloat1622float2(x2[j]);
+        const int k0 = 2 * j, k1 = 2 * j + 1;
+        r1[j] = __floats2bfloat162_rn(p.x * c[k0] - q.x * sn[k0], p.y * c[k1] - q.y * sn[k1]);
+        r2[j] = __floats2bfloat162_rn(q.x * c[k0] + p.x * sn[k0], q.y * c[k1] + p.y * sn[k1]);
+      }
+      if (h < hq) {
+        *reinterpret_cast<uint4*>(hp + i0) = o1;
+        *reinterpret_cast<uint4*>(hp + half + i0) = o2;
+      } else {
+        bool ok;
+        const int64_t o = pool_offset(slot, h - hq, i0, bs, hkv, dh, num_blocks, ok);
+        if (!ok) {
+          raise_device_error(err, kErrSlot);
+          continue;
+        }
+        *reinterpret_cast<uint4*>(kpool + o) = o1;
+        *reinterpret_cast<uint4*>(kpool + o + half) = o2;
+      }
+    } else {
+      const int vt = task - n_rot, g = vt / vc, d0 = (vt - g * vc) * 8;
+      bool ok;
+      const int64_t o = pool_offset(slot, g, d0, bs, hkv, dh, num_blocks, ok);
+      if (!ok) {
+        raise_device_error(err, kErrSlot);
+        continue;
+      }
+      *reinterpret_cast<uint4*>(vpool + o) =
+          *reinterpret_cast<const uint4*>(row + (hq + hkv) * dh + g * dh + d0);
+    }
+  }
+}
+
 template <typename T>
 __global__ void kv_write_kernel(const int32_t* __restrict__ slots, int n_tokens,
                                 const float* __restrict__ keys, const float* __restrict__ values,
@@ -277,7 +350,17 @@ int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, con
         static_cast<float*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
         cache.block_size, cache.num_blocks, static_cast<float*>(cache.k_pool[layer]),
         static_cast<float*>(cache.v_pool[layer]), device_error_word());
-  else if (dtype == MS_DTYPE_BF16)
+  else if (dtype == MS_DTYPE_BF16 && dh % 16 == 0 &&
+           (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(cos_t) & 15) == 0 &&
+           (reinterpret_cast<uintptr_t>(sin_t) & 15) == 0) {
+    rope_kv_vec_kernel<<<ceil_div(n_tokens, kRopeTokens), threads, 0, s>>>(
+        static_cast<__nv_bfloat16*>(qkv), positions, slots, cos_t, sin_t, max_pos, n_tokens, hq,
+        hkv, dh, cache.block_size, cache.num_blocks,
+        static_cast<__nv_bfloat16*>(cache.k_pool[layer]),
+        static_cast<__nv_bfloat16*>(cache.v_pool[layer]), device_error_word());
+    return check_launch("rope_kv_vec_kernel");
+  } else if (dtype == MS_DTYPE_BF16)
     rope_kv_kernel<__nv_bfloat16><<<n_tokens, threads, 0, s>>>(
         static_cast<__nv_bfloat16*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
         cache.block_size, cache.num_blocks, static_cast<__nv_bfloat16*>(cache.k_pool[layer]),
