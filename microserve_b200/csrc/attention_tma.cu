@@ -127,6 +127,12 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// 2^x by the SFU's ex2.approx (ftz): 2^-inf = +0; arguments here are <= 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -362,17 +368,14 @@ __global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
           mma_bf16(sc[nt + 1], a0, a1, a2, a3, b2, b3);
         }
       }
+      // Raw scores: the scale is positive, so it commutes with the max and
+      // folds into the exponent's FMA; masked scores are -inf.
       float mx_a = -INFINITY, mx_b = -INFINITY;
       if (jlo + KW <= jfree) {
 #pragma unroll
         for (int nt = 0; nt < KW / 8; ++nt) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            sc[nt][e] *= a.scale_log2;
-            sc[nt][2 + e] *= a.scale_log2;
-            mx_a = fmaxf(mx_a, sc[nt][e]);
-            mx_b = fmaxf(mx_b, sc[nt][2 + e]);
-          }
+          mx_a = fmaxf(mx_a, fmaxf(sc[nt][0], sc[nt][1]));
+          mx_b = fmaxf(mx_b, fmaxf(sc[nt][2], sc[nt][3]));
         }
       } else {
         const int jbase = jlo + 2 * (lane & 3);
@@ -382,8 +385,8 @@ __global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
           for (int e = 0; e < 2; ++e) {
             const int j = jbase + nt * 8 + e;
             const bool va = j < kend && j <= pos_a, vb = j < kend && j <= pos_b;
-            sc[nt][e] = va ? sc[nt][e] * a.scale_log2 : -INFINITY;
-            sc[nt][2 + e] = vb ? sc[nt][2 + e] * a.scale_log2 : -INFINITY;
+            sc[nt][e] = va ? sc[nt][e] : -INFINITY;
+            sc[nt][2 + e] = vb ? sc[nt][2 + e] : -INFINITY;
             mx_a = fmaxf(mx_a, sc[nt][e]);
             mx_b = fmaxf(mx_b, sc[nt][2 + e]);
           }
@@ -394,32 +397,37 @@ __global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
         mx_a = fmaxf(mx_a, __shfl_xor_sync(0xffffffffu, mx_a, o_));
         mx_b = fmaxf(mx_b, __shfl_xor_sync(0xffffffffu, mx_b, o_));
       }
-      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
-      const float al_a = mn_a == -INFINITY ? 1.f : exp2f(m_a - mn_a);
-      const float al_b = mn_b == -INFINITY ? 1.f : exp2f(m_b - mn_b);
+      const float mn_a = fmaxf(m_a, mx_a * a.scale_log2), mn_b = fmaxf(m_b, mx_b * a.scale_log2);
+      const bool grow_a = mn_a > m_a, grow_b = mn_b > m_b;
+      const float al_a = grow_a ? (m_a == -INFINITY ? 0.f : fast_exp2(m_a - mn_a)) : 1.f;
+      const float al_b = grow_b ? (m_b == -INFINITY ? 0.f : fast_exp2(m_b - mn_b)) : 1.f;
       const float sub_a = mn_a == -INFINITY ? 0.f : mn_a;
       const float sub_b = mn_b == -INFINITY ? 0.f : mn_b;
-      float ps_a = 0.f, ps_b = 0.f;
+      float ps_a0 = 0.f, ps_a1 = 0.f, ps_b0 = 0.f, ps_b1 = 0.f;
 #pragma unroll
       for (int nt = 0; nt < KW / 8; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          sc[nt][e] = exp2f(sc[nt][e] - sub_a);
-          sc[nt][2 + e] = exp2f(sc[nt][2 + e] - sub_b);
-          ps_a += sc[nt][e];
-          ps_b += sc[nt][2 + e];
-        }
+        sc[nt][0] = fast_exp2(fmaf(sc[nt][0], a.scale_log2, -sub_a));
+        sc[nt][1] = fast_exp2(fmaf(sc[nt][1], a.scale_log2, -sub_a));
+        sc[nt][2] = fast_exp2(fmaf(sc[nt][2], a.scale_log2, -sub_b));
+        sc[nt][3] = fast_exp2(fmaf(sc[nt][3], a.scale_log2, -sub_b));
+        ps_a0 += sc[nt][0];
+        ps_a1 += sc[nt][1];
+        ps_b0 += sc[nt][2];
+        ps_b1 += sc[nt][3];
       }
-      l_a = l_a * al_a + ps_a;
-      l_b = l_b * al_b + ps_b;
+      l_a = l_a * al_a + (ps_a0 + ps_a1);
+      l_b = l_b * al_b + (ps_b0 + ps_b1);
       m_a = mn_a;
       m_b = mn_b;
+      // O is rescaled only when a row's maximum grew (exact: alpha is 1 else)
+      if (__any_sync(0xffffffffu, grow_a || grow_b)) {
 #pragma unroll
-      for (int i = 0; i < NT; ++i) {
-        o[i][0] *= al_a;
-        o[i][1] *= al_a;
-        o[i][2] *= al_b;
-        o[i][3] *= al_b;
+        for (int i = 0; i < NT; ++i) {
+          o[i][0] *= al_a;
+          o[i][1] *= al_a;
+          o[i][2] *= al_b;
+          o[i][3] *= al_b;
+        }
       }
 #pragma unroll
       for (int kt = 0; kt < KW / 16; ++kt) {
