@@ -166,7 +166,7 @@ def run_gpu(args: argparse.Namespace) -> None:
     B = args.requests
     rng_seed = args.seed * 1000 + info.rank
     ctx = contexts(B, args.ctx_min, args.ctx_max, rng_seed)
-    rounds_total = args.warmup + args.steps
+    rounds_total = args.warmup + args.steps + 2  # + the attention-rate rounds
     per_req_blocks = (ctx + rounds_total * (GAMMA + 1) + 2 * BLOCK) // BLOCK + 1
     nblocks = int(per_req_blocks.sum()) + 64
     ccfg = CacheConfig(BLOCK, nblocks, "bfloat16")
@@ -207,6 +207,7 @@ def run_gpu(args: argparse.Namespace) -> None:
         one_round()
     acc0, prop0 = dec.num_accepted, dec.num_proposed
     dec.round_events = []
+    dec.verify_events = []
     launches0 = _lib.launch_count()
     clocks = ClockSampler(info.local_rank) if info.rank == 0 else None
     distributed.barrier()
@@ -234,6 +235,24 @@ def run_gpu(args: argparse.Namespace) -> None:
     clk = clocks.stop() if clocks else None
     e2e_ms = start.elapsed_time(end)
     dev_ms = sum(a.elapsed_time(b) for a, b in dec.round_events)
+    verify_us = 1e3 * sum(a.elapsed_time(b) for a, b in dec.verify_events) / max(
+        1, len(dec.verify_events))
+    dec.round_events = dec.verify_events = None
+    # Paged-attention HBM rate, from extra rounds outside the timed region:
+    # attention-class kernel time (CUDA events on the stream) against the K/V
+    # bytes the round's passes read (real context lengths).
+    attn_rounds = max(1, min(2, args.steps))
+    kv_bytes = 0.0
+    _lib.call("ms_profile_start", 2)
+    for _ in range(attn_rounds):
+        one_round()
+        sh = dec.last_round_shape
+        kv_bytes += sh["kv_tokens_verify"] * tcfg.n_layers * 2 * tcfg.kv_heads * tcfg.d_head * 2
+        kv_bytes += sh["kv_tokens_draft"] * dcfg.n_layers * 2 * dcfg.kv_heads * dcfg.d_head * 2
+    torch.cuda.synchronize()
+    attn_ms = _c_double()
+    attn_n = _c_int64()
+    _lib.call("ms_profile_stop", _byref(attn_ms), _byref(attn_n))
     launches = _lib.launch_count() - launches0
     counters = {"emitted": emitted, "accepted": dec.num_accepted - acc0,
                 "proposed": dec.num_proposed - prop0}
@@ -269,7 +288,20 @@ def run_gpu(args: argparse.Namespace) -> None:
         },
         "acceptance_rate": tot["accepted"] / max(1, tot["proposed"]),
         "emitted_tokens": tot["emitted"],
-        "verify_step_us": None,
+        "verify_step_us": verify_us,
+        "attention": {
+            "kernel": "paged attention (verify and draft passes)",
+            "bound": "hbm",
+            "achieved": kv_bytes / (attn_ms.value / 1e3) / 1e9 if attn_ms.value > 0 else 0.0,
+            "peak": peaks["hbm_gbs"],
+            "unit": "GB/s",
+            "frac": (kv_bytes / (attn_ms.value / 1e3) / 1e9 / peaks["hbm_gbs"]
+                     if attn_ms.value > 0 else 0.0),
+            "kv_bytes_per_round": kv_bytes / attn_rounds,
+            "launches": int(attn_n.value),
+            "device_ms": attn_ms.value,
+            "rounds": attn_rounds,
+        },
         "e2e": {
             "value": tot["emitted"] / e2e_s_max,
             "unit": "tok/s",

@@ -169,6 +169,8 @@ class SpeculativeDecoder:
         # list, each round appends a (start, end) CUDA event pair around its
         # kernels; the last round's shapes and copy sizes are kept below.
         self.round_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] | None = None
+        # and when ``verify_events`` is a list, a pair around each verify pass
+        self.verify_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] | None = None
         self.last_round_shape: dict[str, int] = {}
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
@@ -288,6 +290,8 @@ class SpeculativeDecoder:
             "ctx_j": [int(c.max()) for c in ctx_j],
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
             "n_tok": params_n_tok,
+            "kv_verify": int(ctxv.sum()),
+            "kv_draft": int(ctx0.sum()) + sum(int(c.sum()) for c in ctx_j),
         }
 
     def _launch(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
@@ -326,7 +330,10 @@ class SpeculativeDecoder:
         k += 1
         scat = v[k : k + G]
         self.last_round_shape = {"B": B, "T0": int(plan["T0"]), "Tv": int(plan["Tv"]),  # type: ignore[arg-type]
-                                 "gamma": G}
+                                 "gamma": G,
+                                 # keys each pass's attention reads, summed over requests
+                                 "kv_tokens_verify": int(plan["kv_verify"]),  # type: ignore[arg-type]
+                                 "kv_tokens_draft": int(plan["kv_draft"])}  # type: ignore[arg-type]
         self.last_h2d_bytes = int(plan["blob"].nbytes)  # type: ignore[union-attr]
         self.last_d2h_bytes = B * (G + 2) * 4
         ev = None
@@ -343,8 +350,15 @@ class SpeculativeDecoder:
                 buf.proposals[j].data_ptr(), None, buf.dstats[j].data_ptr(),
                 bv.input_ids.data_ptr(), scat[j].data_ptr(), stream,
             )
+        vev = None
+        if self.verify_events is not None:
+            vev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            vev[0].record()
         self.target.forward_paged(bv, target_cache, logit_rows=rowsv, out=buf.vlogits,
                                   out_row_stride=V)
+        if vev is not None and self.verify_events is not None:
+            vev[1].record()
+            self.verify_events.append(vev)
         _lib.call(
             "ms_spec_accept", buf.vlogits.data_ptr(), V, buf.dlogits.data_ptr(), V,
             buf.dstats.data_ptr(), 0, buf.proposals.data_ptr(), params.data_ptr(), B, G, V,
