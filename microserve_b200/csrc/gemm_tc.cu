@@ -534,9 +534,17 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
     return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
   if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
   if (epi == kEpiResidual) {
-    // In place (C += A B^T): stream-K with reductions into C.
+    // In place (C += A B^T): stream-K with reductions into C, unless there is
+    // at least one 256-wide tile per SM and A + B overflow L2.  Stream-K
+    // puts the CTAs at scattered k offsets, so the whole of A and B is live
+    // at once: at M 1536, K 14336 (160 MB) that re-read DRAM ~7 times, while
+    // whole tiles dealt round-robin keep the CTAs near the same k-step.
     const bool in_place = static_cast<const void*>(R) == C;
-    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, in_place, s);
+    const int tiles256 = ((M + BM - 1) / BM) * (N / 256);
+    const double ab_bytes = 2.0 * ((double)M + (double)N) * (double)K;
+    const bool stream_k =
+        in_place && (N % 256 != 0 || tiles256 < kNumSMs || ab_bytes <= 64.0 * (1 << 20));
+    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s);
   }
   if (c_dtype == MS_DTYPE_F32) return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
   return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
