@@ -64,6 +64,11 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
+    ap.add_argument("--micro", choices=["gemm8b", "attention"], default=None,
+                    help="time one kernel family alone (1 GPU) instead of the speculative round")
+    ap.add_argument("--only", default=None, help="--micro gemm8b: one shape (qkv, o_proj, ...)")
+    ap.add_argument("--qlen", type=int, default=5, help="--micro attention: query tokens per sequence")
+    ap.add_argument("--iters", type=int, default=20, help="--micro: timed launches")
     return ap.parse_args()
 
 
@@ -462,9 +467,103 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+# -- kernel micro-benchmarks (one GPU; not the headline metric) --------------------------
+GEMM8B = [  # (name, N, K, epilogue, output dtype) at M = 256 requests x 6 tokens
+    ("qkv", 6144, 4096, 0, "bf16"), ("o_proj", 4096, 4096, 1, "f32"),
+    ("gate_up", 28672, 4096, 2, "bf16"), ("down", 4096, 14336, 1, "f32"),
+    ("lm_head", 128256, 4096, 0, "f32"),
+]
+
+
+def _time_launches(call, iters: int) -> float:
+    """Mean microseconds per launch over `iters` back-to-back launches (CUDA events)."""
+    import torch
+
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters * 1e3
+
+
+def run_micro(args: argparse.Namespace) -> None:
+    import ctypes
+
+    import torch
+
+    from microserve_b200 import _lib
+
+    _lib.load()
+    peaks = _peaks()
+    g = torch.Generator(device="cuda").manual_seed(args.seed)
+    if args.micro == "gemm8b":
+        M = 1536
+        for name, N, K, epi, cd in GEMM8B:
+            if args.only and name != args.only:
+                continue
+            A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).bfloat16()
+            B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+            C = torch.zeros(M, N // 2 if epi == 2 else N, device="cuda",
+                            dtype=torch.float32 if cd == "f32" else torch.bfloat16)
+            R = C if epi == 1 else None
+            cdt = _lib.DTYPE_F32 if cd == "f32" else _lib.DTYPE_BF16
+
+            def call() -> None:
+                _lib.call("ms_gemm", A.data_ptr(), B.data_ptr(), C.data_ptr(), _lib.ptr(R), M, N,
+                          K, 0, _lib.DTYPE_BF16, cdt, epi, _lib.stream_ptr())
+
+            us = _time_launches(call, args.iters)
+            tf = 2.0 * M * N * K / us / 1e6
+            print(json.dumps({"micro": "gemm8b", "gemm": name, "M": M, "N": N, "K": K, "us": us,
+                              "tflops": tf, "frac_sustained": tf / peaks["bf16_sustained"],
+                              "device_error": _lib.device_error()}), flush=True)
+        return
+    # attention: the config-3 verify (qlen 5) or draft (qlen 1) pass of one layer
+    from microserve_b200.batching import build_paged_batch
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import CacheConfig, ModelConfig
+
+    hq, hkv, dh, bs, nseq = TARGET["n_heads"], TARGET["n_kv_heads"], 64, BLOCK, args.requests
+    ctx = contexts(nseq, args.ctx_min, args.ctx_max, args.seed)
+    cfg = ModelConfig(vocab_size=16, n_layers=1, d_model=hq * dh, n_heads=hq, n_kv_heads=hkv,
+                      max_seq_len=4096, dtype="bfloat16")
+    cache = PagedKVCache(cfg, CacheConfig(bs, int(sum(-(-int(c) // bs) for c in ctx)) + 16,
+                                          "bfloat16"), "cuda")
+    cache.pool.normal_(generator=g)
+    pre = ctx - args.qlen
+    done = np.zeros(nseq, np.int64)
+    ids = list(range(nseq))
+    while (done < pre).any():  # interleaved block allocation
+        step = np.minimum(bs, pre - done)
+        live = [i for i in ids if step[i] > 0]
+        cache.append_many(live, step[live])
+        done += step
+    batch = build_paged_batch(cache, ids, [[1] * args.qlen for _ in ids], pre.tolist())
+    q = torch.randn(batch.n_tokens, hq * dh, device="cuda", generator=g).bfloat16()
+    out = torch.empty_like(q)
+    cb, cs = batch.c_struct(), cache.c_struct()
+
+    def call() -> None:
+        _lib.call("ms_paged_attention", q.data_ptr(), ctypes.byref(cs), 0, ctypes.byref(cb), hq,
+                  out.data_ptr(), _lib.stream_ptr())
+
+    us = _time_launches(call, args.iters)
+    kv = float(ctx.sum()) * hkv * dh * 2 * 2
+    print(json.dumps({"micro": "attention", "qlen": args.qlen, "seqs": nseq, "us": us,
+                      "kv_bytes": kv, "gbs": kv / us / 1e3, "frac_hbm": kv / us / 1e3 / peaks["hbm_gbs"],
+                      "device_error": _lib.device_error()}), flush=True)
+
+
 def main() -> None:
     args = parse()
-    if args.impl == "reference":
+    if args.micro:
+        run_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
