@@ -447,10 +447,7 @@ def run_reference(args: argparse.Namespace) -> None:
     if info_rank != 0:
         return
     target, draft, reqs = cpu_workload(args, args.cpu_requests, args.seed + 99)
-    from oracle.spec import spec_round
-
-    for _ in range(args.warmup):
-        spec_round(target, draft, GAMMA, reqs)
+    cpu_rounds(target, draft, reqs, args.warmup)  # warm-up rounds append their tokens too
     emitted, secs = cpu_rounds(target, draft, reqs, args.steps)
     value = emitted / secs
     line = {
