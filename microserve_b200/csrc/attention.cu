@@ -172,7 +172,7 @@ int attn_by_dh(const void* q, int q_stride, const ms_kv_cache& c, int layer, con
 
 int paged_attention(const void* q, int q_stride, const ms_kv_cache& c, int layer,
                     const ms_batch& bt, int hq, void* out, void* scratch, size_t scratch_bytes,
-                    cudaStream_t s) {
+                    cudaStream_t s, const int32_t* seq_order) {
   if (bt.n_seqs == 0 || bt.n_tokens == 0) return MS_OK;
   if (hq % c.n_kv_heads != 0)
     return fail(MS_ERR_INVALID, "paged_attention: n_heads %d not a multiple of n_kv_heads %d", hq,
@@ -184,7 +184,7 @@ int paged_attention(const void* q, int q_stride, const ms_kv_cache& c, int layer
     const int max_ctx = bt.max_context > 0 ? min(bt.max_context, table_bound) : table_bound;
     if (attn_tma_supported(c, hq))
       return paged_attention_tma(q, q_stride, c, layer, bt, hq, out, max_ctx, scratch,
-                                 scratch_bytes, s);
+                                 scratch_bytes, s, seq_order);
     return paged_attention_tc(q, q_stride, c, layer, bt, hq, out, max_ctx, scratch, scratch_bytes,
                               s);
   }
@@ -192,6 +192,44 @@ int paged_attention(const void* q, int q_stride, const ms_kv_cache& c, int layer
   if (c.dtype == MS_DTYPE_BF16)
     return attn_by_dh<__nv_bfloat16>(q, q_stride, c, layer, bt, hq, out, s);
   return fail(MS_ERR_UNSUPPORTED, "paged_attention: dtype %d", c.dtype);
+}
+
+namespace {
+
+constexpr int kOrderThreads = 256;
+constexpr int kOrderTile = 2048;
+
+// Rank of sequence b under (context length descending, index ascending): a
+// strict total order, so the ranks are a permutation and each order[] slot is
+// written exactly once.
+__global__ void __launch_bounds__(kOrderThreads)
+    seq_order_kernel(const int32_t* __restrict__ ctx, int n, int32_t* __restrict__ order) {
+  __shared__ int keys[kOrderTile];
+  const int b = blockIdx.x * kOrderThreads + threadIdx.x;
+  const int kb = b < n ? ctx[b] : 0;
+  int rank = 0;
+  for (int base = 0; base < n; base += kOrderTile) {
+    const int cnt = min(kOrderTile, n - base);
+    __syncthreads();
+    for (int i = threadIdx.x; i < cnt; i += kOrderThreads) keys[i] = ctx[base + i];
+    __syncthreads();
+    if (b < n) {
+      for (int i = 0; i < cnt; ++i) {
+        const int kc = keys[i];
+        rank += (kc > kb) | ((kc == kb) & (base + i < b));
+      }
+    }
+  }
+  if (b < n) order[rank] = b;
+}
+
+}  // namespace
+
+int attn_seq_order(const int32_t* context_lens, int n_seqs, int32_t* order, cudaStream_t s) {
+  if (n_seqs <= 0) return MS_OK;
+  seq_order_kernel<<<(n_seqs + kOrderThreads - 1) / kOrderThreads, kOrderThreads, 0, s>>>(
+      context_lens, n_seqs, order);
+  return check_launch("seq_order_kernel");
 }
 
 }  // namespace ms

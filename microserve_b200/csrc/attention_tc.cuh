@@ -18,6 +18,6 @@ int paged_attention_tc(const void* q, int q_stride, const ms_kv_cache& c, int la
 bool attn_tma_supported(const ms_kv_cache& c, int hq);
 int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int layer,
                         const ms_batch& bt, int hq, void* out, int max_context, void* scratch,
-                        size_t scratch_bytes, cudaStream_t s);
+                        size_t scratch_bytes, cudaStream_t s, const int32_t* seq_order);
 
 }  // namespace ms

@@ -43,12 +43,14 @@ constexpr int kErrTimeout = 5;
 constexpr int kErrRows = 6;  // a row tile wider than the launch's slice layout covers
 constexpr int kTblCap = 64;  // block-table entries staged per refill (multiple of 16)
 
-template <int DH> struct TmaCfg {
+// Default layout: 8 (dh 64) or 4 (dh 128) consumer warps, 3 or 2 ring stages,
+// 2 CTAs per SM.  A launch may pick fewer warps and stages to fit more CTAs.
+template <int DH, int NW = (DH == 64 ? 8 : 4), int NS = (DH == 64 ? 3 : 2)> struct TmaCfg {
   static constexpr int kCh = DH == 64 ? 128 : 64;   // keys per stage
-  static constexpr int kWarps = DH == 64 ? 8 : 4;   // consumer warps
+  static constexpr int kWarps = NW;                 // consumer warps
   static constexpr int kThreads = (kWarps + 1) * 32;
   static constexpr int kHalves = DH / 64;           // 128-byte column halves
-  static constexpr int kStages = DH == 64 ? 3 : 2;
+  static constexpr int kStages = NS;
   static constexpr int kTileBytes = kCh * DH * 2;   // one operand, one chunk
   static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
   static constexpr int kLdQ = DH + 8;
@@ -169,6 +171,7 @@ struct TmaArgs {
   const int32_t* context_lens;
   const int32_t* positions;
   const int32_t* tables;
+  const int32_t* seq_order;  // null: sequence b is grid column b
   int max_blocks, bs, log2_bs, num_blocks, hq, hkv, row_tiles, n_splits, split_len;
   float scale_log2;
   __nv_bfloat16* out;
@@ -177,11 +180,11 @@ struct TmaArgs {
   int* err;
 };
 
-template <int DH, int KW>
-__global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
+template <int DH, int KW, int NWARPS, int NSTAGES, int MINB>
+__global__ void __launch_bounds__(TmaCfg<DH, NWARPS, NSTAGES>::kThreads, MINB)
     attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     TmaArgs a) {
-  using Cfg = TmaCfg<DH>;
+  using Cfg = TmaCfg<DH, NWARPS, NSTAGES>;
   constexpr int S = Cfg::kStages;
   constexpr int CH = Cfg::kCh;
   constexpr int NW = Cfg::kWarps;
@@ -202,7 +205,7 @@ __global__ void __launch_bounds__(TmaCfg<DH>::kThreads, 2)
   int* tbl = reinterpret_cast<int*>(smem + S * Cfg::kStageBytes + Cfg::kQBytes + kRows * 4 + 128);
 
   const int split = blockIdx.x % a.n_splits, rt = blockIdx.x / a.n_splits;
-  const int g = blockIdx.y, b = blockIdx.z;
+  const int g = blockIdx.y, b = a.seq_order ? a.seq_order[blockIdx.z] : blockIdx.z;
   const int group = a.hq / a.hkv;
   const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
   const int nrows = qlen * group;
@@ -635,23 +638,25 @@ __global__ void attn_tma_combine_kernel(TmaArgs a, int dh) {
   }
 }
 
-template <int DH, int KW>
+template <int DH, int KW, int NW = TmaCfg<DH>::kWarps, int NS = TmaCfg<DH>::kStages, int MINB = 2>
 int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
                cudaStream_t s) {
-  using Cfg = TmaCfg<DH>;
+  using Cfg = TmaCfg<DH, NW, NS>;
+  static_assert(MINB * (Cfg::kSmem + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
   // The shared-memory opt-in is per device; remember it per device.
   static uint64_t attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set & bit)) {
-    const cudaError_t e = cudaFuncSetAttribute(
-        attn_tma_kernel<DH, KW>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
+    const cudaError_t e =
+        cudaFuncSetAttribute(attn_tma_kernel<DH, KW, NW, NS, MINB>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "attn_tma: smem attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
-  attn_tma_kernel<DH, KW><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
+  attn_tma_kernel<DH, KW, NW, NS, MINB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
   MS_TRY(check_launch("attn_tma_kernel"));
   if (a.n_splits > 1) {
     attn_tma_combine_kernel<<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a, DH);
@@ -668,6 +673,11 @@ int launch_by_rows(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int
   const int mt = (min(max_rows, kRows) + 15) / 16;
   if (mt <= 1) return launch_tma<DH, TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
   if (mt == 2) return launch_tma<DH, 2 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
+  // Three m-tiles (33-48 rows: a 5-token verify of 8 GQA heads): 3 m-tiles x 2
+  // key slices on 6 warps, 2 stages, so 3 CTAs share an SM (no idle warps).
+  if constexpr (DH == 64) {
+    if (mt == 3) return launch_tma<DH, TmaCfg<DH>::kCh / 2, 6, 3, 2>(a, km, vm, n_seqs, s);
+  }
   return launch_tma<DH, 4 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
 }
 
@@ -683,7 +693,7 @@ bool attn_tma_supported(const ms_kv_cache& c, int hq) {
 
 int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int layer,
                         const ms_batch& bt, int hq, void* out, int max_context, void* scratch,
-                        size_t scratch_bytes, cudaStream_t s) {
+                        size_t scratch_bytes, cudaStream_t s, const int32_t* seq_order) {
   if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out)) & 15 || q_stride % 8)
     return fail(MS_ERR_INVALID, "attn_tma: q/out must be 16-byte aligned");
   TmaArgs a{};
@@ -693,6 +703,7 @@ int paged_attention_tma(const void* q, int q_stride, const ms_kv_cache& c, int l
   a.context_lens = bt.context_lens;
   a.positions = bt.positions;
   a.tables = bt.block_tables;
+  a.seq_order = seq_order;
   a.max_blocks = bt.max_blocks;
   a.bs = c.block_size;
   a.log2_bs = __builtin_ctz((unsigned)c.block_size);

@@ -20,6 +20,7 @@ struct Workspace {
   void* attn;    // (T, hq dh)
   void* h;       // (T, d_ff)
   void* xl;      // (R, d) final-normed logit rows
+  int32_t* order;  // (T) attention schedule order of the sequences
   size_t bytes;
 };
 
@@ -39,6 +40,7 @@ Workspace carve(const ms_model& m, int T, int R, unsigned char* base) {
   w.attn = take((size_t)T * m.n_heads * m.d_head * es);
   w.h = take((size_t)T * m.d_ff * es);
   w.xl = take((size_t)(R > 0 ? R : 1) * m.d_model * es);
+  w.order = reinterpret_cast<int32_t*>(take((size_t)(T > 0 ? T : 1) * 4));
   w.bytes = off;
   return w;
 }
@@ -101,6 +103,12 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
   void* attn_scratch = static_cast<unsigned char*>(workspace) + w.bytes;
   const size_t attn_scratch_bytes = workspace_bytes - w.bytes;
 
+  // Longest sequences first in every layer's attention grid (one sort per pass).
+  const int32_t* order = nullptr;
+  if (bt.n_seqs > 1 && bt.n_seqs <= T) {
+    MS_TRY(attn_seq_order(bt.context_lens, bt.n_seqs, w.order, s));
+    order = w.order;
+  }
   MS_TRY(embed_rmsnorm(m.embed, bt.input_ids, T, m.vocab_size, d, m.attn_norm[0], m.norm_eps, w.x,
                        w.xn, dt, s));
   for (int l = 0; l < m.n_layers; ++l) {
@@ -109,7 +117,7 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
                          T, hq, hkv, dh, c, l, dt, s));
     // q occupies the first hq*dh columns of each qkv row.
     MS_TRY(paged_attention(w.qkv, qkv_w, c, l, bt, hq, w.attn, attn_scratch, attn_scratch_bytes,
-                           s));
+                           s, order));
     MS_TRY(gemm_dispatch(w.attn, m.w_o[l], w.x, w.x, T, d, hq * dh, 0, dt, MS_DTYPE_F32,
                          kEpiResidual, s));
     MS_TRY(rmsnorm(w.x, m.ffn_norm[l], w.xn, nullptr, T, d, m.norm_eps, dt, s));
