@@ -526,7 +526,8 @@ def run_micro(args: argparse.Namespace) -> None:
     from microserve_b200.config import CacheConfig, ModelConfig
 
     hq, hkv, dh, bs, nseq = TARGET["n_heads"], TARGET["n_kv_heads"], 64, BLOCK, args.requests
-    ctx = contexts(nseq, args.ctx_min, args.ctx_max, args.seed)
+    # longest context first: the order ms_forward schedules a batch's sequences in
+    ctx = np.sort(contexts(nseq, args.ctx_min, args.ctx_max, args.seed))[::-1].copy()
     cfg = ModelConfig(vocab_size=16, n_layers=1, d_model=hq * dh, n_heads=hq, n_kv_heads=hkv,
                       max_seq_len=4096, dtype="bfloat16")
     cache = PagedKVCache(cfg, CacheConfig(bs, int(sum(-(-int(c) // bs) for c in ctx)) + 16,
@@ -551,7 +552,8 @@ def run_micro(args: argparse.Namespace) -> None:
 
     us = _time_launches(call, args.iters)
     kv = float(ctx.sum()) * hkv * dh * 2 * 2
-    print(json.dumps({"micro": "attention", "qlen": args.qlen, "seqs": nseq, "us": us,
+    print(json.dumps({"micro": "attention", "qlen": args.qlen, "seqs": nseq, "order": "longest first",
+                      "us": us,
                       "kv_bytes": kv, "gbs": kv / us / 1e3, "frac_hbm": kv / us / 1e3 / peaks["hbm_gbs"],
                       "device_error": _lib.device_error()}), flush=True)
 

@@ -9,14 +9,14 @@
 //                  half) of K and of V into a kStages-deep ring, 128-byte
 //                  swizzled, completing on the stage's "full" mbarrier;
 //   consumer warps: warp w owns m-tile (w % MTP) of the query rows and key
-//                  slice (w / MTP) of every chunk, KW keys wide.  The slice
-//                  width is picked at launch from the batch's largest row
-//                  count, so a decode tile (8 rows, one m-tile) spreads each
-//                  chunk over all consumer warps instead of leaving all but
-//                  one idle.  Per slice: S = Q K^T and O += P V with ldmatrix
-//                  (swizzle-aware addresses) + mma.sync m16n8k16 bf16, online
-//                  softmax in base 2; then arrive on the stage's "empty"
-//                  barrier.
+//                  slice (w / MTP) of every chunk, KW keys wide.  Per slice:
+//                  S = Q K^T and O += P V with ldmatrix (swizzle-aware
+//                  addresses) + mma.sync m16n8k16 bf16, online softmax in
+//                  base 2; then arrive on the stage's "empty" barrier.
+// The layout is picked at launch from the batch's widest row tile.  For dh 64
+// each warp takes a whole 64-key chunk of one m-tile, so the CTA is as narrow
+// as its rows (1-4 consumer warps) and 3-6 CTAs share an SM; the dh 128
+// layout splits each chunk's keys over the warps that the m-tiles leave.
 // When a chunk is split over several warps, their (max, sum, O) states are
 // merged through shared memory at the end, with the same rescaling the
 // cross-CTA split-KV combine uses.
@@ -43,26 +43,40 @@ constexpr int kErrTimeout = 5;
 constexpr int kErrRows = 6;  // a row tile wider than the launch's slice layout covers
 constexpr int kTblCap = 64;  // block-table entries staged per refill (multiple of 16)
 
-// Default layout: 8 (dh 64) or 4 (dh 128) consumer warps, 3 or 2 ring stages,
-// 2 CTAs per SM.  A launch may pick fewer warps and stages to fit more CTAs.
-template <int DH, int NW = (DH == 64 ? 8 : 4), int NS = (DH == 64 ? 3 : 2)> struct TmaCfg {
-  static constexpr int kCh = DH == 64 ? 128 : 64;   // keys per stage
+// One launch layout: CHK keys per ring stage, NS stages, NW consumer warps,
+// each owning one 16-row m-tile and a KW-key slice of every chunk.  The Q
+// tile holds the rows those m-tiles cover, so a decode layout (one m-tile)
+// keeps 2 KB of Q instead of 9 KB and more CTAs fit on an SM.
+template <int DH, int KW, int NW, int NS, int CHK>
+struct TmaCfg {
+  static constexpr int kCh = CHK;                   // keys per stage
   static constexpr int kWarps = NW;                 // consumer warps
+  static constexpr int kKS = CHK / KW;              // key slices per chunk
+  static constexpr int kMTP = NW / kKS;             // m-tiles the warps cover
+  static constexpr int kQRows = kMTP * 16;
   static constexpr int kThreads = (kWarps + 1) * 32;
   static constexpr int kHalves = DH / 64;           // 128-byte column halves
   static constexpr int kStages = NS;
   static constexpr int kTileBytes = kCh * DH * 2;   // one operand, one chunk
   static constexpr int kStageBytes = 2 * kTileBytes;  // K + V
   static constexpr int kLdQ = DH + 8;
-  static constexpr int kQBytes = kRows * kLdQ * 2;
+  static constexpr int kQBytes = kQRows * kLdQ * 2;
   static constexpr int kLdPart = DH + 8;            // merge buffer row stride (floats)
   static constexpr int kPartBytes = kWarps * 16 * (kLdPart * 4 + 8);
-  static_assert(kPartBytes <= kStages * kStageBytes, "merge buffer must fit in the ring");
+  static_assert(KW % 16 == 0 && CHK % KW == 0 && NW % kKS == 0 && kQRows <= kRows,
+                "slice layout");
+  static_assert(kKS == 1 || kPartBytes <= kStages * kStageBytes, "merge buffer must fit in the ring");
   static_assert(kTblCap % (kCh / 8) == 0, "table refill must hold whole chunks");
   static constexpr int kSmem =
       1024 + kStages * kStageBytes + kQBytes + kRows * 4 + 128 + kTblCap * 4;
 };
-
+// Default layout (wide row tiles): 8 (dh 64) or 4 (dh 128) consumer warps,
+// 3 or 2 stages of 128 or 64 keys, 2 CTAs per SM.
+template <int DH> struct TmaDefault {
+  static constexpr int kCh = DH == 64 ? 128 : 64;
+  static constexpr int kWarps = DH == 64 ? 8 : 4;
+  static constexpr int kStages = DH == 64 ? 3 : 2;
+};
 __device__ __forceinline__ uint32_t s_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -156,12 +170,11 @@ __device__ __forceinline__ bool consumer_any(int threads, bool pred) {
   return r != 0;
 }
 
-// Address of the 16-byte chunk `c` (0 .. DH/8-1) of key row `k` (0..kCh-1) in
+// Address of the 16-byte chunk `c` (0 .. dh/8-1) of key row `k` (0..CH-1) in
 // a swizzled operand tile: half c/8, row k of 128 bytes, chunk (c%8) ^ (k%8).
-template <int DH>
+template <int CH>
 __device__ __forceinline__ uint32_t tile_addr(uint32_t tile, int k, int c) {
-  return tile +
-         (uint32_t)((c >> 3) * (TmaCfg<DH>::kCh * 128) + k * 128 + (((c & 7) ^ (k & 7)) << 4));
+  return tile + (uint32_t)((c >> 3) * (CH * 128) + k * 128 + (((c & 7) ^ (k & 7)) << 4));
 }
 
 struct TmaArgs {
@@ -180,11 +193,11 @@ struct TmaArgs {
   int* err;
 };
 
-template <int DH, int KW, int NWARPS, int NSTAGES, int MINB>
-__global__ void __launch_bounds__(TmaCfg<DH, NWARPS, NSTAGES>::kThreads, MINB)
+template <int DH, int KW, int NWARPS, int NSTAGES, int MINB, int CHK>
+__global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads, MINB)
     attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     TmaArgs a) {
-  using Cfg = TmaCfg<DH, NWARPS, NSTAGES>;
+  using Cfg = TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>;
   constexpr int S = Cfg::kStages;
   constexpr int CH = Cfg::kCh;
   constexpr int NW = Cfg::kWarps;
@@ -234,7 +247,7 @@ __global__ void __launch_bounds__(TmaCfg<DH, NWARPS, NSTAGES>::kThreads, MINB)
   for (int i = threadIdx.x; i < S * Cfg::kStageBytes / 16; i += Cfg::kThreads)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   // Q tile (zero rows past nr).
-  for (int idx = threadIdx.x; idx < kRows * (DH / 8); idx += Cfg::kThreads) {
+  for (int idx = threadIdx.x; idx < Cfg::kQRows * (DH / 8); idx += Cfg::kThreads) {
     const int r = idx / (DH / 8), c = (idx % (DH / 8)) * 8;
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < nr) {
@@ -366,7 +379,7 @@ __global__ void __launch_bounds__(TmaCfg<DH, NWARPS, NSTAGES>::kThreads, MINB)
           uint32_t b0, b1, b2, b3;
           const int key = kof + nt * 8 + (lane & 7) + ((lane >> 4) << 3);
           const int c = 2 * k + ((lane >> 3) & 1);
-          ldm_x4(tile_addr<DH>(Kt, key, c), b0, b1, b2, b3);
+          ldm_x4(tile_addr<CH>(Kt, key, c), b0, b1, b2, b3);
           mma_bf16(sc[nt], a0, a1, a2, a3, b0, b1);
           mma_bf16(sc[nt + 1], a0, a1, a2, a3, b2, b3);
         }
@@ -442,7 +455,7 @@ __global__ void __launch_bounds__(TmaCfg<DH, NWARPS, NSTAGES>::kThreads, MINB)
 #pragma unroll
         for (int nt = 0; nt < NT; nt += 2) {
           uint32_t b0, b1, b2, b3;
-          ldm_x4_t(tile_addr<DH>(Vt, key, nt + (lane >> 4)), b0, b1, b2, b3);
+          ldm_x4_t(tile_addr<CH>(Vt, key, nt + (lane >> 4)), b0, b1, b2, b3);
           mma_bf16(o[nt], p0, p1, p2, p3, b0, b1);
           mma_bf16(o[nt + 1], p0, p1, p2, p3, b2, b3);
         }
@@ -638,10 +651,11 @@ __global__ void attn_tma_combine_kernel(TmaArgs a, int dh) {
   }
 }
 
-template <int DH, int KW, int NW = TmaCfg<DH>::kWarps, int NS = TmaCfg<DH>::kStages, int MINB = 2>
+template <int DH, int KW, int NW = TmaDefault<DH>::kWarps, int NS = TmaDefault<DH>::kStages,
+          int MINB = 2, int CHK = TmaDefault<DH>::kCh>
 int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
                cudaStream_t s) {
-  using Cfg = TmaCfg<DH, NW, NS>;
+  using Cfg = TmaCfg<DH, KW, NW, NS, CHK>;
   static_assert(MINB * (Cfg::kSmem + 1024) <= 228 * 1024, "CTAs per SM exceed shared memory");
   // The shared-memory opt-in is per device; remember it per device.
   static uint64_t attr_set = 0;
@@ -650,13 +664,13 @@ int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_s
   const uint64_t bit = 1ull << (dev & 63);
   if (!(attr_set & bit)) {
     const cudaError_t e =
-        cudaFuncSetAttribute(attn_tma_kernel<DH, KW, NW, NS, MINB>,
+        cudaFuncSetAttribute(attn_tma_kernel<DH, KW, NW, NS, MINB, CHK>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmem);
     if (e != cudaSuccess) return fail(MS_ERR_CUDA, "attn_tma: smem attribute: %s", cudaGetErrorString(e));
     attr_set |= bit;
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
-  attn_tma_kernel<DH, KW, NW, NS, MINB><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
+  attn_tma_kernel<DH, KW, NW, NS, MINB, CHK><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
   MS_TRY(check_launch("attn_tma_kernel"));
   if (a.n_splits > 1) {
     attn_tma_combine_kernel<<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a, DH);
@@ -665,20 +679,31 @@ int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_s
   return MS_OK;
 }
 
-// Slice width: the fewest m-tiles that cover the batch's widest row tile,
-// and the remaining consumer warps split each chunk's keys.
+// Layout by the batch's widest row tile.  dh 64: one warp per 16-row m-tile,
+// each warp covering a whole 64-key chunk (no cross-warp merge), 2-3 stages,
+// and as many CTAs per SM as shared memory and registers allow -- many
+// independent TMA streams per SM keep more K/V bytes in flight than wide
+// CTAs do (one layer of 256 sequences x 4 kv heads, contexts 512-2048: decode
+// 8 rows 60 us, 5-token verify 40 rows 78 us).  Otherwise the default layout:
+// the fewest m-tiles that cover the rows, the other warps splitting each
+// chunk's keys.
 template <int DH>
 int launch_by_rows(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
                    int max_rows, cudaStream_t s) {
   const int mt = (min(max_rows, kRows) + 15) / 16;
-  if (mt <= 1) return launch_tma<DH, TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
-  if (mt == 2) return launch_tma<DH, 2 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
-  // Three m-tiles (33-48 rows: a 5-token verify of 8 GQA heads): 3 m-tiles x 2
-  // key slices on 6 warps, 2 stages, so 3 CTAs share an SM (no idle warps).
   if constexpr (DH == 64) {
-    if (mt == 3) return launch_tma<DH, TmaCfg<DH>::kCh / 2, 6, 3, 2>(a, km, vm, n_seqs, s);
+    switch (mt) {
+      case 0:
+      case 1: return launch_tma<DH, 64, 1, 2, 6, 64>(a, km, vm, n_seqs, s);
+      case 2: return launch_tma<DH, 64, 2, 3, 4, 64>(a, km, vm, n_seqs, s);
+      case 3: return launch_tma<DH, 64, 3, 2, 4, 64>(a, km, vm, n_seqs, s);
+      default: return launch_tma<DH, 64, 4, 2, 3, 64>(a, km, vm, n_seqs, s);
+    }
   }
-  return launch_tma<DH, 4 * TmaCfg<DH>::kCh / TmaCfg<DH>::kWarps>(a, km, vm, n_seqs, s);
+  constexpr int kCh = TmaDefault<DH>::kCh, kW = TmaDefault<DH>::kWarps;
+  if (mt <= 1) return launch_tma<DH, kCh / kW>(a, km, vm, n_seqs, s);
+  if (mt == 2) return launch_tma<DH, 2 * kCh / kW>(a, km, vm, n_seqs, s);
+  return launch_tma<DH, 4 * kCh / kW>(a, km, vm, n_seqs, s);
 }
 
 }  // namespace
