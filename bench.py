@@ -64,7 +64,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
-    ap.add_argument("--micro", choices=["gemm8b", "attention"], default=None,
+    ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention"], default=None,
                     help="time one kernel family alone (1 GPU) instead of the speculative round")
     ap.add_argument("--only", default=None, help="--micro gemm8b: one shape (qkv, o_proj, ...)")
     ap.add_argument("--qlen", type=int, default=5, help="--micro attention: query tokens per sequence")
@@ -472,6 +472,18 @@ GEMM8B = [  # (name, N, K, epilogue, output dtype) at M = 256 requests x 6 token
 ]
 
 
+# The 1.1B target's verify GEMMs (M = 256 requests x 5 tokens) and the draft's (M = 256):
+# (name, M, N, K, epilogue, output dtype); weights cycle over the 22 layers' copies.
+GEMM1B = [
+    ("qkv", 1280, 2560, 2048, 0, "bf16"), ("o_proj", 1280, 2048, 2048, 1, "f32"),
+    ("gate_up", 1280, 11264, 2048, 2, "bf16"), ("down", 1280, 2048, 5632, 1, "f32"),
+    ("lm_head", 1280, 32000, 2048, 0, "f32"),
+    ("draft_qkv", 256, 2560, 2048, 0, "bf16"), ("draft_o_proj", 256, 2048, 2048, 1, "f32"),
+    ("draft_gate_up", 256, 11264, 2048, 2, "bf16"), ("draft_down", 256, 2048, 5632, 1, "f32"),
+    ("draft_lm_head", 256, 32000, 2048, 0, "f32"),
+]
+
+
 def _time_launches(call, iters: int) -> float:
     """Mean microseconds per launch over `iters` back-to-back launches (CUDA events)."""
     import torch
@@ -519,6 +531,35 @@ def run_micro(args: argparse.Namespace) -> None:
             print(json.dumps({"micro": "gemm8b", "gemm": name, "M": M, "N": N, "K": K, "us": us,
                               "tflops": tf, "frac_sustained": tf / peaks["bf16_sustained"],
                               "device_error": _lib.device_error()}), flush=True)
+        return
+    if args.micro == "gemm1b":
+        for name, M, N, K, epi, cd in GEMM1B:
+            if args.only and name != args.only:
+                continue
+            copies = 1 if name.endswith("lm_head") else TARGET["n_layers"]
+            A = (torch.randn(M, K, device="cuda", generator=g) * 0.5).bfloat16()
+            Bs = [(torch.randn(N, K, device="cuda", generator=g) * 0.02).bfloat16()
+                  for _ in range(copies)]
+            C = torch.zeros(M, N // 2 if epi == 2 else N, device="cuda",
+                            dtype=torch.float32 if cd == "f32" else torch.bfloat16)
+            R = C if epi == 1 else None
+            cdt = _lib.DTYPE_F32 if cd == "f32" else _lib.DTYPE_BF16
+            it = [0]
+
+            def call() -> None:
+                B = Bs[it[0] % copies]
+                it[0] += 1
+                _lib.call("ms_gemm", A.data_ptr(), B.data_ptr(), C.data_ptr(), _lib.ptr(R), M, N,
+                          K, 0, _lib.DTYPE_BF16, cdt, epi, _lib.stream_ptr())
+
+            us = _time_launches(call, max(args.iters, copies))
+            tf = 2.0 * M * N * K / us / 1e6
+            wbytes = N * K * 2
+            print(json.dumps({"micro": "gemm1b", "gemm": name, "M": M, "N": N, "K": K, "us": us,
+                              "tflops": tf, "frac_sustained": tf / peaks["bf16_sustained"],
+                              "weight_gbs": wbytes / us / 1e3, "weight_copies": copies,
+                              "device_error": _lib.device_error()}), flush=True)
+            del Bs
         return
     # attention: the config-3 verify (qlen 5) or draft (qlen 1) pass of one layer
     from microserve_b200.batching import build_paged_batch

@@ -28,6 +28,7 @@ __global__ void __launch_bounds__(kWarps * 32)
                      const int32_t* __restrict__ context_lens, const int32_t* __restrict__ positions,
                      const int32_t* __restrict__ tables, int max_blocks, int bs, int num_blocks,
                      int hq, int hkv, float scale, T* __restrict__ out, int* __restrict__ err) {
+  pdl_enter();
   // Lane l owns output dims l, l+32, ...; for d_head < 32 lanes >= DH idle.
   constexpr int PER_LANE = DH >= 32 ? DH / 32 : 1;
   constexpr int kRowsPerWarp = rows_per_warp<DH>();
@@ -147,7 +148,7 @@ int launch_attn(const void* q, int q_stride, const ms_kv_cache& c, int layer, co
   const int tiles = ceil_div(bt.max_q_len * group, kWarps * rows_per_warp<DH>());
   dim3 grid(tiles, c.n_kv_heads, bt.n_seqs);
   const float scale = 1.f / sqrtf((float)DH);
-  attn_simt_kernel<T, DH><<<grid, kWarps * 32, 0, s>>>(
+  launch_pdl(attn_simt_kernel<T, DH>, grid, kWarps * 32, 0, s,
       static_cast<const T*>(q), q_stride, static_cast<const T*>(c.k_pool[layer]),
       static_cast<const T*>(c.v_pool[layer]), bt.q_start, bt.context_lens, bt.positions,
       bt.block_tables, bt.max_blocks, c.block_size, c.num_blocks, hq, c.n_kv_heads, scale,
@@ -204,6 +205,7 @@ constexpr int kOrderTile = 2048;
 // written exactly once.
 __global__ void __launch_bounds__(kOrderThreads)
     seq_order_kernel(const int32_t* __restrict__ ctx, int n, int32_t* __restrict__ order) {
+  pdl_enter();
   __shared__ int keys[kOrderTile];
   const int b = blockIdx.x * kOrderThreads + threadIdx.x;
   const int kb = b < n ? ctx[b] : 0;
@@ -227,7 +229,7 @@ __global__ void __launch_bounds__(kOrderThreads)
 
 int attn_seq_order(const int32_t* context_lens, int n_seqs, int32_t* order, cudaStream_t s) {
   if (n_seqs <= 0) return MS_OK;
-  seq_order_kernel<<<(n_seqs + kOrderThreads - 1) / kOrderThreads, kOrderThreads, 0, s>>>(
+  launch_pdl(seq_order_kernel, (n_seqs + kOrderThreads - 1) / kOrderThreads, kOrderThreads, 0, s,
       context_lens, n_seqs, order);
   return check_launch("seq_order_kernel");
 }

@@ -97,6 +97,7 @@ struct AttnArgs {
 
 template <int DH>
 __global__ void __launch_bounds__(kThreads) attn_tc_kernel(AttnArgs a) {
+  pdl_enter();
   using Cfg = AttnCfg<DH>;
   constexpr int LD = Cfg::kLd;
   constexpr int NT = DH / 8;  // n8 tiles of the output
@@ -316,6 +317,7 @@ __global__ void __launch_bounds__(kThreads) attn_tc_kernel(AttnArgs a) {
 // Merge the split partials of sequences with more than one KV range.
 template <int DH>
 __global__ void attn_combine_kernel(AttnArgs a) {
+  pdl_enter();
   const int rt = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int group = a.hq / a.hkv;
   const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
@@ -359,10 +361,10 @@ int launch(AttnArgs& a, int n_seqs, cudaStream_t s) {
     attr_set |= 1ull << (dev & 63);
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
-  attn_tc_kernel<DH><<<grid, kThreads, Cfg::kSmem, s>>>(a);
+  launch_pdl(attn_tc_kernel<DH>, grid, kThreads, Cfg::kSmem, s, a);
   MS_TRY(check_launch("attn_tc_kernel"));
   if (a.n_splits > 1) {
-    attn_combine_kernel<DH><<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a);
+    launch_pdl(attn_combine_kernel<DH>, dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s, a);
     MS_TRY(check_launch("attn_combine_kernel"));
   }
   return MS_OK;

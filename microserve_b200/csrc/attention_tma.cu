@@ -197,6 +197,7 @@ template <int DH, int KW, int NWARPS, int NSTAGES, int MINB, int CHK>
 __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads, MINB)
     attn_tma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                     TmaArgs a) {
+  pdl_enter();
   using Cfg = TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>;
   constexpr int S = Cfg::kStages;
   constexpr int CH = Cfg::kCh;
@@ -622,6 +623,7 @@ int pool_map(const void* pool, int64_t rows, int dh, int bs, CUtensorMap* out) {
 }
 
 __global__ void attn_tma_combine_kernel(TmaArgs a, int dh) {
+  pdl_enter();
   const int rt = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int group = a.hq / a.hkv;
   const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
@@ -670,10 +672,10 @@ int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_s
     attr_set |= bit;
   }
   dim3 grid(a.row_tiles * a.n_splits, a.hkv, n_seqs);
-  attn_tma_kernel<DH, KW, NW, NS, MINB, CHK><<<grid, Cfg::kThreads, Cfg::kSmem, s>>>(km, vm, a);
+  launch_pdl(attn_tma_kernel<DH, KW, NW, NS, MINB, CHK>, grid, Cfg::kThreads, Cfg::kSmem, s, km, vm, a);
   MS_TRY(check_launch("attn_tma_kernel"));
   if (a.n_splits > 1) {
-    attn_tma_combine_kernel<<<dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s>>>(a, DH);
+    launch_pdl(attn_tma_combine_kernel, dim3(a.row_tiles, a.hkv, n_seqs), 256, 0, s, a, DH);
     MS_TRY(check_launch("attn_tma_combine_kernel"));
   }
   return MS_OK;

@@ -72,6 +72,7 @@ ProfScope::~ProfScope() {
 
 __global__ void philox_uniforms_kernel(const uint64_t* seeds, const uint64_t* steps, int n,
                                        uint32_t lane, float* out) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) out[i] = philox_uniform(seeds[i], steps[i], lane);
 }
@@ -134,7 +135,7 @@ extern "C" int ms_philox_uniforms(const uint64_t* seeds, const uint64_t* steps, 
   MS_REQUIRE(n >= 0, "ms_philox_uniforms: n < 0");
   if (n == 0) return MS_OK;
   MS_REQUIRE(seeds && steps && out, "ms_philox_uniforms: null pointer");
-  philox_uniforms_kernel<<<ceil_div(n, 256), 256, 0, as_stream(stream)>>>(seeds, steps, n,
+  launch_pdl(philox_uniforms_kernel, ceil_div(n, 256), 256, 0, as_stream(stream), seeds, steps, n,
                                                                           (uint32_t)lane, out);
   return check_launch("ms_philox_uniforms");
 }

@@ -8,6 +8,7 @@
 #include <atomic>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/microserve_b200.h"
 
@@ -21,6 +22,37 @@ extern std::atomic<uint64_t> g_launches;
 int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---- programmatic dependent launch -------------------------------------------
+// Every kernel of this library begins with pdl_enter(): it waits until the
+// previous kernel on the stream has completed and its writes are visible
+// (griddepcontrol.wait), then allows the next launch to begin
+// (griddepcontrol.launch_dependents).  Launched with launch_pdl, a kernel's
+// CTAs are scheduled while its predecessor's last CTAs still run and start
+// the moment it completes, so back-to-back launches lose no launch latency.
+// Nothing is read or written before the wait, so ordering is the stream's.
+// Launched without the attribute, the wait returns at once.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  // A failure is recorded as the thread's last error; check_launch reports it.
+  (void)cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- live per-kernel-class timing (ms_profile_start / ms_profile_stop) -----
 // While a class is selected, every launch of that class is bracketed by a

@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const TA* __restrict__ A
                                                        TC* __restrict__ C,
                                                        const float* __restrict__ R, int M, int N,
                                                        int K, int64_t ldc, int epilogue) {
+  pdl_enter();
   __shared__ float As[BK][BM + 4];
   __shared__ float Bs[BK][BN + 4];
   __shared__ float Cs[BM][BN + 1];
@@ -86,7 +87,7 @@ template <typename TA, typename TC>
 int launch_simt(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
                 int64_t ldc, int epi, cudaStream_t s) {
   dim3 grid(ceil_div(N, BN), ceil_div(M, BM));
-  gemm_simt_kernel<TA, TC><<<grid, 256, 0, s>>>(static_cast<const TA*>(A),
+  launch_pdl(gemm_simt_kernel<TA, TC>, grid, 256, 0, s, static_cast<const TA*>(A),
                                                 static_cast<const TA*>(B), static_cast<TC*>(C),
                                                 R, M, N, K, ldc, epi);
   return check_launch("gemm_simt_kernel");

@@ -271,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
                    const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
                    int* err) {
+  pdl_enter();
   using Cfg = TileCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -497,7 +498,7 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
   int grid = stream_k ? (int)std::min<int64_t>((int64_t)tiles * kiters, kNumSMs)
                       : std::min(tiles, kNumSMs);
   if (grid < 1) grid = 1;
-  kern<<<grid, kThreads, Cfg::kSmem, s>>>(ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
+  launch_pdl(kern, grid, kThreads, Cfg::kSmem, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
                                           stream_k ? 1 : 0, device_error_word());
   return check_launch("gemm_tc_kernel");
 }

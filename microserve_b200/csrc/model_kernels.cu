@@ -16,6 +16,7 @@ template <typename TY>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                TY* __restrict__ y, const int32_t* __restrict__ row_idx, int n_rows,
                                int dim, float eps) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n_rows) return;
@@ -40,6 +41,7 @@ template <typename TY>
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_vec_kernel(const float* __restrict__ x, const float* __restrict__ w, TY* __restrict__ y,
                        const int32_t* __restrict__ row_idx, int dim, float eps) {
+  pdl_enter();
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   const int src = row_idx ? row_idx[row] : row;
@@ -85,6 +87,7 @@ __global__ void embed_rmsnorm_kernel(const TW* __restrict__ embed, const int32_t
                                      int n_tokens, int vocab, int dim, const float* __restrict__ w,
                                      float eps, float* __restrict__ x, TW* __restrict__ y,
                                      int* __restrict__ err) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= n_tokens) return;
@@ -122,6 +125,7 @@ __global__ void rope_kv_kernel(T* __restrict__ qkv, const int32_t* __restrict__ 
                                const float* __restrict__ sin_t, int max_pos, int hq, int hkv,
                                int dh, int bs, int num_blocks, T* __restrict__ kpool,
                                T* __restrict__ vpool, int* __restrict__ err) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int width = (hq + 2 * hkv) * dh;
   T* row = qkv + (int64_t)t * width;
@@ -181,6 +185,7 @@ __global__ void __launch_bounds__(128)
                        const float* __restrict__ sin_t, int max_pos, int n_tokens, int hq, int hkv,
                        int dh, int bs, int num_blocks, __nv_bfloat16* __restrict__ kpool,
                        __nv_bfloat16* __restrict__ vpool, int* __restrict__ err) {
+  pdl_enter();
   const int width = (hq + 2 * hkv) * dh;
   const int half = dh / 2, hc = half / 8, vc = dh / 8;
   const int n_rot = (hq + hkv) * hc, per_token = n_rot + hkv * vc;
@@ -249,6 +254,7 @@ __global__ void kv_write_kernel(const int32_t* __restrict__ slots, int n_tokens,
                                 const float* __restrict__ keys, const float* __restrict__ values,
                                 int hkv, int dh, int bs, int num_blocks, T* __restrict__ kpool,
                                 T* __restrict__ vpool, int* __restrict__ err) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int slot = slots[t];
   for (int idx = threadIdx.x; idx < hkv * dh; idx += blockDim.x) {
@@ -272,6 +278,7 @@ __global__ void kv_gather_kernel(const int32_t* __restrict__ tables, int max_blo
                                  const T* __restrict__ kpool, const T* __restrict__ vpool,
                                  float* __restrict__ keys, float* __restrict__ values,
                                  int* __restrict__ err) {
+  pdl_enter();
   const int j = blockIdx.x, b = blockIdx.y;
   int blk = tables[(int64_t)b * max_blocks + j / bs];
   if (blk < 0 || blk >= num_blocks) {
@@ -300,10 +307,10 @@ int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int
                          reinterpret_cast<uintptr_t>(y)) & 15) == 0;
   if (dim % 4 == 0 && dim <= 4 * kNormThreads * kVec && aligned) {
     if (dtype == MS_DTYPE_F32)
-      rmsnorm_vec_kernel<float><<<n_rows, kNormThreads, 0, s>>>(x, w, static_cast<float*>(y),
+      launch_pdl(rmsnorm_vec_kernel<float>, n_rows, kNormThreads, 0, s, x, w, static_cast<float*>(y),
                                                                 row_idx, dim, eps);
     else if (dtype == MS_DTYPE_BF16)
-      rmsnorm_vec_kernel<__nv_bfloat16><<<n_rows, kNormThreads, 0, s>>>(
+      launch_pdl(rmsnorm_vec_kernel<__nv_bfloat16>, n_rows, kNormThreads, 0, s,
           x, w, static_cast<__nv_bfloat16*>(y), row_idx, dim, eps);
     else
       return fail(MS_ERR_UNSUPPORTED, "rmsnorm: dtype %d", dtype);
@@ -311,10 +318,10 @@ int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int
   }
   const int blocks = ceil_div(n_rows, 8);
   if (dtype == MS_DTYPE_F32)
-    rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(x, w, static_cast<float*>(y), row_idx, n_rows, dim,
+    launch_pdl(rmsnorm_kernel<float>, blocks, 256, 0, s, x, w, static_cast<float*>(y), row_idx, n_rows, dim,
                                                  eps);
   else if (dtype == MS_DTYPE_BF16)
-    rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(x, w, static_cast<__nv_bfloat16*>(y),
+    launch_pdl(rmsnorm_kernel<__nv_bfloat16>, blocks, 256, 0, s, x, w, static_cast<__nv_bfloat16*>(y),
                                                          row_idx, n_rows, dim, eps);
   else
     return fail(MS_ERR_UNSUPPORTED, "rmsnorm: dtype %d", dtype);
@@ -327,11 +334,11 @@ int embed_rmsnorm(const void* embed, const int32_t* ids, int n_tokens, int vocab
   ProfScope prof(kClsNorm, s);
   const int blocks = ceil_div(n_tokens, 8);
   if (dtype == MS_DTYPE_F32)
-    embed_rmsnorm_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(embed), ids,
+    launch_pdl(embed_rmsnorm_kernel<float>, blocks, 256, 0, s, static_cast<const float*>(embed), ids,
                                                        n_tokens, vocab, dim, w, eps, x,
                                                        static_cast<float*>(y), device_error_word());
   else if (dtype == MS_DTYPE_BF16)
-    embed_rmsnorm_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(
+    launch_pdl(embed_rmsnorm_kernel<__nv_bfloat16>, blocks, 256, 0, s,
         static_cast<const __nv_bfloat16*>(embed), ids, n_tokens, vocab, dim, w, eps, x,
         static_cast<__nv_bfloat16*>(y), device_error_word());
   else
@@ -346,7 +353,7 @@ int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, con
   ProfScope prof(kClsNorm, s);
   const int threads = 128;
   if (dtype == MS_DTYPE_F32)
-    rope_kv_kernel<float><<<n_tokens, threads, 0, s>>>(
+    launch_pdl(rope_kv_kernel<float>, n_tokens, threads, 0, s,
         static_cast<float*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
         cache.block_size, cache.num_blocks, static_cast<float*>(cache.k_pool[layer]),
         static_cast<float*>(cache.v_pool[layer]), device_error_word());
@@ -354,14 +361,14 @@ int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, con
            (reinterpret_cast<uintptr_t>(qkv) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(cos_t) & 15) == 0 &&
            (reinterpret_cast<uintptr_t>(sin_t) & 15) == 0) {
-    rope_kv_vec_kernel<<<ceil_div(n_tokens, kRopeTokens), threads, 0, s>>>(
+    launch_pdl(rope_kv_vec_kernel, ceil_div(n_tokens, kRopeTokens), threads, 0, s,
         static_cast<__nv_bfloat16*>(qkv), positions, slots, cos_t, sin_t, max_pos, n_tokens, hq,
         hkv, dh, cache.block_size, cache.num_blocks,
         static_cast<__nv_bfloat16*>(cache.k_pool[layer]),
         static_cast<__nv_bfloat16*>(cache.v_pool[layer]), device_error_word());
     return check_launch("rope_kv_vec_kernel");
   } else if (dtype == MS_DTYPE_BF16)
-    rope_kv_kernel<__nv_bfloat16><<<n_tokens, threads, 0, s>>>(
+    launch_pdl(rope_kv_kernel<__nv_bfloat16>, n_tokens, threads, 0, s,
         static_cast<__nv_bfloat16*>(qkv), positions, slots, cos_t, sin_t, max_pos, hq, hkv, dh,
         cache.block_size, cache.num_blocks, static_cast<__nv_bfloat16*>(cache.k_pool[layer]),
         static_cast<__nv_bfloat16*>(cache.v_pool[layer]), device_error_word());
@@ -400,13 +407,13 @@ extern "C" int ms_kv_write(const ms_kv_cache* cache, int layer, const int32_t* s
   const ms_kv_cache& c = *cache;
   cudaStream_t s = as_stream(stream);
   if (c.dtype == MS_DTYPE_F32)
-    kv_write_kernel<float><<<n_tokens, 128, 0, s>>>(slots, n_tokens, keys, values, c.n_kv_heads,
+    launch_pdl(kv_write_kernel<float>, n_tokens, 128, 0, s, slots, n_tokens, keys, values, c.n_kv_heads,
                                                     c.d_head, c.block_size, c.num_blocks,
                                                     static_cast<float*>(c.k_pool[layer]),
                                                     static_cast<float*>(c.v_pool[layer]),
                                                     device_error_word());
   else if (c.dtype == MS_DTYPE_BF16)
-    kv_write_kernel<__nv_bfloat16><<<n_tokens, 128, 0, s>>>(
+    launch_pdl(kv_write_kernel<__nv_bfloat16>, n_tokens, 128, 0, s,
         slots, n_tokens, keys, values, c.n_kv_heads, c.d_head, c.block_size, c.num_blocks,
         static_cast<__nv_bfloat16*>(c.k_pool[layer]), static_cast<__nv_bfloat16*>(c.v_pool[layer]),
         device_error_word());
@@ -429,14 +436,14 @@ extern "C" int ms_kv_gather(const ms_kv_cache* cache, int layer, const int32_t* 
   dim3 grid(max_context, n_seqs);
   cudaStream_t s = as_stream(stream);
   if (c.dtype == MS_DTYPE_F32)
-    kv_gather_kernel<float><<<grid, 128, 0, s>>>(block_tables, max_blocks, max_context,
+    launch_pdl(kv_gather_kernel<float>, grid, 128, 0, s, block_tables, max_blocks, max_context,
                                                  c.n_kv_heads, c.d_head, c.block_size,
                                                  c.num_blocks,
                                                  static_cast<const float*>(c.k_pool[layer]),
                                                  static_cast<const float*>(c.v_pool[layer]), keys,
                                                  values, device_error_word());
   else if (c.dtype == MS_DTYPE_BF16)
-    kv_gather_kernel<__nv_bfloat16><<<grid, 128, 0, s>>>(
+    launch_pdl(kv_gather_kernel<__nv_bfloat16>, grid, 128, 0, s,
         block_tables, max_blocks, max_context, c.n_kv_heads, c.d_head, c.block_size, c.num_blocks,
         static_cast<const __nv_bfloat16*>(c.k_pool[layer]),
         static_cast<const __nv_bfloat16*>(c.v_pool[layer]), keys, values, device_error_word());

@@ -834,6 +834,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const float* __rest
                                    int32_t* __restrict__ tokens, float* __restrict__ probs,
                                    ms_row_stats* __restrict__ stats, int32_t* scatter_dst,
                                    const int32_t* __restrict__ scatter_idx, int stage) {
+  pdl_enter();
   RowSmem sm;
   setup_smem(sm, V, stage != 0);
   const int r = blockIdx.x;
@@ -893,6 +894,7 @@ struct AcceptArgs {
 };
 
 __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int stage) {
+  pdl_enter();
   RowSmem sm;
   setup_smem(sm, a.V, stage != 0);
   const int b = blockIdx.x;
@@ -1037,7 +1039,7 @@ int launch_accept(AcceptArgs a, int B, void* stream) {
                                        (int)smem);
   if (e != cudaSuccess) return fail(MS_ERR_CUDA, "spec_accept: smem attribute: %s", cudaGetErrorString(e));
   ProfScope prof(kClsAccept, as_stream(stream));
-  spec_accept_kernel<<<B, threads, smem, as_stream(stream)>>>(a, stage ? 1 : 0);
+  launch_pdl(spec_accept_kernel, B, threads, smem, as_stream(stream), a, stage ? 1 : 0);
   return check_launch("spec_accept_kernel");
 }
 
@@ -1061,7 +1063,7 @@ extern "C" int ms_sample(const float* logits, int64_t row_stride, int n_rows, in
                                        (int)smem);
   if (e != cudaSuccess) return fail(MS_ERR_CUDA, "ms_sample: smem attribute: %s", cudaGetErrorString(e));
   ProfScope prof(kClsSample, as_stream(stream));
-  sample_rows_kernel<<<n_rows, threads, smem, as_stream(stream)>>>(
+  launch_pdl(sample_rows_kernel, n_rows, threads, smem, as_stream(stream),
       logits, row_stride, vocab, params, pidx, (uint32_t)lane, tokens, probs, stats, scatter_dst,
       scatter_idx, stage ? 1 : 0);
   return check_launch("sample_rows_kernel");
