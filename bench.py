@@ -64,10 +64,12 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
-    ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention"], default=None,
+    ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention", "accept", "engine"],
+                    default=None,
                     help="time one kernel family alone (1 GPU) instead of the speculative round")
     ap.add_argument("--only", default=None, help="--micro gemm8b: one shape (qkv, o_proj, ...)")
     ap.add_argument("--qlen", type=int, default=5, help="--micro attention: query tokens per sequence")
+    ap.add_argument("--dh", type=int, default=64, choices=[64, 128], help="--micro attention: head size")
     ap.add_argument("--iters", type=int, default=20, help="--micro: timed launches")
     return ap.parse_args()
 
@@ -500,6 +502,119 @@ def _time_launches(call, iters: int) -> float:
     return e0.elapsed_time(e1) / iters * 1e3
 
 
+def run_micro_accept(args: argparse.Namespace, peaks: dict[str, float]) -> None:
+    """The acceptance microbenchmark: 4096 requests, gamma 5, vocab 32000, fp32 logits.
+
+    Target logits N(0, 2^2); draft logits = the target's first gamma rows plus
+    N(0, 0.5^2) noise (seed 1234).  Proposals are drawn from the draft rows
+    (ms_sample, untimed); the timed call is ms_spec_accept over all requests.
+    Algorithmic bytes: every target and draft row read once,
+    4096 * (2*gamma + 1) * V * 4 B = 5.77 GB per call.
+    """
+    import torch
+
+    from microserve_b200 import _lib
+    from microserve_b200.sampling import params_to_device
+
+    B, G, V = 4096, 5, 32000
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    target = torch.randn(B, G + 1, V, device="cuda", generator=gen) * 2.0
+    noise = torch.randn(G, B, V, device="cuda", generator=gen) * 0.5
+    draft = target[:, :G, :].permute(1, 0, 2) + noise  # position-major: row i*B + b
+    del noise
+    target = target.reshape(B * (G + 1), V)
+    draft = draft.contiguous().reshape(G * B, V)
+    proposals = torch.empty(G * B, dtype=torch.int32, device="cuda")
+    stats = torch.empty(G * B * 16, dtype=torch.uint8, device="cuda")
+    out = torch.empty(B * (G + 1), dtype=torch.int32, device="cuda")
+    nacc = torch.empty(B, dtype=torch.int32, device="cuda")
+    kv_bytes = float(B) * (2 * G + 1) * V * 4
+    stream = _lib.stream_ptr()
+    for label, top_k, top_p in (("plain", 0, 1.0), ("top-k 50", 50, 1.0), ("top-p 0.9", 0, 0.9)):
+        p = np.zeros(B, dtype=_lib.SAMPLING_PARAMS_DTYPE)
+        p["temperature"] = 1.0
+        p["top_k"] = top_k
+        p["top_p"] = top_p
+        p["seed"] = 1234
+        p["step"] = np.arange(B, dtype=np.uint64)
+        params = params_to_device(p, torch.device("cuda"))
+        for i in range(G):
+            _lib.call("ms_sample", draft[i * B:].data_ptr(), V, B, V, params.data_ptr(), None,
+                      _lib.LANE_DRAFT + i, proposals[i * B:].data_ptr(), None,
+                      stats[i * B * 16:].data_ptr(), None, None, stream)
+
+        def call() -> None:
+            _lib.call("ms_spec_accept", target.data_ptr(), V, draft.data_ptr(), V,
+                      stats.data_ptr(), 0, proposals.data_ptr(), params.data_ptr(), B, G, V,
+                      out.data_ptr(), nacc.data_ptr(), stream)
+
+        us = _time_launches(call, args.iters)
+        rate = float(nacc.float().mean()) / G
+        print(json.dumps({"micro": "accept", "variant": label, "requests": B, "gamma": G,
+                          "vocab": V, "us": us, "algorithmic_bytes": kv_bytes,
+                          "gbs": kv_bytes / us / 1e3, "frac_hbm": kv_bytes / us / 1e3 / peaks["hbm_gbs"],
+                          "acceptance_rate": rate, "device_error": _lib.device_error()}),
+              flush=True)
+
+
+def run_micro_engine(args: argparse.Namespace) -> None:
+    """Continuous batching with speculative decoding through the public LLMEngine.
+
+    The character-level fp32 models (target d128 L4 H4 ff352 V65, draft d64
+    L2 H2 ff176), random-init weights; 1024 concurrent requests, prompts
+    lognormal (mean 100, std 50, clipped to [8, 512]) of uniform token ids,
+    output budgets uniform in [1, 50]; block 16 with interleaved allocation
+    (the scheduler admits requests in arrival order).  One line per (gamma,
+    greedy | T 0.8): generated tokens / wall time of ``LLMEngine.run`` from
+    the first prefill to the last request finishing, and the K/V bytes the
+    speculative rounds' attention read (target 4 KB and draft 1 KB per cached
+    token per pass).
+    """
+    import torch
+
+    from microserve_b200.config import (CacheConfig, EngineConfig, ModelConfig, SamplingConfig,
+                                        SchedulerConfig, SpeculativeConfig)
+    from microserve_b200.engine import LLMEngine
+    from microserve_b200.model import Transformer
+
+    n_req = 1024
+    rng = np.random.default_rng(args.seed)
+    mean, std = 100.0, 50.0
+    sig2 = np.log(1.0 + (std / mean) ** 2)
+    lens = np.clip(rng.lognormal(np.log(mean) - sig2 / 2, np.sqrt(sig2), n_req), 8, 512).astype(int)
+    outs = rng.integers(1, 51, n_req)
+    prompts = [rng.integers(0, 65, int(n)).tolist() for n in lens]
+    msl = 512 + 64
+    tcfg = ModelConfig(vocab_size=65, d_model=128, n_layers=4, n_heads=4, d_ff=352, max_seq_len=msl)
+    dcfg = ModelConfig(vocab_size=65, d_model=64, n_layers=2, n_heads=2, d_ff=176, max_seq_len=msl)
+    target = Transformer(tcfg, "cuda", seed=0)
+    draft = Transformer(dcfg, "cuda", seed=1)
+    blocks = int(((lens + outs + 16) // 16 + 2).sum()) + 64
+    for gamma in (1, 2, 3, 5):
+        for temp in (0.0, 0.8):
+            cfg = EngineConfig(
+                model=tcfg, cache=CacheConfig(16, blocks, "float32"),
+                scheduler=SchedulerConfig(max_batch_size=n_req, max_batched_tokens=1 << 18),
+                speculative=SpeculativeConfig(enabled=True, gamma=gamma), seed=args.seed)
+            eng = LLMEngine(target, cfg, draft_model=draft)
+            for pr, o in zip(prompts, outs.tolist()):
+                eng.add_request(pr, SamplingConfig(temperature=temp, max_new_tokens=o))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            results = eng.run()
+            torch.cuda.synchronize()
+            secs = time.perf_counter() - t0
+            toks = sum(len(r.output_ids) for r in results)
+            st = eng.stats
+            print(json.dumps({"micro": "engine", "gamma": gamma, "temperature": temp,
+                              "requests": n_req, "generated_tokens": toks, "seconds": secs,
+                              "tok_s": toks / secs, "steps": st.num_steps,
+                              "spec_rounds": st.num_spec_rounds,
+                              "acceptance_rate": st.acceptance_rate,
+                              "mean_batch": st.mean_batch_size}), flush=True)
+            del eng
+
+
 def run_micro(args: argparse.Namespace) -> None:
     import ctypes
 
@@ -561,16 +676,25 @@ def run_micro(args: argparse.Namespace) -> None:
                               "device_error": _lib.device_error()}), flush=True)
             del Bs
         return
+    if args.micro == "accept":
+        run_micro_accept(args, peaks)
+        return
+    if args.micro == "engine":
+        run_micro_engine(args)
+        return
     # attention: the config-3 verify (qlen 5) or draft (qlen 1) pass of one layer
     from microserve_b200.batching import build_paged_batch
     from microserve_b200.cache import PagedKVCache
     from microserve_b200.config import CacheConfig, ModelConfig
 
-    hq, hkv, dh, bs, nseq = TARGET["n_heads"], TARGET["n_kv_heads"], 64, BLOCK, args.requests
+    # dh 64: the 1.1B target (4 kv heads); dh 128: the 8B target's heads (8 kv heads)
+    hq, bs, nseq = TARGET["n_heads"], BLOCK, args.requests
+    dh = args.dh
+    hkv = TARGET["n_kv_heads"] if dh == 64 else 8
     # longest context first: the order ms_forward schedules a batch's sequences in
     ctx = np.sort(contexts(nseq, args.ctx_min, args.ctx_max, args.seed))[::-1].copy()
     cfg = ModelConfig(vocab_size=16, n_layers=1, d_model=hq * dh, n_heads=hq, n_kv_heads=hkv,
-                      max_seq_len=4096, dtype="bfloat16")
+                      max_seq_len=max(4096, args.ctx_max + 64), dtype="bfloat16")
     cache = PagedKVCache(cfg, CacheConfig(bs, int(sum(-(-int(c) // bs) for c in ctx)) + 16,
                                           "bfloat16"), "cuda")
     cache.pool.normal_(generator=g)
@@ -593,7 +717,8 @@ def run_micro(args: argparse.Namespace) -> None:
 
     us = _time_launches(call, args.iters)
     kv = float(ctx.sum()) * hkv * dh * 2 * 2
-    print(json.dumps({"micro": "attention", "qlen": args.qlen, "seqs": nseq, "order": "longest first",
+    print(json.dumps({"micro": "attention", "qlen": args.qlen, "dh": dh, "kv_heads": hkv,
+                      "seqs": nseq, "ctx_range": [args.ctx_min, args.ctx_max], "order": "longest first",
                       "us": us,
                       "kv_bytes": kv, "gbs": kv / us / 1e3, "frac_hbm": kv / us / 1e3 / peaks["hbm_gbs"],
                       "device_error": _lib.device_error()}), flush=True)

@@ -14,9 +14,10 @@
 //                  addresses) + mma.sync m16n8k16 bf16, online softmax in
 //                  base 2; then arrive on the stage's "empty" barrier.
 // The layout is picked at launch from the batch's widest row tile.  For dh 64
-// each warp takes a whole 64-key chunk of one m-tile, so the CTA is as narrow
-// as its rows (1-4 consumer warps) and 3-6 CTAs share an SM; the dh 128
-// layout splits each chunk's keys over the warps that the m-tiles leave.
+// (and dh 128 up to 32 rows) each warp takes a whole 64-key chunk of one
+// m-tile, so the CTA is as narrow as its rows (1-4 consumer warps) and 3-6
+// CTAs share an SM; wider dh-128 tiles split each chunk's keys over the warps
+// that the m-tiles leave.
 // When a chunk is split over several warps, their (max, sum, O) states are
 // merged through shared memory at the end, with the same rescaling the
 // cross-CTA split-KV combine uses.
@@ -686,9 +687,10 @@ int launch_tma(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_s
 // and as many CTAs per SM as shared memory and registers allow -- many
 // independent TMA streams per SM keep more K/V bytes in flight than wide
 // CTAs do (one layer of 256 sequences x 4 kv heads, contexts 512-2048: decode
-// 8 rows 60 us, 5-token verify 40 rows 78 us).  Otherwise the default layout:
-// the fewest m-tiles that cover the rows, the other warps splitting each
-// chunk's keys.
+// 8 rows 60 us, 5-token verify 40 rows 78 us).  dh 128 up to 32 rows: the
+// same one-warp-per-m-tile layout at 3 CTAs per SM.  Wider dh-128 tiles: the
+// default layout, the fewest m-tiles that cover the rows and the other warps
+// splitting each chunk's keys.
 template <int DH>
 int launch_by_rows(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int n_seqs,
                    int max_rows, cudaStream_t s) {
@@ -701,6 +703,12 @@ int launch_by_rows(TmaArgs& a, const CUtensorMap& km, const CUtensorMap& vm, int
       case 3: return launch_tma<DH, 64, 3, 2, 4, 64>(a, km, vm, n_seqs, s);
       default: return launch_tma<DH, 64, 4, 2, 3, 64>(a, km, vm, n_seqs, s);
     }
+  }
+  if constexpr (DH == 128) {
+    // 8B-class heads (256 sequences x 8 kv heads, contexts 1024-3072): decode
+    // 4 rows 320 us, 6-token verify 24 rows 340 us, both at the copy bandwidth.
+    if (mt <= 1) return launch_tma<DH, 64, 1, 2, 3, 64>(a, km, vm, n_seqs, s);
+    if (mt == 2) return launch_tma<DH, 64, 2, 2, 3, 64>(a, km, vm, n_seqs, s);
   }
   constexpr int kCh = TmaDefault<DH>::kCh, kW = TmaDefault<DH>::kWarps;
   if (mt <= 1) return launch_tma<DH, kCh / kW>(a, km, vm, n_seqs, s);

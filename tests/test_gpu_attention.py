@@ -79,7 +79,7 @@ def test_tensor_core_attention_decode_and_verify(hq, hkv, dh, bs) -> None:
 
 
 @pytest.mark.parametrize("dh", [64, 128])
-@pytest.mark.parametrize("qlen", [1, 2, 5])
+@pytest.mark.parametrize("qlen", [1, 2, 4, 5])
 def test_tensor_core_attention_key_slices(dh: int, qlen: int) -> None:
     """Uniform decode (8 rows: every consumer warp takes a key slice of each
     chunk), two-token (16 rows) and verify (40 rows) batches, with contexts
