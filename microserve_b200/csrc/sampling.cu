@@ -990,18 +990,36 @@ __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int s
       continue;
     }
     // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0.
+    // With the target row staged, the residual replaces it in shared memory
+    // (each thread overwrites only the entries it has just read), so the
+    // draw walks shared memory instead of evaluating both rows again.
+    const Dist pv = p, qv = q;
+    const bool in_smem = p.mode == 0 && sm.stage != nullptr && p.row == sm.stage;
     float part = 0.f;
-    {
-      const Dist pv = p, qv = q;
+    if (in_smem) {
+      float* res = sm.stage;
+#pragma unroll 4
+      for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float r = fmaxf(pv.prob(j) - qv.prob(j), 0.f);
+        res[j] = r;
+        part += r;
+      }
+    } else {
 #pragma unroll 4
       for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(pv.prob(j) - qv.prob(j), 0.f);
     }
-    const float total = block_sum_b(part, sm);
+    const float total = block_sum_b(part, sm);  // its barriers also publish the residual
     const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
     int tok;
-    const Dist pv = p, qv = q;
     if (total <= 1e-9f) {
+      if (in_smem) {  // the residual overwrote p's staged row: stage it again
+        Dist again;
+        load_logits(again, a.target + (int64_t)(b * (G + 1) + i) * a.tstride, V, P.temperature, sm);
+      }
       tok = inverse_cdf([pv](int j) { return pv.prob(j); }, V, u2, sm);
+    } else if (in_smem) {
+      const float* res = sm.stage;
+      tok = inverse_cdf([res](int j) { return res[j]; }, V, u2, sm);
     } else {
       tok = inverse_cdf([pv, qv](int j) { return fmaxf(pv.prob(j) - qv.prob(j), 0.f); }, V, u2, sm);
     }
