@@ -112,9 +112,23 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
   MS_TRY(embed_rmsnorm(m.embed, bt.input_ids, T, m.vocab_size, d, m.attn_norm[0], m.norm_eps, w.x,
                        w.xn, dt, s));
   for (int l = 0; l < m.n_layers; ++l) {
-    MS_TRY(gemm_dispatch(w.xn, m.w_qkv[l], w.qkv, nullptr, T, qkv_w, d, 0, dt, dt, kEpiStore, s));
-    MS_TRY(rope_kv_write(w.qkv, bt.positions, bt.slot_mapping, m.rope_cos, m.rope_sin, m.max_seq_len,
-                         T, hq, hkv, dh, c, l, dt, s));
+    // q, k, v projection with RoPE and the cache write in the GEMM's epilogue
+    // (bf16 tensor-core shapes), else the projection and then rope_kv_write.
+    int rc = MS_ERR_UNSUPPORTED;
+    if (dt == MS_DTYPE_BF16) {
+      const RopeKv rk{bt.positions, bt.slot_mapping, m.rope_cos, m.rope_sin, m.max_seq_len, hq,
+                      hkv, dh, c.block_size, c.num_blocks,
+                      static_cast<__nv_bfloat16*>(c.k_pool[l]),
+                      static_cast<__nv_bfloat16*>(c.v_pool[l])};
+      rc = gemm_qkv_rope(w.xn, m.w_qkv[l], w.qkv, T, qkv_w, d, rk, s);
+    }
+    if (rc == MS_ERR_UNSUPPORTED) {
+      MS_TRY(gemm_dispatch(w.xn, m.w_qkv[l], w.qkv, nullptr, T, qkv_w, d, 0, dt, dt, kEpiStore, s));
+      MS_TRY(rope_kv_write(w.qkv, bt.positions, bt.slot_mapping, m.rope_cos, m.rope_sin,
+                           m.max_seq_len, T, hq, hkv, dh, c, l, dt, s));
+    } else {
+      MS_TRY(rc);
+    }
     // q occupies the first hq*dh columns of each qkv row.
     MS_TRY(paged_attention(w.qkv, qkv_w, c, l, bt, hq, w.attn, attn_scratch, attn_scratch_bytes,
                            s, order));

@@ -227,6 +227,92 @@ __device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const f
   }
 }
 
+// kEpiRopeKV: row m of a BN-column tile of the qkv projection.  Every head
+// lies inside one tile (dh divides BN and the tile start); the thread holds
+// the row, so the two halves of a head (columns j and j + dh/2) rotate
+// together.  Values are rounded to bf16 first and the rotation is the same
+// arithmetic as rope_kv_write's, so q and the cache get the bits the
+// separate kernels would write.  k and v go to the cache at the row's slot
+// (pool layout (num_blocks, kv heads, block_size, dh)).
+template <int BN>
+__device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0, const RopeKv& rk,
+                                            __nv_bfloat16* qkv, int64_t ldc, int* err) {
+  const int dh = rk.dh, half = dh >> 1;
+  const bool live = m < M;
+  int pos = 0, slot = -1;
+  if (live) {
+    pos = rk.positions[m];
+    if (pos < 0 || pos >= rk.max_pos) {
+      raise_device_error(err, kErrPosition);
+      pos = 0;
+    }
+    slot = rk.slots[m];
+  }
+  const int blk = slot >= 0 ? slot / rk.bs : 0, off = slot - blk * rk.bs;
+  const bool slot_ok = slot >= 0 && blk < rk.num_blocks;
+#pragma unroll 1
+  for (int hc = 0; hc < BN; hc += dh) {
+    const int head = (n0 + hc) / dh;
+#pragma unroll 1
+    for (int j = 0; j < half; j += 32) {
+      float a[32], b[32];
+      tmem_ld32(base + hc + j, a);
+      tmem_ld32(base + hc + half + j, b);
+      if (!live) continue;
+      uint32_t w1[16], w2[16];
+      __nv_bfloat16* dst;
+      if (head < rk.hq + rk.hkv) {
+        const float4* c4 = reinterpret_cast<const float4*>(rk.cos_t + (int64_t)pos * half + j);
+        const float4* s4 = reinterpret_cast<const float4*>(rk.sin_t + (int64_t)pos * half + j);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float4 cv = c4[i], sv = s4[i];
+          const float c[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
+          float r1[4], r2[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p = __bfloat162float(__float2bfloat16_rn(a[4 * i + e]));
+            const float q = __bfloat162float(__float2bfloat16_rn(b[4 * i + e]));
+            r1[e] = p * c[e] - q * sn[e];
+            r2[e] = q * c[e] + p * sn[e];
+          }
+          w1[2 * i] = pack_bf16(r1[0], r1[1]);
+          w1[2 * i + 1] = pack_bf16(r1[2], r1[3]);
+          w2[2 * i] = pack_bf16(r2[0], r2[1]);
+          w2[2 * i + 1] = pack_bf16(r2[2], r2[3]);
+        }
+        if (head < rk.hq) {
+          dst = qkv + (int64_t)m * ldc + n0 + hc + j;
+        } else {
+          if (!slot_ok) {
+            raise_device_error(err, kErrSlot);
+            continue;
+          }
+          dst = rk.kpool + (((int64_t)blk * rk.hkv + (head - rk.hq)) * rk.bs + off) * dh + j;
+        }
+      } else {
+        if (!slot_ok) {
+          raise_device_error(err, kErrSlot);
+          continue;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          w1[i] = pack_bf16(a[2 * i], a[2 * i + 1]);
+          w2[i] = pack_bf16(b[2 * i], b[2 * i + 1]);
+        }
+        dst = rk.vpool + (((int64_t)blk * rk.hkv + (head - rk.hq - rk.hkv)) * rk.bs + off) * dh + j;
+      }
+      uint4* d1 = reinterpret_cast<uint4*>(dst);
+      uint4* d2 = reinterpret_cast<uint4*>(dst + half);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        d1[i] = make_uint4(w1[4 * i], w1[4 * i + 1], w1[4 * i + 2], w1[4 * i + 3]);
+        d2[i] = make_uint4(w2[4 * i], w2[4 * i + 1], w2[4 * i + 2], w2[4 * i + 3]);
+      }
+    }
+  }
+}
+
 // The sequence of (tile, k-begin, k-end) pieces one CTA works on.  Every role
 // of the CTA walks the same sequence.
 struct Schedule {
@@ -270,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
                    const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
-                   int* err) {
+                   int* err, const RopeKv rk) {
   pdl_enter();
   using Cfg = TileCfg<BN>;
   constexpr int S = Cfg::kStages;
@@ -387,11 +473,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
       const int m = m0 + row_group * 32 + lane;
       const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
+      if constexpr (EPI == kEpiRopeKV) {
+        rope_kv_row<BN>(base, m, M, n0, rk, reinterpret_cast<__nv_bfloat16*>(C), ldc, err);
+      } else {
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld32(base + c, v);
-        if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(base + c, v);
+          if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
+        }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -477,7 +567,7 @@ int tensor_map(const void* ptr, int rows, int cols, int box_rows, CUtensorMap* o
 
 template <int BN, int EPI, typename TC>
 int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-              int64_t ldc, bool stream_k, cudaStream_t s) {
+              int64_t ldc, bool stream_k, cudaStream_t s, const RopeKv& rk = RopeKv{}) {
   CUtensorMap ta, tb;
   MS_TRY(tensor_map(A, M, K, BM, &ta));
   MS_TRY(tensor_map(B, N, K, BN, &tb));
@@ -499,7 +589,7 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
                       : std::min(tiles, kNumSMs);
   if (grid < 1) grid = 1;
   launch_pdl(kern, grid, kThreads, Cfg::kSmem, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-                                          stream_k ? 1 : 0, device_error_word());
+                                          stream_k ? 1 : 0, device_error_word(), rk);
   return check_launch("gemm_tc_kernel");
 }
 
@@ -520,6 +610,19 @@ int launch_any(const void* A, const void* B, void* C, const float* R, int M, int
 }
 
 }  // namespace
+
+int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, const RopeKv& rk,
+                  cudaStream_t s) {
+  if ((rk.dh != 64 && rk.dh != 128) || N != (rk.hq + 2 * rk.hkv) * rk.dh ||
+      !gemm_tc_supported(M, N, K, N, MS_DTYPE_BF16, kEpiStore) ||
+      ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) |
+        reinterpret_cast<uintptr_t>(qkv)) & 15))
+    return MS_ERR_UNSUPPORTED;
+  ProfScope prof(kClsGemm, s);
+  if (use_bn256(M, N, false))
+    return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk);
+  return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk);
+}
 
 bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi) {
   if (M <= 0 || K % 8 != 0 || N % 128 != 0) return false;

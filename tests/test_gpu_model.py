@@ -236,3 +236,54 @@ def test_device_error_word_flags_bad_slots() -> None:
     cache.write(0, torch.tensor([5, 10_000]), torch.ones(2, 4, 8), torch.ones(2, 4, 8))
     assert _lib.device_error() == 1  # kErrSlot
     assert _lib.device_error() == 0  # read clears it
+
+
+@pytest.mark.parametrize("dh", [64, 128])
+def test_fused_qkv_rope_writes_the_cache(dh: int) -> None:
+    """The bf16 qkv projection applies RoPE and writes k, v to the cache in its
+    epilogue: layer 0's cached k and v against torch (projection of the
+    normalised, bf16-rounded embeddings, rounded to bf16, k rotated with the
+    model's tables and rounded again).  The rotated q reaches the logits, which
+    the oracle tests check."""
+    from microserve_b200.batching import build_paged_batch
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    hq, hkv = 8, 2
+    cfg = ModelConfig(vocab_size=300, n_layers=1, d_model=hq * dh, n_heads=hq, n_kv_heads=hkv,
+                      d_ff=256, max_seq_len=512, dtype="bfloat16")
+    m = Transformer(cfg, DEV, seed=11)
+    cache = new_cache(m, 16, 64)
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 300, int(n)).tolist() for n in (70, 150, 3)]
+    starts = [0, 0, 0]
+    batch = build_paged_batch(cache, [0, 1, 2], prompts, starts)
+    m.forward_paged(batch, cache)
+    torch.cuda.synchronize()
+
+    ids = torch.tensor([t for p in prompts for t in p], device=DEV)
+    pos = torch.cat([torch.arange(len(p), device=DEV) for p in prompts])
+    x = m.embed[ids].float()
+    xn = (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.norm_eps)).bfloat16().float()
+    qkv = (xn @ m.w_qkv[0].float().T).bfloat16().float()
+    half = dh // 2
+    c, s = m.rope_cos[pos].float(), m.rope_sin[pos].float()
+
+    def rope(t: torch.Tensor) -> torch.Tensor:  # (T, heads, dh)
+        a, b = t[..., :half], t[..., half:]
+        return torch.cat([a * c[:, None] - b * s[:, None], b * c[:, None] + a * s[:, None]], -1)
+
+    T = ids.numel()
+    k = rope(qkv[:, hq * dh : (hq + hkv) * dh].view(T, hkv, dh)).bfloat16().float()
+    v = qkv[:, (hq + hkv) * dh :].view(T, hkv, dh)
+    slots = batch.slot_mapping.long()
+    blk, off = slots // 16, slots % 16
+    got_k = cache.pool[0, 0][blk, :, off].float()  # (T, hkv, dh)
+    got_v = cache.pool[1, 0][blk, :, off].float()
+    # two bf16 roundings around the rotation: where x1*c - x2*s cancels, one
+    # ulp of the inputs (different accumulation orders) is a few ulps of k
+    torch.testing.assert_close(got_k, k, rtol=1.6e-2, atol=4e-3 * k.abs().max().item())
+    torch.testing.assert_close(got_v, v, rtol=1.6e-2, atol=2e-3 * v.abs().max().item())
+    from microserve_b200 import _lib
+
+    assert _lib.device_error() == 0
