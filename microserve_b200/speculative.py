@@ -219,8 +219,12 @@ class SpeculativeDecoder:
         npre = n_tok - t_cached
         if np.any(npre < 1):
             raise ValueError("every request needs at least one uncomputed token")
-        pending = _tails(requests, n0)
-        prefix = _tails(requests, npre)
+        # One walk over the token lists: the longer of the two suffixes, split
+        # into the draft's catch-up tokens and the target's uncomputed ones.
+        kmax = np.maximum(n0, npre)
+        tails = np.fromiter(itertools.chain.from_iterable(_tails(requests, kmax)), np.int32,
+                            int(kmax.sum()))
+        tail_end = np.cumsum(kmax)
 
         # Slots for the whole round, reserved up front (all-or-nothing).
         dslots = dcache.append_many(ids, n0 + (G - 1))
@@ -236,7 +240,7 @@ class SpeculativeDecoder:
         T0 = int(q0[-1])
         seg0 = np.repeat(np.arange(B), n0)
         within0 = np.arange(T0) - q0[:-1][seg0]
-        ids0 = np.fromiter(itertools.chain.from_iterable(pending), np.int32, T0)
+        ids0 = tails[tail_end[seg0] - n0[seg0] + within0]
         pos0 = d_cached[seg0] + within0
         slots0 = dslots[dstart[:-1][seg0] + within0]
         ctx0 = d_cached + n0
@@ -256,8 +260,8 @@ class SpeculativeDecoder:
         withinv = np.arange(Tv) - qv[:-1][segv]
         idsv = np.zeros(Tv, np.int32)
         is_prefix = withinv < npre[segv]
-        idsv[is_prefix] = np.fromiter(itertools.chain.from_iterable(prefix), np.int32,
-                                      int(npre.sum()))
+        segp = segv[is_prefix]
+        idsv[is_prefix] = tails[tail_end[segp] - npre[segp] + withinv[is_prefix]]
         posv = t_cached[segv] + withinv
         ctxv = t_cached + npre + G
         rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
