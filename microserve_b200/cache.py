@@ -272,6 +272,19 @@ class PagedKVCache:
         needed = (ntok + num_new_tokens + self.block_size - 1) // self.block_size
         return max(0, needed - nblk)
 
+    def blocks_needed_many(self, seq_ids: Sequence[int], counts: Sequence[int] | np.ndarray) -> int:
+        """Total extra blocks ``append_many(seq_ids, counts)`` would take (no change)."""
+        counts = np.asarray(counts, dtype=np.int64)
+        get = self._rows.get
+        rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
+        known = rows >= 0
+        ntok = np.zeros(len(rows), np.int64)
+        nblk = np.zeros(len(rows), np.int64)
+        ntok[known] = self._ntok[rows[known]]
+        nblk[known] = self._nblk[rows[known]]
+        need = (ntok + counts + self.block_size - 1) // self.block_size - nblk
+        return int(np.maximum(need, 0).sum())
+
     def can_append(self, seq_id: int, num_new_tokens: int) -> bool:
         return self.blocks_needed(seq_id, num_new_tokens) <= self.allocator.num_free
 

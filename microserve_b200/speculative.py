@@ -34,7 +34,7 @@ import torch
 
 from . import _lib
 from .batching import HostStaging, batch_from_host, pack_int32
-from .cache import PagedKVCache
+from .cache import OutOfCacheMemory, PagedKVCache
 from .config import CacheConfig, SamplingConfig
 from .model import PagedBatch, Transformer
 from .sampling import generator_seed_and_step, make_params, validate
@@ -163,6 +163,7 @@ class SpeculativeDecoder:
         self.num_proposed = 0
         self.num_accepted = 0
         self._staging = HostStaging(self.device)
+        self._staging_v = HostStaging(self.device)  # the verify batch's blob (phase B)
         self._buf = _Buffers(self.device)
         self.last_round_launches = 0
         # Measurement hooks (set by benchmarks): when ``round_events`` is a
@@ -208,7 +209,12 @@ class SpeculativeDecoder:
         target_cache: PagedKVCache,
         generators: dict[int, torch.Generator],
     ) -> dict[str, object]:
-        """Reserve every slot of the round and pack its metadata into one blob."""
+        """What the draft passes need, packed into one blob (phase A).
+
+        The round stays all-or-nothing: the target cache's room for the round
+        is checked here, before the draft cache reserves anything, and its
+        slots are taken in :meth:`_plan_verify` while the draft passes run.
+        """
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
         dcache = self.draft_cache
@@ -219,6 +225,9 @@ class SpeculativeDecoder:
         npre = n_tok - t_cached
         if np.any(npre < 1):
             raise ValueError("every request needs at least one uncomputed token")
+        need = target_cache.blocks_needed_many(ids, npre + G)
+        if need > target_cache.num_free_blocks:
+            raise OutOfCacheMemory(f"need {need} blocks, {target_cache.num_free_blocks} free")
         # One walk over the token lists: the longer of the two suffixes, split
         # into the draft's catch-up tokens and the target's uncomputed ones.
         kmax = np.maximum(n0, npre)
@@ -226,11 +235,9 @@ class SpeculativeDecoder:
                             int(kmax.sum()))
         tail_end = np.cumsum(kmax)
 
-        # Slots for the whole round, reserved up front (all-or-nothing).
+        # The draft's slots for the whole round (all-or-nothing).
         dslots = dcache.append_many(ids, n0 + (G - 1))
-        tslots = target_cache.append_many(ids, npre + G)
         dtab, _, dw = dcache.table_rows(ids)
-        ttab, _, tw = target_cache.table_rows(ids)
 
         # Draft pass 0: the catch-up tokens (usually 1 or 2 per request).
         dstart = np.zeros(B + 1, np.int64)
@@ -252,7 +259,8 @@ class SpeculativeDecoder:
         slots_j = [dslots[dstart[:-1] + n0 + j - 1] for j in range(1, G)]
         ctx_j = [d_cached + n0 + j for j in range(1, G)]
 
-        # Target verify: [uncached tokens] + G proposals per request.
+        # Target verify tokens: [uncached tokens] + G proposals per request;
+        # the draft samplers write the proposals into their places.
         qv = np.zeros(B + 1, np.int64)
         np.cumsum(npre + G, out=qv[1:])
         Tv = int(qv[-1])
@@ -262,41 +270,54 @@ class SpeculativeDecoder:
         is_prefix = withinv < npre[segv]
         segp = segv[is_prefix]
         idsv[is_prefix] = tails[tail_end[segp] - npre[segp] + withinv[is_prefix]]
-        posv = t_cached[segv] + withinv
-        ctxv = t_cached + npre + G
-        rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
         scat = [qv[:-1] + npre + j for j in range(G)]
 
         seeds = [generators[i].initial_seed() for i in ids]
         steps = [r.rng_step for r in requests]
         params = make_params([r.sampling for r in requests], seeds, steps)
-        params_n_tok = n_tok
-        pwords = params.view(np.int32)
 
         parts = [
-            pwords,
+            params.view(np.int32),
             # draft pass 0 batch (order matches batch_from_host)
             ids0, pos0, slots0, q0, ctx0, n0, dtab,
             rows0,
             # shared unit batch arrays for passes >= 1
             unit_qs, ones,
             *[a for j in range(G - 1) for a in (pos_j[j], slots_j[j], ctx_j[j])],
-            # verify batch
-            idsv, posv, tslots, qv, ctxv, npre + G, ttab,
-            rowsv,
+            # verify token ids and where each draft pass's proposals go
+            idsv,
             *scat,
         ]
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
         return {
-            "blob": blob, "spans": spans, "B": B, "dw": dw, "tw": tw, "T0": T0, "Tv": Tv,
+            "blob": blob, "spans": spans, "B": B, "dw": dw, "T0": T0, "Tv": Tv,
             "max_q0": int(n0.max()), "max_qv": int((npre + G).max()),
-            "ctx0": int(ctx0.max()), "ctxv": int(ctxv.max()),
-            "ctx_j": [int(c.max()) for c in ctx_j],
+            "ctx0": int(ctx0.max()), "ctx_j": [int(c.max()) for c in ctx_j],
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
-            "n_tok": params_n_tok,
-            "kv_verify": int(ctxv.sum()),
+            "n_tok": n_tok, "qv": qv, "segv": segv, "withinv": withinv,
             "kv_draft": int(ctx0.sum()) + sum(int(c.sum()) for c in ctx_j),
         }
+
+    def _plan_verify(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
+        """Phase B, run on the host while the draft passes execute: the target
+        cache's slots (room checked in :meth:`_plan`) and the verify batch's
+        metadata, packed into a second blob."""
+        G = self.gamma
+        ids: list[int] = plan["ids"]  # type: ignore[assignment]
+        npre: np.ndarray = plan["npre"]  # type: ignore[assignment]
+        t_cached: np.ndarray = plan["t_cached"]  # type: ignore[assignment]
+        qv: np.ndarray = plan["qv"]  # type: ignore[assignment]
+        segv: np.ndarray = plan["segv"]  # type: ignore[assignment]
+        withinv: np.ndarray = plan["withinv"]  # type: ignore[assignment]
+        tslots = target_cache.append_many(ids, npre + G)
+        ttab, _, tw = target_cache.table_rows(ids)
+        posv = t_cached[segv] + withinv
+        ctxv = t_cached + npre + G
+        rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
+        parts = [posv, tslots, qv, ctxv, npre + G, ttab, rowsv]
+        blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
+        plan.update(blob_v=blob, spans_v=spans, tw=tw, ctxv=int(ctxv.max()),
+                    kv_verify=int(ctxv.sum()))
 
     def _launch(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
         G, V = self.gamma, self.target.cfg.vocab_size
@@ -327,19 +348,9 @@ class SpeculativeDecoder:
                 n_tokens=B, max_context=plan["ctx_j"][j - 1],  # type: ignore[index]
             )
             batches.append((bj, None))
-        bv = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["tw"]), int(plan["max_qv"]),
-                             int(plan["Tv"]), int(plan["ctxv"]))  # type: ignore[arg-type]
-        k += 7
-        rowsv = v[k]
+        idsv = v[k]
         k += 1
         scat = v[k : k + G]
-        self.last_round_shape = {"B": B, "T0": int(plan["T0"]), "Tv": int(plan["Tv"]),  # type: ignore[arg-type]
-                                 "gamma": G,
-                                 # keys each pass's attention reads, summed over requests
-                                 "kv_tokens_verify": int(plan["kv_verify"]),  # type: ignore[arg-type]
-                                 "kv_tokens_draft": int(plan["kv_draft"])}  # type: ignore[arg-type]
-        self.last_h2d_bytes = int(plan["blob"].nbytes)  # type: ignore[union-attr]
-        self.last_d2h_bytes = B * (G + 2) * 4
         ev = None
         if self.round_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -352,8 +363,26 @@ class SpeculativeDecoder:
             _lib.call(
                 "ms_sample", out.data_ptr(), V, B, V, params.data_ptr(), None, _lib.LANE_DRAFT + j,
                 buf.proposals[j].data_ptr(), None, buf.dstats[j].data_ptr(),
-                bv.input_ids.data_ptr(), scat[j].data_ptr(), stream,
+                idsv.data_ptr(), scat[j].data_ptr(), stream,
             )
+        # The target side is planned while the draft passes run on the GPU.
+        self._plan_verify(plan, target_cache)
+        vblob = self._staging_v.upload(plan["blob_v"])  # type: ignore[arg-type]
+        w = [vblob[o : o + n] for o, n in plan["spans_v"]]  # type: ignore[union-attr]
+        tw = int(plan["tw"])  # type: ignore[arg-type]
+        bv = PagedBatch(
+            input_ids=idsv, positions=w[0], slot_mapping=w[1], q_start=w[2], context_lens=w[3],
+            q_lens=w[4], block_tables=w[5].view(B, tw), max_q=int(plan["max_qv"]),  # type: ignore[arg-type]
+            n_tokens=int(plan["Tv"]), max_context=int(plan["ctxv"]),  # type: ignore[arg-type]
+        )
+        rowsv = w[6]
+        self.last_round_shape = {"B": B, "T0": int(plan["T0"]), "Tv": int(plan["Tv"]),  # type: ignore[arg-type]
+                                 "gamma": G,
+                                 # keys each pass's attention reads, summed over requests
+                                 "kv_tokens_verify": int(plan["kv_verify"]),  # type: ignore[arg-type]
+                                 "kv_tokens_draft": int(plan["kv_draft"])}  # type: ignore[arg-type]
+        self.last_h2d_bytes = int(plan["blob"].nbytes) + int(plan["blob_v"].nbytes)  # type: ignore[union-attr]
+        self.last_d2h_bytes = B * (G + 2) * 4
         vev = None
         if self.verify_events is not None:
             vev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))

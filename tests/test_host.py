@@ -127,6 +127,20 @@ class TestCacheTables:
         assert c.num_tokens(0) == 4
         assert c.num_free_blocks == 2
 
+    def test_blocks_needed_many_predicts_append_many(self) -> None:
+        rng = np.random.default_rng(1)
+        c = host_cache(4, 256)
+        ids = [5, 2, 9, 11]
+        c.append(2, 3)
+        for _ in range(8):
+            counts = rng.integers(0, 9, len(ids))
+            free = c.num_free_blocks
+            need = c.blocks_needed_many(ids, counts)
+            assert need == sum(c.blocks_needed(i, int(n)) for i, n in zip(ids, counts))
+            c.append_many(ids, counts)
+            assert free - c.num_free_blocks == need
+            c.truncate_many(ids, [max(0, c.num_tokens(i) - int(rng.integers(0, 6))) for i in ids])
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
