@@ -250,11 +250,30 @@ __device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0,
   }
   const int blk = slot >= 0 ? slot / rk.bs : 0, off = slot - blk * rk.bs;
   const bool slot_ok = slot >= 0 && blk < rk.num_blocks;
+  // Columns j .. j+31 of every head's halves share the row's cos/sin: load
+  // them once per j, then walk the tile's heads.
 #pragma unroll 1
-  for (int hc = 0; hc < BN; hc += dh) {
-    const int head = (n0 + hc) / dh;
+  for (int j = 0; j < half; j += 32) {
+    float cs[32], sn[32];
+    if (live) {
+      const float4* c4 = reinterpret_cast<const float4*>(rk.cos_t + (int64_t)pos * half + j);
+      const float4* s4 = reinterpret_cast<const float4*>(rk.sin_t + (int64_t)pos * half + j);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 cv = c4[i], sv = s4[i];
+        cs[4 * i] = cv.x;
+        cs[4 * i + 1] = cv.y;
+        cs[4 * i + 2] = cv.z;
+        cs[4 * i + 3] = cv.w;
+        sn[4 * i] = sv.x;
+        sn[4 * i + 1] = sv.y;
+        sn[4 * i + 2] = sv.z;
+        sn[4 * i + 3] = sv.w;
+      }
+    }
 #pragma unroll 1
-    for (int j = 0; j < half; j += 32) {
+    for (int hc = 0; hc < BN; hc += dh) {
+      const int head = (n0 + hc) / dh;
       float a[32], b[32];
       tmem_ld32(base + hc + j, a);
       tmem_ld32(base + hc + half + j, b);
@@ -262,24 +281,19 @@ __device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0,
       uint32_t w1[16], w2[16];
       __nv_bfloat16* dst;
       if (head < rk.hq + rk.hkv) {
-        const float4* c4 = reinterpret_cast<const float4*>(rk.cos_t + (int64_t)pos * half + j);
-        const float4* s4 = reinterpret_cast<const float4*>(rk.sin_t + (int64_t)pos * half + j);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float4 cv = c4[i], sv = s4[i];
-          const float c[4] = {cv.x, cv.y, cv.z, cv.w}, sn[4] = {sv.x, sv.y, sv.z, sv.w};
-          float r1[4], r2[4];
+        for (int i = 0; i < 16; ++i) {
+          float r1[2], r2[2];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p = __bfloat162float(__float2bfloat16_rn(a[4 * i + e]));
-            const float q = __bfloat162float(__float2bfloat16_rn(b[4 * i + e]));
-            r1[e] = p * c[e] - q * sn[e];
-            r2[e] = q * c[e] + p * sn[e];
+          for (int e = 0; e < 2; ++e) {
+            const int k = 2 * i + e;
+            const float p = __bfloat162float(__float2bfloat16_rn(a[k]));
+            const float q = __bfloat162float(__float2bfloat16_rn(b[k]));
+            r1[e] = p * cs[k] - q * sn[k];
+            r2[e] = q * cs[k] + p * sn[k];
           }
-          w1[2 * i] = pack_bf16(r1[0], r1[1]);
-          w1[2 * i + 1] = pack_bf16(r1[2], r1[3]);
-          w2[2 * i] = pack_bf16(r2[0], r2[1]);
-          w2[2 * i + 1] = pack_bf16(r2[2], r2[3]);
+          w1[i] = pack_bf16(r1[0], r1[1]);
+          w2[i] = pack_bf16(r2[0], r2[1]);
         }
         if (head < rk.hq) {
           dst = qkv + (int64_t)m * ldc + n0 + hc + j;
