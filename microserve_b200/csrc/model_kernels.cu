@@ -110,6 +110,74 @@ __global__ void embed_rmsnorm_kernel(const TW* __restrict__ embed, const int32_t
   for (int i = lane; i < dim; i += 32) yr[i] = from_f<TW>(to_f(er[i]) * r * w[i]);
 }
 
+// bf16 rows with dim % 256 == 0 (<= 4096): one warp per token, 16-byte
+// loads, the row kept in registers between the sum of squares and the
+// scaled write (one read of the embedding row).
+constexpr int kEmbedChunks = 16;  // 8-element chunks per lane: dim <= 32 * 8 * 16
+constexpr int kEmbedWarps = 4;
+__global__ void __launch_bounds__(kEmbedWarps * 32)
+    embed_rmsnorm_vec_kernel(const __nv_bfloat16* __restrict__ embed,
+                             const int32_t* __restrict__ ids, int n_tokens, int vocab, int dim,
+                             const float* __restrict__ w, float eps, float* __restrict__ x,
+                             __nv_bfloat16* __restrict__ y, int* __restrict__ err) {
+  pdl_enter();
+  const int tok = blockIdx.x * kEmbedWarps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (tok >= n_tokens) return;
+  int id = ids[tok];
+  if (id < 0 || id >= vocab) {
+    if (lane == 0) raise_device_error(err, kErrToken);
+    id = 0;
+  }
+  const uint4* er = reinterpret_cast<const uint4*>(embed + (int64_t)id * dim);
+  const int nc = dim >> 8;
+  uint4 raw[kEmbedChunks];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kEmbedChunks; ++c) {
+    if (c < nc) {
+      raw[c] = er[c * 32 + lane];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+      }
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = 1.f / sqrtf(ss / (float)dim + eps);
+  float4* xr = reinterpret_cast<float4*>(x + (int64_t)tok * dim);
+  uint4* yr = reinterpret_cast<uint4*>(y + (int64_t)tok * dim);
+  const float4* wr = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int c = 0; c < kEmbedChunks; ++c) {
+    if (c < nc) {
+      const int q = c * 32 + lane;  // chunk of 8 elements
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[c]);
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+      }
+      xr[2 * q] = make_float4(v[0], v[1], v[2], v[3]);
+      xr[2 * q + 1] = make_float4(v[4], v[5], v[6], v[7]);
+      const float4 g0 = wr[2 * q], g1 = wr[2 * q + 1];
+      const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat162 b =
+            __floats2bfloat162_rn(v[2 * e] * r * g[2 * e], v[2 * e + 1] * r * g[2 * e + 1]);
+        o[e] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+      yr[q] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 __device__ __forceinline__ int64_t pool_offset(int slot, int g, int d, int bs, int hkv, int dh,
                                                int num_blocks, bool& ok) {
   const int blk = slot / bs, off = slot - blk * bs;
@@ -332,6 +400,14 @@ int embed_rmsnorm(const void* embed, const int32_t* ids, int n_tokens, int vocab
                   const float* w, float eps, float* x, void* y, int dtype, cudaStream_t s) {
   if (n_tokens == 0) return MS_OK;
   ProfScope prof(kClsNorm, s);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(embed) | reinterpret_cast<uintptr_t>(w) |
+                         reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  if (dtype == MS_DTYPE_BF16 && aligned && dim % 256 == 0 && dim <= 32 * 8 * kEmbedChunks) {
+    launch_pdl(embed_rmsnorm_vec_kernel, ceil_div(n_tokens, kEmbedWarps), kEmbedWarps * 32, 0, s,
+               static_cast<const __nv_bfloat16*>(embed), ids, n_tokens, vocab, dim, w, eps, x,
+               static_cast<__nv_bfloat16*>(y), device_error_word());
+    return check_launch("embed_rmsnorm_vec_kernel");
+  }
   const int blocks = ceil_div(n_tokens, 8);
   if (dtype == MS_DTYPE_F32)
     launch_pdl(embed_rmsnorm_kernel<float>, blocks, 256, 0, s, static_cast<const float*>(embed), ids,
