@@ -51,6 +51,16 @@ TARGET = dict(vocab_size=32000, n_layers=22, d_model=2048, n_heads=32, n_kv_head
 DRAFT = dict(TARGET, n_layers=2)
 GAMMA = 4
 BLOCK = 16
+MAX_SEQ = 4096
+CTX_LOGNORMAL: tuple[float, float] | None = None  # (mean, std) of the context lengths
+
+# --model 8b: the 8B-class workload (a Llama-3-8B-shape target with a 1B-class
+# draft, 2048 requests over 8 GPUs = 256 per GPU, contexts lognormal with mean
+# 2048 and std 1024 clipped to [8, 8192], gamma 5).  Not the headline metric.
+TARGET_8B = dict(vocab_size=128256, n_layers=32, d_model=4096, n_heads=32, n_kv_heads=8,
+                 d_ff=14336, rope_theta=500000.0)
+DRAFT_8B = dict(vocab_size=128256, n_layers=16, d_model=2048, n_heads=32, n_kv_heads=8,
+                d_ff=8192, rope_theta=500000.0)
 
 
 def parse() -> argparse.Namespace:
@@ -67,6 +77,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
+    ap.add_argument("--model", choices=["1b", "8b"], default="1b",
+                    help="8b: the 8B-target workload instead of the headline 1.1B one")
     ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention", "accept", "engine"],
                     default=None,
                     help="time one kernel family alone (1 GPU) instead of the speculative round")
@@ -84,13 +96,19 @@ def model_cfgs(small: bool):
     if small:
         t.update(n_layers=2)
         d.update(n_layers=1)
-    msl = 4096
+    msl = MAX_SEQ
     return (ModelConfig(**t, max_seq_len=msl, dtype="bfloat16"),
             ModelConfig(**d, max_seq_len=msl, dtype="bfloat16"))
 
 
 def contexts(n: int, lo: int, hi: int, seed: int) -> np.ndarray:
-    return np.random.default_rng(seed).integers(lo, hi + 1, n)
+    rng = np.random.default_rng(seed)
+    if CTX_LOGNORMAL is not None:  # lognormal with the given mean and std, clipped
+        mean, std = CTX_LOGNORMAL
+        sig2 = np.log(1.0 + (std / mean) ** 2)
+        x = rng.lognormal(np.log(mean) - sig2 / 2, np.sqrt(sig2), n)
+        return np.clip(x, lo, hi).astype(np.int64)
+    return rng.integers(lo, hi + 1, n)
 
 
 # -- clocks during the timed region ------------------------------------------------
@@ -303,7 +321,8 @@ def run_gpu(args: argparse.Namespace) -> None:
             "ctx_range": [args.ctx_min, args.ctx_max],
             "target": TARGET if not args.small else dict(TARGET, n_layers=2),
             "draft_layers": dcfg.n_layers, "temperature": 0.8, "top_p": 0.9,
-            "l2": "inputs larger than L2 (2.1 GB target weights + ~7 GB of K/V read per round)",
+            "l2": f"inputs larger than L2 ({target.weight_bytes() / 1e9:.1f} GB target weights + "
+                  f"{kv_bytes / attn_rounds / 1e9:.1f} GB of K/V read per round)",
             "parallelism": f"request-sharded x{info.world_size}, no decode-loop collective",
         },
         "acceptance_rate": tot["accepted"] / max(1, tot["proposed"]),
@@ -739,8 +758,24 @@ def run_micro(args: argparse.Namespace) -> None:
                       "device_error": _lib.device_error()}), flush=True)
 
 
+def use_8b(args: argparse.Namespace) -> None:
+    """Switch the module's workload constants to the 8B-class configuration."""
+    global TARGET, DRAFT, GAMMA, MAX_SEQ, CTX_LOGNORMAL, METRIC, WORKLOAD
+    TARGET, DRAFT, GAMMA, MAX_SEQ = dict(TARGET_8B), dict(DRAFT_8B), 5, 8192 + 512
+    CTX_LOGNORMAL = (2048.0, 1024.0)
+    args.ctx_min, args.ctx_max = 8, 8192
+    METRIC = "accepted tok/s per B200 (spec γ=5, 8B target)"
+    WORKLOAD = ("llama-3-8b-shape bf16 target + 1b-class 16-layer draft, 256 req/GPU, "
+                "ctx lognormal(2048, 1024) in [8, 8192], gamma 5, T 0.8, top-p 0.9")
+    args.no_cpu_baseline = True  # the CPU restatement of an 8B model is out of reach
+
+
 def main() -> None:
     args = parse()
+    if args.model == "8b":
+        if args.impl == "reference" or args.micro:
+            raise SystemExit("--model 8b runs the speculative rounds on the GPU only")
+        use_8b(args)
     if args.micro:
         run_micro(args)
     elif args.impl == "reference":
