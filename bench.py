@@ -79,7 +79,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
     ap.add_argument("--model", choices=["1b", "8b"], default="1b",
                     help="8b: the 8B-target workload instead of the headline 1.1B one")
-    ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention", "accept", "engine"],
+    ap.add_argument("--micro", choices=["gemm8b", "gemm1b", "attention", "accept", "engine",
+                                        "sample"],
                     default=None,
                     help="time one kernel family alone (1 GPU) instead of the speculative round")
     ap.add_argument("--only", default=None, help="--micro gemm8b: one shape (qkv, o_proj, ...)")
@@ -649,6 +650,39 @@ def run_micro_engine(args: argparse.Namespace) -> None:
             del eng
 
 
+def run_micro_sample(args: argparse.Namespace) -> None:
+    """One ms_sample launch over 256 rows (a draft pass's draws) at vocab
+    32000 (the 1.1B model) and 128256 (the 8B one): logits N(0, 1.3^2),
+    temperature 0.8, top-p 0.9 and no filter."""
+    import torch
+
+    from microserve_b200 import _lib
+    from microserve_b200.sampling import params_to_device
+
+    B = args.requests
+    gen = torch.Generator(device="cuda").manual_seed(args.seed)
+    for V in (32000, 128256):
+        logits = torch.randn(B, V, device="cuda", generator=gen) * 1.3
+        tokens = torch.empty(B, dtype=torch.int32, device="cuda")
+        for top_p in (0.9, 1.0):
+            p = np.zeros(B, dtype=_lib.SAMPLING_PARAMS_DTYPE)
+            p["temperature"] = 0.8
+            p["top_p"] = top_p
+            p["seed"] = 7
+            p["step"] = np.arange(B, dtype=np.uint64)
+            params = params_to_device(p, torch.device("cuda"))
+
+            def call() -> None:
+                _lib.call("ms_sample", logits.data_ptr(), V, B, V, params.data_ptr(), None, 0,
+                          tokens.data_ptr(), None, None, None, None, _lib.stream_ptr())
+
+            us = _time_launches(call, args.iters)
+            print(json.dumps({"micro": "sample", "rows": B, "vocab": V, "temperature": 0.8,
+                              "top_p": top_p, "us": us, "gbs": B * V * 4 / us / 1e3,
+                              "device_error": _lib.device_error()}), flush=True)
+        del logits
+
+
 def run_micro(args: argparse.Namespace) -> None:
     import ctypes
 
@@ -715,6 +749,9 @@ def run_micro(args: argparse.Namespace) -> None:
         return
     if args.micro == "engine":
         run_micro_engine(args)
+        return
+    if args.micro == "sample":
+        run_micro_sample(args)
         return
     # attention: the config-3 verify (qlen 5) or draft (qlen 1) pass of one layer
     from microserve_b200.batching import build_paged_batch

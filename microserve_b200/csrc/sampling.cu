@@ -15,10 +15,14 @@
 #include <cfloat>
 #include <cmath>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace ms {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr int kMaxStagedV = 40960;  // 160 KB of float32 in shared memory
 constexpr int kHistBins = 256;
@@ -609,30 +613,37 @@ __device__ void row_stats(Dist& dref, int V, int top_k, float top_p, RowSmem& sm
 //
 // Warp w owns a contiguous segment of the row, walked in chunks of 4 * 32
 // elements (element c0 + 32k + lane in slot k of a lane, so loads are
-// conflict-free).  Pass 1: each lane sums its elements, one butterfly gives
-// the warp's total, and a block scan places the warps.  Pass 2: only the
-// warp holding the target re-walks its segment, skipping whole chunks by
-// their totals, and scans inside the one chunk that crosses.
-template <typename W>
-__device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+// conflict-free).  Pass 1 (cdf_totals): each lane sums its elements, one
+// butterfly gives the warp's total, kept in red_d[warp] with the warp's last
+// positive index in red_i[warp].  Pass 2 (cdf_search): only the warp holding
+// the target re-walks its segment, skipping whole chunks by their totals, and
+// scans inside the one chunk that crosses.  The two passes are separate so a
+// cluster can place the target between them.
+__device__ __forceinline__ void cdf_segment(int V, int& s0, int& s1) {
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   int seg = (V + nw - 1) / nw;
   seg = (seg + 127) & ~127;
-  const int s0 = min(V, warp * seg), s1 = min(V, s0 + seg);
-  auto chunk = [&](int c0, float (&v)[4]) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int i = c0 + 32 * k + lane;
-      v[k] = i < s1 ? w(i) : 0.f;
-    }
-  };
-  // pass 1: lane sums (four independent chunks at a time), one butterfly
+  s0 = min(V, warp * seg);
+  s1 = min(V, s0 + seg);
+}
+
+// Pass 1: returns the total weight and the last positive index (-1: none).
+template <typename W>
+__device__ void cdf_totals(const W& w, int V, RowSmem& sm, double& total, int& glast) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int s0, s1;
+  cdf_segment(V, s0, s1);
   float lsum = 0.f;
   int last = -1;
   for (int c0 = s0; c0 < s1; c0 += 4 * 128) {
     float v[4][4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) chunk(c0 + 128 * q, v[q]);
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = c0 + 128 * q + 32 * k + lane;
+        v[q][k] = i < s1 ? w(i) : 0.f;
+      }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       lsum += (v[q][0] + v[q][1]) + (v[q][2] + v[q][3]);
@@ -643,28 +654,44 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-  const double wtot = (double)lsum;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) last = max(last, __shfl_xor_sync(0xffffffffu, last, o));
   __syncthreads();  // earlier users of red_* are done
   if (lane == 0) {
-    sm.red_d[warp] = wtot;
+    sm.red_d[warp] = (double)lsum;
     sm.red_i[warp] = last;
   }
   if (threadIdx.x == 0) sm.red_i[40] = -1;
   __syncthreads();
-  double before = 0.0, total = 0.0;
-  int glast = -1;
+  total = 0.0;
+  glast = -1;
   for (int k = 0; k < nw; ++k) {
-    const double t = sm.red_d[k];
-    if (k < warp) before += t;
-    total += t;
+    total += sm.red_d[k];
     glast = max(glast, sm.red_i[k]);
   }
-  const double target = (double)u * total;
+}
+
+// Pass 2, after cdf_totals with nothing in between touching red_*: the index
+// where the running sum, starting at `base`, first exceeds `target`; the
+// crossing warp's last positive index when rounding finds none inside it; -1
+// when the target lies in no warp's range.
+template <typename W>
+__device__ int cdf_search(const W& w, int V, double base, double target, RowSmem& sm) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int s0, s1;
+  cdf_segment(V, s0, s1);
+  auto chunk = [&](int c0, float (&v)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = c0 + 32 * k + lane;
+      v[k] = i < s1 ? w(i) : 0.f;
+    }
+  };
+  double before = base;
+  for (int k = 0; k < warp; ++k) before += sm.red_d[k];
+  const double wtot = sm.red_d[warp];
+  const int last = sm.red_i[warp];
   if (wtot > 0.0 && before <= target && target < before + wtot) {
-    // pass 2 (the target's warp): chunk totals four at a time, skip whole
-    // chunks, scan inside the one that crosses
     double run = before;
     int found = last;  // rounding: the segment's last positive weight
     bool done = false;
@@ -713,10 +740,19 @@ __device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
     if (lane == 0) sm.red_i[40] = found;
   }
   __syncthreads();
-  int res = sm.red_i[40];
+  const int res = sm.red_i[40];
+  __syncthreads();
+  return res;
+}
+
+template <typename W>
+__device__ int inverse_cdf(const W& w, int V, float u, RowSmem& sm) {
+  double total;
+  int glast;
+  cdf_totals(w, V, sm, total, glast);
+  int res = cdf_search(w, V, 0.0, (double)u * total, sm);
   if (res < 0) res = glast;
   if (res < 0) res = 0;
-  __syncthreads();
   return res;
 }
 
@@ -828,17 +864,32 @@ __device__ bool load_logits(Dist& d, const float* row, int V, float temp, RowSme
 }
 
 // ---- K8: one draw per row ----------------------------------------------------
-__global__ void __launch_bounds__(512, 1) sample_rows_kernel(const float* __restrict__ logits, int64_t stride, int V,
-                                   const ms_sampling_params* __restrict__ params,
-                                   const int32_t* __restrict__ pidx, uint32_t lane_id,
-                                   int32_t* __restrict__ tokens, float* __restrict__ probs,
-                                   ms_row_stats* __restrict__ stats, int32_t* scatter_dst,
-                                   const int32_t* __restrict__ scatter_idx, int stage) {
-  pdl_enter();
-  RowSmem sm;
-  setup_smem(sm, V, stage != 0);
-  const int r = blockIdx.x;
-  const ms_sampling_params P = params[pidx ? pidx[r] : r];
+struct SampleArgs {
+  const float* logits;
+  int64_t stride;
+  int V;
+  const ms_sampling_params* params;
+  const int32_t* pidx;
+  uint32_t lane_id;
+  int32_t* tokens;
+  float* probs;
+  ms_row_stats* stats;
+  int32_t* scatter_dst;
+  const int32_t* scatter_idx;
+};
+
+// Row r drawn by one CTA (staged in shared memory when sm.stage is set).
+__device__ __forceinline__ void sample_row_body(const SampleArgs& a, int r, RowSmem& sm) {
+  const float* __restrict__ logits = a.logits;
+  const int64_t stride = a.stride;
+  const int V = a.V;
+  const uint32_t lane_id = a.lane_id;
+  int32_t* __restrict__ tokens = a.tokens;
+  float* __restrict__ probs = a.probs;
+  ms_row_stats* __restrict__ stats = a.stats;
+  int32_t* scatter_dst = a.scatter_dst;
+  const int32_t* __restrict__ scatter_idx = a.scatter_idx;
+  const ms_sampling_params P = a.params[a.pidx ? a.pidx[r] : r];
   const float* row = logits + (int64_t)r * stride;
   Dist d;
   int token;
@@ -874,6 +925,13 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const float* __rest
   }
 }
 
+__global__ void __launch_bounds__(512, 1) sample_rows_kernel(SampleArgs a, int stage) {
+  pdl_enter();
+  RowSmem sm;
+  setup_smem(sm, a.V, stage != 0);
+  sample_row_body(a, blockIdx.x, sm);
+}
+
 // ---- K9: fused accept / resample / bonus, one CTA per request ---------------
 struct AcceptArgs {
   const float* target;
@@ -893,11 +951,8 @@ struct AcceptArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int stage) {
-  pdl_enter();
-  RowSmem sm;
-  setup_smem(sm, a.V, stage != 0);
-  const int b = blockIdx.x;
+// Request b of B, processed by one CTA (target rows staged when sm.stage is set).
+__device__ __forceinline__ void accept_body(const AcceptArgs& a, int b, int B, RowSmem& sm) {
   const int V = a.V, G = a.gamma;
   ms_sampling_params P;
   if (a.params) {
@@ -939,7 +994,7 @@ __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int s
   };
   // Builds the draft distribution for position i (never staged).
   auto draft_dist = [&](int i, Dist& q) {
-    const int r = i * (int)gridDim.x + b;  // position-major: row of (b, i)
+    const int r = i * B + b;  // position-major: row of (b, i)
     const float* row = a.draft + (int64_t)r * a.dstride;
     q.row = row;
     if (a.draft_probs) {
@@ -975,7 +1030,7 @@ __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int s
     Dist p, q;
     target_dist(i, p);
     draft_dist(i, q);
-    int x = a.proposals[i * (int)gridDim.x + b];
+    int x = a.proposals[i * B + b];
     if (x < 0 || x >= V) {
       if (threadIdx.x == 0) raise_device_error(a.err, kErrToken);
       x = 0;
@@ -983,7 +1038,7 @@ __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int s
     const float px = p.prob(x);
     const float qx = q.prob(x);
     const float ratio = fminf(__fdiv_rn(px, fmaxf(qx, 1e-10f)), 1.f);
-    const float u = a.accept_u ? a.accept_u[i * (int)gridDim.x + b]
+    const float u = a.accept_u ? a.accept_u[i * B + b]
                                : philox_uniform(P.seed, P.step, MS_LANE_ACCEPT + i);
     if (u < ratio) {
       if (threadIdx.x == 0) out[i] = x;
@@ -1041,6 +1096,840 @@ __global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int s
   }
 }
 
+__global__ void __launch_bounds__(512, 1) spec_accept_kernel(AcceptArgs a, int stage) {
+  pdl_enter();
+  RowSmem sm;
+  setup_smem(sm, a.V, stage != 0);
+  accept_body(a, blockIdx.x, gridDim.x, sm);
+}
+
+// ---- cluster sampling: one thread-block cluster per row or request -------------
+// A cluster of C CTAs shares a row: CTA k stages the slice [k*S, k*S + S) of
+// the row, divided by the temperature, in its own shared memory, so the row
+// is read from global memory once and every later pass is a shared-memory
+// pass over V/C elements on C SMs.  Row-wide quantities (maximum, kept mass,
+// mass bins, candidates, draw totals) are combined through distributed shared
+// memory: every CTA publishes its part, all pass a cluster barrier, and every
+// CTA reads all parts in rank order and combines them the same way.  Every
+// CTA therefore reaches the same decisions and passes the same barriers.
+//
+// Top-p uses the linear mass bins of the single-CTA path summed over the
+// cluster (CTA k sums bins [k*nb/C, (k+1)*nb/C) over all CTAs and writes the
+// sums into every CTA), then, when the crossing bin holds more than kClCand
+// elements, a second level of kSubBins sub-bins inside it.  Top-k rows, and
+// rows whose crossing sub-bin still holds too many elements (flat or tied
+// rows), are left to CTA 0 running the single-CTA code on global memory.
+constexpr int kClThreads = 256;
+constexpr int kClCand = 512;
+constexpr int kSubBins = 256;
+constexpr int kClMinV = kMaxStagedV + 1;  // rows one CTA can stage stay on one CTA
+constexpr int kClMaxSlice = 32768;   // floats of one CTA's slice
+// 32-bit words: region A = local bins (counts, deficits) + local candidate
+// keys; region B = combined bin masses + counts.
+constexpr int kClRegionA = 2 * kLinBins + 2 * kClCand;
+constexpr int kClRegionB = 2 * kLinBins;
+constexpr size_t kClFixedBytes = 64 * sizeof(double) + 64 * sizeof(float) + 64 * sizeof(int) +
+                                 16 * sizeof(unsigned long long) +
+                                 (size_t)(kClRegionA + kClRegionB) * sizeof(uint32_t);
+static_assert(kClFixedBytes % 16 == 0, "the slice must start 16-byte aligned");
+static_assert(kClRegionA >= (kClThreads / 32) * kHistBins, "single-CTA radix histograms");
+static_assert(kLinBins % kClThreads == 0 && kSubBins % kClThreads == 0, "bins per thread");
+
+struct ClSmem {
+  RowSmem row;               // red_*; row.hist = region A (single-CTA code); row.stage = null
+  unsigned long long* xch;   // two sets of 8 exchange words, used alternately
+  uint32_t* hc;              // region A: local bin counts
+  uint32_t* hd;              // region A: local bin deficits
+  unsigned long long* kl;    // region A: this CTA's candidate keys
+  unsigned long long* km;    // over hc once the bins are combined: every CTA's candidates
+  unsigned long long* ks;    // over hc: the candidates ranked
+  float* hm;                 // region B: combined bin masses
+  uint32_t* hn;              // region B: combined bin counts (candidate prefix masses later)
+  float* xs;                 // the slice
+};
+
+__device__ __forceinline__ void cl_setup(ClSmem& s) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* p = smem_raw;
+  s.row.red_d = reinterpret_cast<double*>(p);
+  p += 64 * sizeof(double);
+  s.row.red = reinterpret_cast<float*>(p);
+  p += 64 * sizeof(float);
+  s.row.red_i = reinterpret_cast<int*>(p);
+  p += 64 * sizeof(int);
+  s.xch = reinterpret_cast<unsigned long long*>(p);
+  p += 16 * sizeof(unsigned long long);
+  uint32_t* A = reinterpret_cast<uint32_t*>(p);
+  p += (size_t)kClRegionA * sizeof(uint32_t);
+  uint32_t* Bw = reinterpret_cast<uint32_t*>(p);
+  p += (size_t)kClRegionB * sizeof(uint32_t);
+  s.row.hist = A;
+  s.row.stage = nullptr;
+  s.hc = A;
+  s.hd = A + kLinBins;
+  s.kl = reinterpret_cast<unsigned long long*>(A + 2 * kLinBins);
+  s.km = reinterpret_cast<unsigned long long*>(A);
+  s.ks = s.km + kClCand;
+  s.hm = reinterpret_cast<float*>(Bw);
+  s.hn = Bw + kLinBins;
+  s.xs = reinterpret_cast<float*>(p);
+}
+
+__device__ __forceinline__ void cl_sync() { cg::this_cluster().sync(); }
+template <typename T>
+__device__ __forceinline__ T* cl_map(T* p, int rank) {
+  return cg::this_cluster().map_shared_rank(p, (unsigned int)rank);
+}
+
+// Exchange state: the CTA's rank, the cluster size and which word set is next.
+// A set written at exchange k was last read before the barrier of exchange
+// k-1, so alternating two sets needs one barrier per exchange.
+struct ClX {
+  int rank, C, par;
+  __device__ __forceinline__ unsigned long long* slot(ClSmem& s) const { return s.xch + 8 * par; }
+};
+
+// Stages [lo, lo + n) of `row` (divided by temp when div) into xs and returns
+// the slice's maximum and first argmax (row index) to every thread.
+__device__ void cl_stage(const float* __restrict__ row, int lo, int n, float temp, bool div,
+                         float* xs, RowSmem& sm, float& m, int& am) {
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  auto note = [&](float v, int i) {
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  };
+  const float* src = row + lo;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const float4* r4 = reinterpret_cast<const float4*>(src);
+    float4* s4 = reinterpret_cast<float4*>(xs);
+    const int n4 = n >> 2;
+    for (int base = threadIdx.x; base < n4; base += 8 * blockDim.x) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * blockDim.x;
+        v[u] = i < n4 ? __ldg(r4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * blockDim.x;
+        if (i < n4) {
+          float4 w = v[u];
+          if (div) {
+            w.x = __fdiv_rn(w.x, temp);
+            w.y = __fdiv_rn(w.y, temp);
+            w.z = __fdiv_rn(w.z, temp);
+            w.w = __fdiv_rn(w.w, temp);
+          }
+          s4[i] = w;
+          note(w.x, lo + 4 * i);
+          note(w.y, lo + 4 * i + 1);
+          note(w.z, lo + 4 * i + 2);
+          note(w.w, lo + 4 * i + 3);
+        }
+      }
+    }
+    for (int i = (n4 << 2) + threadIdx.x; i < n; i += blockDim.x) {
+      const float v = __ldg(src + i);
+      const float x = div ? __fdiv_rn(v, temp) : v;
+      xs[i] = x;
+      note(x, lo + i);
+    }
+  } else {
+#pragma unroll 8
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float v = __ldg(src + i);
+      const float x = div ? __fdiv_rn(v, temp) : v;
+      xs[i] = x;
+      note(x, lo + i);
+    }
+  }
+  block_argmax(best, bi, sm, m, am);  // its barriers also publish the slice
+}
+
+// Row maximum and first argmax from every CTA's slice result.
+__device__ void cl_argmax(ClSmem& s, ClX& x, float mloc, int aloc, float& m, int& am) {
+  unsigned long long* slot = x.slot(s);
+  if (threadIdx.x == 0) {
+    slot[0] = __float_as_uint(mloc);
+    slot[1] = (uint32_t)aloc;
+  }
+  cl_sync();
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int r = 0; r < x.C; ++r) {
+    const unsigned long long* rs = cl_map(slot, r);
+    const float v = __uint_as_float((uint32_t)rs[0]);
+    const int i = (int)(uint32_t)rs[1];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+  x.par ^= 1;
+  m = best;
+  am = bi == 0x7fffffff ? 0 : bi;
+}
+
+// Sum of every CTA's (block-uniform) float, in rank order.
+__device__ float cl_sum(ClSmem& s, ClX& x, float v) {
+  unsigned long long* slot = x.slot(s);
+  if (threadIdx.x == 0) slot[0] = __float_as_uint(v);
+  cl_sync();
+  float t = 0.f;
+  for (int r = 0; r < x.C; ++r) t += __uint_as_float((uint32_t)cl_map(slot, r)[0]);
+  x.par ^= 1;
+  return t;
+}
+
+// The slice's kept mass sum exp(x - m) over x >= thresh; with kBins, also
+// the linear mass bins (counts and deficits) of those elements.
+template <bool kBins>
+__device__ float cl_mass_pass(const float* xs, int n, float m, float thresh, ClSmem& s) {
+  if (kBins) {
+    for (int i = threadIdx.x; i < 2 * kLinBins; i += blockDim.x) s.hc[i] = 0u;
+    __syncthreads();
+  }
+  float zl = 0.f;
+  auto note = [&](float xv) {
+    if (xv >= thresh) {
+      zl += __expf(xv - m);
+      if (kBins) {
+        const int b = lin_bin(m, xv);
+        atomicAdd(&s.hc[b], 1u);
+        atomicAdd(&s.hd[b], lin_deficit(m, xv, b));
+      }
+    }
+  };
+  const float4* x4 = reinterpret_cast<const float4*>(xs);
+  const int n4 = n >> 2;
+  int i = threadIdx.x;
+  for (; i + (int)blockDim.x < n4; i += 2 * blockDim.x) {
+    const float4 a = x4[i], b = x4[i + blockDim.x];
+    note(a.x);
+    note(a.y);
+    note(a.z);
+    note(a.w);
+    note(b.x);
+    note(b.y);
+    note(b.z);
+    note(b.w);
+  }
+  for (; i < n4; i += blockDim.x) {
+    const float4 a = x4[i];
+    note(a.x);
+    note(a.y);
+    note(a.z);
+    note(a.w);
+  }
+  for (int j = (n4 << 2) + threadIdx.x; j < n; j += blockDim.x) note(xs[j]);
+  return block_sum_b(zl, s.row);  // its barriers also complete the bins
+}
+
+// Second-level bins of the elements in first-level bin b1: sub-bin
+// floor(frac(t) * kSubBins) of t = (m - x) * kBinsPerUnit, with deficits
+// against the sub-bin's upper edge, in hc / hd [0, kSubBins).
+__device__ __forceinline__ int sub_bin(float m, float x, int b1) {
+  const float t = (m - x) * kBinsPerUnit;
+  const int s = (int)((t - (float)b1) * (float)kSubBins);
+  return s < kSubBins - 1 ? s : kSubBins - 1;
+}
+__device__ void cl_sub_pass(const float* xs, int n, float m, int b1, ClSmem& s) {
+  for (int i = threadIdx.x; i < kSubBins; i += blockDim.x) {
+    s.hc[i] = 0u;
+    s.hd[i] = 0u;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float xv = xs[j];
+    if (xv >= -INFINITY && lin_bin(m, xv) == b1) {
+      const int sb = sub_bin(m, xv, b1);
+      const float edge = (float)b1 + (float)sb * (1.f / kSubBins);
+      const float r = __expf((xv - m) + edge * (1.f / kBinsPerUnit));
+      atomicAdd(&s.hc[sb], 1u);
+      atomicAdd(&s.hd[sb], __float2uint_rn(fmaxf(1.f - r, 0.f) * kDefScale));
+    }
+  }
+  __syncthreads();
+}
+
+// After a cluster barrier that follows every CTA's bin pass: CTA `rank` sums
+// bins [rank*nb/C, (rank+1)*nb/C) over all CTAs and writes the mass and count
+// of each into every CTA's hm / hn.  Bin b's upper edge lies (e0 + b * ew) /
+// kBinsPerUnit below the maximum.  Ends with a cluster barrier.
+__device__ void cl_combine_bins(ClSmem& s, const ClX& x, int nb, float e0, float ew) {
+  const int per = nb / x.C;
+  for (int j = threadIdx.x; j < per; j += blockDim.x) {
+    const int b = x.rank * per + j;
+    double acc = 0.0;
+    uint32_t cnt = 0;
+    for (int r = 0; r < x.C; ++r) {
+      const uint32_t c = cl_map(s.hc, r)[b];
+      const uint32_t d = cl_map(s.hd, r)[b];
+      cnt += c;
+      acc += (double)c - (double)d * (1.0 / kDefScale);
+    }
+    const float mass = (float)acc * __expf(-(e0 + (float)b * ew) * (1.f / kBinsPerUnit));
+    for (int r = 0; r < x.C; ++r) {
+      cl_map(s.hm, r)[b] = mass;
+      cl_map(s.hn, r)[b] = cnt;
+    }
+  }
+  cl_sync();
+}
+
+// First bin of hm[0, nb) whose inclusive mass prefix, starting at `base`,
+// reaches `target` (-1 if none); `before` = the prefix before that bin.
+__device__ int cl_find(const float* hm, int nb, double base, double target, RowSmem& sm,
+                       double& before) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int per = nb / blockDim.x;
+  const int b0 = threadIdx.x * per;
+  double own = 0.0;
+  for (int j = 0; j < per; ++j) own += (double)hm[b0 + j];
+  double inc = own;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, inc, o);
+    if (lane >= o) inc += t;
+  }
+  __syncthreads();
+  if (lane == 31) sm.red_d[warp] = inc;
+  if (threadIdx.x == 0) sm.red_i[48] = -1;
+  __syncthreads();
+  double wb = base;
+  for (int w = 0; w < warp && w < nw; ++w) wb += sm.red_d[w];
+  const double ex = wb + inc - own;
+  if (ex < target && ex + own >= target) {
+    double a = ex;
+    for (int j = 0; j < per; ++j) {
+      const double h = (double)hm[b0 + j];
+      if (a + h >= target) {
+        sm.red_i[48] = b0 + j;
+        sm.red_d[48] = a;
+        break;
+      }
+      a += h;
+    }
+  }
+  __syncthreads();
+  const int bin = sm.red_i[48];
+  before = sm.red_d[48];
+  __syncthreads();
+  return bin;
+}
+
+// This slice's candidates: elements in bin b1 (and sub-bin sb when sb >= 0),
+// as sort keys in kl (the first kClCand of them); returns their number.
+__device__ int cl_gather(const float* xs, int n, int lo, float m, int b1, int sb, ClSmem& s) {
+  if (threadIdx.x == 0) s.row.red_i[50] = 0;
+  __syncthreads();
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float xv = xs[j];
+    if (xv >= -INFINITY && lin_bin(m, xv) == b1 && (sb < 0 || sub_bin(m, xv, b1) == sb)) {
+      const int slot = atomicAdd(&s.row.red_i[50], 1);
+      if (slot < kClCand)
+        s.kl[slot] = ((unsigned long long)fkey(xv) << 32) | (uint32_t)~(uint32_t)(lo + j);
+    }
+  }
+  __syncthreads();
+  const int cnt = s.row.red_i[50];
+  __syncthreads();
+  return cnt;
+}
+
+// The top-p crossing among the ranked candidates ks[0, n), their exact
+// masses accumulated from `before`: the cut value and the mass kept at and
+// above it (ties kept).  False when rounding finds no crossing.
+__device__ bool cl_cross(ClSmem& s, int n, float m, double before, double target, float& cut,
+                         double& z_keep) {
+  RowSmem& sm = s.row;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  double* cum_of = reinterpret_cast<double*>(s.hn);  // n <= kClCand doubles
+  if (threadIdx.x == 0) sm.red_i[51] = 0x7fffffff;
+  double carry = before;
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int c = base + threadIdx.x;
+    const float xc = c < n ? kfloat((uint32_t)(s.ks[c] >> 32)) : -INFINITY;
+    const double e = c < n ? (double)__expf(xc - m) : 0.0;
+    double inc = e;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, inc, o);
+      if (lane >= o) inc += t;
+    }
+    __syncthreads();
+    if (lane == 31) sm.red_d[warp] = inc;
+    __syncthreads();
+    double wb = carry, all = carry;
+    for (int w = 0; w < nw; ++w) {
+      if (w < warp) wb += sm.red_d[w];
+      all += sm.red_d[w];
+    }
+    const double cum = wb + inc;
+    if (c < n) {
+      cum_of[c] = cum;
+      if (cum - e < target && cum >= target) atomicMin(&sm.red_i[51], c);
+    }
+    carry = all;
+  }
+  __syncthreads();
+  const int cross = sm.red_i[51];
+  if (cross >= n) {
+    __syncthreads();
+    return false;
+  }
+  cut = kfloat((uint32_t)(s.ks[cross] >> 32));
+  for (int c = cross + threadIdx.x; c < n; c += blockDim.x) {
+    const float xc = kfloat((uint32_t)(s.ks[c] >> 32));
+    if (xc == cut && (c + 1 == n || kfloat((uint32_t)(s.ks[c + 1] >> 32)) < cut))
+      sm.red_d[49] = cum_of[c];
+  }
+  __syncthreads();
+  z_keep = sm.red_d[49];
+  __syncthreads();
+  return true;
+}
+
+// Fills d.thresh, d.z, d.inv_z of a staged logits row (temperature > 0, no
+// top-k) whose d.m is the row maximum.  Returns false when the row needs the
+// single-CTA path; the answer is the same in every CTA of the cluster.
+__device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX& x) {
+  const float m = d.m;
+  d.thresh = -INFINITY;
+  const bool want_p = top_p < 1.f;
+  const float zloc = want_p ? cl_mass_pass<true>(s.xs, n, m, -INFINITY, s)
+                            : cl_mass_pass<false>(s.xs, n, m, -INFINITY, s);
+  d.z = cl_sum(s, x, zloc);  // its barrier also completes every CTA's bins
+  d.inv_z = 1.f / d.z;
+  if (!want_p) return true;
+  if (1.f >= top_p * d.z) {  // the maximum alone already covers top_p
+    d.thresh = m;
+    d.z = cl_sum(s, x, cl_mass_pass<false>(s.xs, n, m, m, s));
+    d.inv_z = 1.f / d.z;
+    return true;
+  }
+  const double target = (double)top_p * (double)d.z;
+  cl_combine_bins(s, x, kLinBins, 0.f, 1.f);
+  double before;
+  const int b1 = cl_find(s.hm, kLinBins, 0.0, target, s.row, before);
+  if (b1 < 0 || b1 >= kLinBins - 1) return false;
+  int sb = -1;
+  if (s.hn[b1] > (uint32_t)kClCand) {
+    cl_sub_pass(s.xs, n, m, b1, s);
+    cl_sync();  // every CTA's sub-bins are complete; hm / hn have been read
+    cl_combine_bins(s, x, kSubBins, (float)b1, 1.f / kSubBins);
+    double before2;
+    sb = cl_find(s.hm, kSubBins, before, target, s.row, before2);
+    if (sb < 0 || s.hn[sb] > (uint32_t)kClCand) return false;
+    before = before2;
+  }
+  const int nloc = cl_gather(s.xs, n, lo, m, b1, sb, s);
+  unsigned long long* slot = x.slot(s);
+  if (threadIdx.x == 0) slot[0] = (uint32_t)nloc;
+  cl_sync();
+  int cnt[8], total = 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    cnt[r] = r < x.C ? (int)cl_map(slot, r)[0] : 0;
+    total += cnt[r];
+  }
+  x.par ^= 1;
+  if (total > kClCand || total == 0) return false;
+  int off = 0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r < x.C) {
+      const unsigned long long* rk = cl_map(s.kl, r);
+      for (int j = threadIdx.x; j < cnt[r]; j += blockDim.x) s.km[off + j] = rk[j];
+      off += cnt[r];
+    }
+  }
+  __syncthreads();
+  rank_keys_desc(s.km, s.ks, total);
+  float cut;
+  double zk;
+  if (!cl_cross(s, total, m, before, target, cut, zk)) return false;
+  if (cut > d.thresh) {
+    d.thresh = cut;
+    d.z = (float)zk;
+    d.inv_z = 1.f / d.z;
+  }
+  return true;
+}
+
+// Inverse-CDF draw over the cluster: slice totals, a rank-order exchange that
+// places u * total in one CTA (the owner), then the owner's in-slice search.
+// Ends every DSMEM use with a cluster barrier, so CTAs may exit afterwards.
+// `mine` tells the one CTA that holds the drawn token.
+template <typename W>
+__device__ void cl_draw(const W& w, int n, int lo, float u, ClSmem& s, ClX& x, int& tok,
+                        bool& mine) {
+  double tot;
+  int last;
+  cdf_totals(w, n, s.row, tot, last);
+  unsigned long long* slot = x.slot(s);
+  if (threadIdx.x == 0) {
+    slot[0] = (unsigned long long)__double_as_longlong(tot);
+    slot[1] = (uint32_t)(last >= 0 ? lo + last : -1);
+  }
+  cl_sync();
+  double T[8];
+  double total = 0.0;
+  int glast = -1;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    T[r] = 0.0;
+    if (r < x.C) {
+      const unsigned long long* rs = cl_map(slot, r);
+      T[r] = __longlong_as_double((long long)rs[0]);
+      total += T[r];
+      glast = max(glast, (int)(uint32_t)rs[1]);
+    }
+  }
+  x.par ^= 1;
+  cl_sync();  // every CTA has read every slot: no DSMEM access after this
+  const double target = (double)u * total;
+  int owner = -1;
+  double obase = 0.0, before = 0.0;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    if (r < x.C) {
+      if (owner < 0 && T[r] > 0.0 && before <= target && target < before + T[r]) {
+        owner = r;
+        obase = before;
+      }
+      before += T[r];
+    }
+  }
+  mine = false;
+  tok = 0;
+  if (owner == x.rank) {
+    int idx = cdf_search(w, n, obase, target, s.row);
+    if (idx < 0) idx = last;
+    tok = idx >= 0 ? lo + idx : (glast >= 0 ? glast : 0);
+    mine = true;
+  } else if (owner < 0 && x.rank == 0) {
+    tok = glast >= 0 ? glast : 0;
+    mine = true;
+  }
+}
+
+// The single-CTA paths for rows the cluster leaves to CTA 0 (shared memory
+// set up without a staged row: they read global memory).
+__device__ __noinline__ void sample_row_single(SampleArgs a, int r, RowSmem sm) {
+  sample_row_body(a, r, sm);
+}
+__device__ __noinline__ void accept_single(AcceptArgs a, int b, int B, RowSmem sm) {
+  accept_body(a, b, B, sm);
+}
+
+__device__ __forceinline__ ClX cl_begin(int C, int S, int V, int& lo, int& n) {
+  ClX x;
+  x.rank = (int)cg::this_cluster().block_rank();
+  x.C = C;
+  x.par = 0;
+  lo = min(V, x.rank * S);
+  n = min(V, lo + S) - lo;
+  return x;
+}
+
+// ---- K8 on a cluster per row ----------------------------------------------------
+template <int C>
+__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kClThreads, 2)
+    sample_cluster_kernel(SampleArgs a, int S) {
+  pdl_enter();
+  ClSmem s;
+  cl_setup(s);
+  const int V = a.V;
+  int lo, n;
+  ClX x = cl_begin(C, S, V, lo, n);
+  const int r = blockIdx.x / C;
+  const ms_sampling_params P = a.params[a.pidx ? a.pidx[r] : r];
+  const bool greedy = P.temperature == 0.f;
+  if (!greedy && P.top_k > 0 && P.top_k < V) {  // top-k: CTA 0 alone, no cluster barrier
+    if (x.rank == 0) sample_row_single(a, r, s.row);
+    return;
+  }
+  const float temp = greedy ? 1.f : P.temperature;
+  const float* row = a.logits + (int64_t)r * a.stride;
+  float mloc;
+  int aloc;
+  cl_stage(row, lo, n, temp, !greedy && temp != 1.f, s.xs, s.row, mloc, aloc);
+  Dist d;
+  d.row = row;
+  d.mode = 0;
+  d.divide = false;
+  d.temp = temp;
+  cl_argmax(s, x, mloc, aloc, d.m, d.argmax);
+  int tok;
+  bool mine;
+  if (greedy) {
+    cl_sync();  // every CTA has read every slot
+    d.mode = 2;
+    d.thresh = d.m;
+    d.z = 1.f;
+    d.inv_z = 1.f;
+    tok = d.argmax;
+    mine = x.rank == 0;
+  } else {
+    if (!cl_row_stats(d, P.top_p < 1.f ? P.top_p : 1.f, n, lo, s, x)) {
+      cl_sync();  // nobody reads this cluster's shared memory any more
+      if (x.rank == 0) sample_row_single(a, r, s.row);
+      return;
+    }
+    const float u = philox_uniform(P.seed, P.step, a.lane_id);
+    const float* xs = s.xs;
+    const float m = d.m, th = d.thresh;
+    cl_draw([xs, m, th](int j) { const float v = xs[j]; return v >= th ? __expf(v - m) : 0.f; }, n,
+            lo, u, s, x, tok, mine);
+  }
+  if (threadIdx.x == 0) {
+    if (mine) {
+      a.tokens[r] = tok;
+      if (a.scatter_dst && a.scatter_idx) a.scatter_dst[a.scatter_idx[r]] = tok;
+    }
+    if (x.rank == 0 && a.stats) a.stats[r] = ms_row_stats{d.m, d.thresh, d.z, d.argmax};
+  }
+  if (a.probs) {
+    float* out = a.probs + (int64_t)r * V + lo;
+    const float* xs = s.xs;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      float pr;
+      if (d.mode == 2) {
+        pr = lo + j == d.argmax ? 1.f : 0.f;
+      } else {
+        const float v = xs[j];
+        pr = v >= d.thresh ? __expf(v - d.m) * d.inv_z : 0.f;
+      }
+      out[j] = pr;
+    }
+  }
+}
+
+// ---- K9 on a cluster per request ------------------------------------------------
+// Target rows staged slice-wise; draft rows come with their statistics
+// (ms_row_stats from the draft draws) and are read from global memory.
+template <int C>
+__global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kClThreads, 2)
+    accept_cluster_kernel(AcceptArgs a, int S) {
+  pdl_enter();
+  ClSmem s;
+  cl_setup(s);
+  const int V = a.V, G = a.gamma;
+  int lo, n;
+  ClX x = cl_begin(C, S, V, lo, n);
+  const int B = gridDim.x / C;
+  const int b = blockIdx.x / C;
+  const ms_sampling_params P = a.params[b];
+  const bool greedy = P.temperature == 0.f;
+  if (!greedy && P.top_k > 0 && P.top_k < V) {  // top-k: CTA 0 alone, no cluster barrier
+    if (x.rank == 0) accept_single(a, b, B, s.row);
+    return;
+  }
+  const float top_p = P.top_p < 1.f ? P.top_p : 1.f;
+  const float temp = greedy ? 1.f : P.temperature;
+  const bool div = !greedy && temp != 1.f;
+  int32_t* out = a.out_tokens + (int64_t)b * (G + 1);
+  const bool lead = x.rank == 0 && threadIdx.x == 0;
+
+  // Target distribution of position i, staged; false: the single-CTA path.
+  auto target_dist = [&](int i, Dist& p) -> bool {
+    const float* row = a.target + (int64_t)(b * (G + 1) + i) * a.tstride;
+    float mloc;
+    int aloc;
+    cl_stage(row, lo, n, temp, div, s.xs, s.row, mloc, aloc);
+    p.row = row;
+    p.divide = div;
+    p.temp = temp;
+    cl_argmax(s, x, mloc, aloc, p.m, p.argmax);
+    if (greedy) {
+      p.mode = 2;
+      return true;
+    }
+    p.mode = 0;
+    return cl_row_stats(p, top_p, n, lo, s, x);
+  };
+  const float* xs = s.xs;
+
+  for (int i = 0; i < G; ++i) {
+    Dist p;
+    if (!target_dist(i, p)) {
+      cl_sync();  // nobody reads this cluster's shared memory any more
+      if (x.rank == 0) accept_single(a, b, B, s.row);
+      return;
+    }
+    const int r = i * B + b;  // position-major: row of (b, i)
+    const ms_row_stats st = a.dstats[r];
+    Dist q;
+    q.row = a.draft + (int64_t)r * a.dstride;
+    q.temp = temp;
+    q.divide = div;
+    q.m = st.max;
+    q.thresh = st.thresh;
+    q.z = st.z;
+    q.inv_z = 1.f / st.z;
+    q.argmax = st.argmax;
+    q.mode = greedy ? 2 : 0;
+    int tokx = a.proposals[i * B + b];
+    if (tokx < 0 || tokx >= V) {
+      if (lead) raise_device_error(a.err, kErrToken);
+      tokx = 0;
+    }
+    const float px = p.prob(tokx);
+    const float qx = q.prob(tokx);
+    const float ratio = fminf(__fdiv_rn(px, fmaxf(qx, 1e-10f)), 1.f);
+    const float u = a.accept_u ? a.accept_u[i * B + b]
+                               : philox_uniform(P.seed, P.step, MS_LANE_ACCEPT + i);
+    if (u < ratio) {
+      if (lead) out[i] = tokx;
+      continue;
+    }
+    // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0;
+    // the residual replaces the staged slice.
+    const Dist pv = p, qv = q;
+    float part = 0.f;
+    float* res = s.xs;
+#pragma unroll 4
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      float pj;
+      if (pv.mode == 2) {
+        pj = lo + j == pv.argmax ? 1.f : 0.f;
+      } else {
+        const float v = res[j];
+        pj = v >= pv.thresh ? __expf(v - pv.m) * pv.inv_z : 0.f;
+      }
+      const float rj = fmaxf(pj - qv.prob(lo + j), 0.f);
+      res[j] = rj;
+      part += rj;
+    }
+    const float total = cl_sum(s, x, block_sum_b(part, s.row));
+    const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
+    int tok;
+    bool mine;
+    if (total <= 1e-9f) {  // the residual overwrote p's slice: stage it again
+      float ml;
+      int al;
+      cl_stage(pv.row, lo, n, temp, div, s.xs, s.row, ml, al);
+      cl_draw([xs, pv, lo](int j) {
+                if (pv.mode == 2) return lo + j == pv.argmax ? 1.f : 0.f;
+                const float v = xs[j];
+                return v >= pv.thresh ? __expf(v - pv.m) * pv.inv_z : 0.f;
+              },
+              n, lo, u2, s, x, tok, mine);
+    } else {
+      cl_draw([xs](int j) { return xs[j]; }, n, lo, u2, s, x, tok, mine);
+    }
+    if (threadIdx.x == 0) {
+      if (mine) out[i] = tok;
+      if (x.rank == 0) a.out_nacc[b] = i;
+    }
+    return;
+  }
+  // Every proposal survived: the bonus token comes from p[gamma].
+  Dist p;
+  if (!target_dist(G, p)) {
+    cl_sync();
+    if (x.rank == 0) accept_single(a, b, B, s.row);
+    return;
+  }
+  if (greedy) {
+    cl_sync();  // every CTA has read every slot
+    if (lead) {
+      out[G] = p.argmax;
+      a.out_nacc[b] = G;
+    }
+    return;
+  }
+  const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
+  const float m = p.m, th = p.thresh;
+  int tok;
+  bool mine;
+  cl_draw([xs, m, th](int j) { const float v = xs[j]; return v >= th ? __expf(v - m) : 0.f; }, n,
+          lo, u2, s, x, tok, mine);
+  if (threadIdx.x == 0) {
+    if (mine) out[G] = tok;
+    if (x.rank == 0) a.out_nacc[b] = G;
+  }
+}
+
+// Cluster shape for a vocabulary: C CTAs of S (a multiple of 4) floats each;
+// 0 when the row is better served by one CTA.
+int cl_shape(int V, int& S) {
+  if (V < kClMinV) return 0;
+  const int C = V <= 65536 ? 4 : 8;
+  S = ((V + C - 1) / C + 3) & ~3;
+  return S <= kClMaxSlice ? C : 0;
+}
+size_t cl_smem(int S) { return kClFixedBytes + (size_t)S * sizeof(float); }
+
+// Sets the kernel's shared-memory size and checks (once per kernel and size)
+// that a cluster of that shape can be resident; false: use the single-CTA
+// kernel.
+template <typename K>
+bool cl_prepare(K kernel, int C, size_t smem) {
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess) {
+    (void)cudaGetLastError();
+    return false;
+  }
+  static thread_local const void* seen_fn[4] = {nullptr, nullptr, nullptr, nullptr};
+  static thread_local size_t seen_smem[4] = {0, 0, 0, 0};
+  static thread_local bool seen_ok[4] = {false, false, false, false};
+  static thread_local int next = 0;
+  for (int i = 0; i < 4; ++i)
+    if (seen_fn[i] == (const void*)kernel && seen_smem[i] == smem) return seen_ok[i];
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(C, 1, 1);
+  cfg.blockDim = dim3(kClThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  int clusters = 0;
+  const bool ok =
+      cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) == cudaSuccess && clusters >= 1;
+  if (!ok) (void)cudaGetLastError();
+  seen_fn[next] = (const void*)kernel;
+  seen_smem[next] = smem;
+  seen_ok[next] = ok;
+  next = (next + 1) & 3;
+  return ok;
+}
+
+// Launches K8 / K9 on clusters when the vocabulary suits them; returns
+// MS_ERR_UNSUPPORTED (nothing launched) otherwise.
+int launch_sample_cluster(const SampleArgs& a, int n_rows, cudaStream_t st) {
+  int S = 0;
+  const int C = cl_shape(a.V, S);
+  if (C == 0) return MS_ERR_UNSUPPORTED;
+  const size_t smem = cl_smem(S);
+  if (C == 4) {
+    if (!cl_prepare(sample_cluster_kernel<4>, 4, smem)) return MS_ERR_UNSUPPORTED;
+    launch_pdl(sample_cluster_kernel<4>, n_rows * 4, kClThreads, smem, st, a, S);
+  } else {
+    if (!cl_prepare(sample_cluster_kernel<8>, 8, smem)) return MS_ERR_UNSUPPORTED;
+    launch_pdl(sample_cluster_kernel<8>, n_rows * 8, kClThreads, smem, st, a, S);
+  }
+  return check_launch("sample_cluster_kernel");
+}
+
+int launch_accept_cluster(const AcceptArgs& a, int B, cudaStream_t st) {
+  if (a.target_probs || a.draft_probs || !a.dstats || !a.params) return MS_ERR_UNSUPPORTED;
+  int S = 0;
+  const int C = cl_shape(a.V, S);
+  if (C == 0) return MS_ERR_UNSUPPORTED;
+  const size_t smem = cl_smem(S);
+  if (C == 4) {
+    if (!cl_prepare(accept_cluster_kernel<4>, 4, smem)) return MS_ERR_UNSUPPORTED;
+    launch_pdl(accept_cluster_kernel<4>, B * 4, kClThreads, smem, st, a, S);
+  } else {
+    if (!cl_prepare(accept_cluster_kernel<8>, 8, smem)) return MS_ERR_UNSUPPORTED;
+    launch_pdl(accept_cluster_kernel<8>, B * 8, kClThreads, smem, st, a, S);
+  }
+  return check_launch("accept_cluster_kernel");
+}
+
 int row_threads(int V) {
   int t = ((V / 16) + 31) & ~31;
   if (t < 128) t = 128;
@@ -1057,6 +1946,8 @@ int launch_accept(AcceptArgs a, int B, void* stream) {
                                        (int)smem);
   if (e != cudaSuccess) return fail(MS_ERR_CUDA, "spec_accept: smem attribute: %s", cudaGetErrorString(e));
   ProfScope prof(kClsAccept, as_stream(stream));
+  const int rc = launch_accept_cluster(a, B, as_stream(stream));
+  if (rc != MS_ERR_UNSUPPORTED) return rc;
   launch_pdl(spec_accept_kernel, B, threads, smem, as_stream(stream), a, stage ? 1 : 0);
   return check_launch("spec_accept_kernel");
 }
@@ -1081,9 +1972,11 @@ extern "C" int ms_sample(const float* logits, int64_t row_stride, int n_rows, in
                                        (int)smem);
   if (e != cudaSuccess) return fail(MS_ERR_CUDA, "ms_sample: smem attribute: %s", cudaGetErrorString(e));
   ProfScope prof(kClsSample, as_stream(stream));
-  launch_pdl(sample_rows_kernel, n_rows, threads, smem, as_stream(stream),
-      logits, row_stride, vocab, params, pidx, (uint32_t)lane, tokens, probs, stats, scatter_dst,
-      scatter_idx, stage ? 1 : 0);
+  const SampleArgs a{logits, row_stride, vocab, params, pidx, (uint32_t)lane, tokens, probs, stats,
+                     scatter_dst, scatter_idx};
+  const int rc = launch_sample_cluster(a, n_rows, as_stream(stream));
+  if (rc != MS_ERR_UNSUPPORTED) return rc;
+  launch_pdl(sample_rows_kernel, n_rows, threads, smem, as_stream(stream), a, stage ? 1 : 0);
   return check_launch("sample_rows_kernel");
 }
 

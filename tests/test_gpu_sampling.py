@@ -48,7 +48,7 @@ SETTINGS = [(1.0, None, None), (0.8, None, None), (1.0, 5, None), (1.0, None, 0.
             (0.7, 5, 0.9), (1.3, None, 0.5), (1.0, 50, 0.9), (0.0, None, None)]
 
 
-@pytest.mark.parametrize("vocab", [65, 1000, 32000, 50000])
+@pytest.mark.parametrize("vocab", [65, 1000, 32000, 50000, 128256])
 def test_sample_distribution_and_draws_match_oracle(vocab: int) -> None:
     L = _lib()
     rng = np.random.default_rng(vocab)
@@ -74,6 +74,57 @@ def test_sample_distribution_and_draws_match_oracle(vocab: int) -> None:
                 assert near_boundary(row, u), (vocab, si, r, got_t[r], tok)
                 mismatches += 1
     assert mismatches <= 1
+
+
+def _ties_kept(logits: np.ndarray, t: float, p, u: float):
+    """The oracle row with every value equal to its top-p cut kept: the kernels
+    keep x >= cut, where the reference's sort keeps a prefix of the ties."""
+    tok, row = sample_row(logits, t, None, p, u)
+    if row.onehot is not None or p is None or p >= 1.0:
+        return tok, row
+    x = logits if t == 1.0 else (logits / np.float32(t)).astype(np.float32)
+    cut = x[row.e > 0].min()
+    e = np.where(x >= cut, np.exp((x - x.max()).astype(np.float32)), np.float32(0)).astype(np.float32)
+    kept = Row(e, float(e.sum(dtype=np.float64)))
+    return draw(e, u), kept
+
+
+@pytest.mark.parametrize("vocab", [50000, 128256])
+def test_sample_flat_and_tied_rows_match_oracle(vocab: int) -> None:
+    """Rows whose top-p crossing bin is crowded: a narrow spread (second-level
+    bins), all-equal and two-valued rows (more tied candidates than one
+    cluster ranks: the single-CTA path), a spike over a flat floor.  Ties at
+    the cut are all kept."""
+    L = _lib()
+    rng = np.random.default_rng(vocab + 1)
+    rows = [rng.standard_normal(vocab) * 0.02, rng.standard_normal(vocab) * 0.002,
+            np.zeros(vocab), np.where(rng.random(vocab) < 0.5, 1.0, 0.0),
+            np.concatenate([[12.0], np.full(vocab - 1, -1.0)]),
+            rng.standard_normal(vocab) * 0.3]
+    logits = np.stack(rows).astype(np.float32)
+    n = logits.shape[0]
+    dl = torch.from_numpy(logits).to(DEV)
+    mismatches = 0
+    for si, (t, k, p) in enumerate([(1.0, None, 0.9), (0.7, None, 0.5), (1.0, None, 0.999),
+                                    (1.0, None, None), (0.0, None, None)]):
+        seeds = [77 + r for r in range(n)]
+        steps = [si] * n
+        params = _params([(t, k, p)] * n, seeds, steps)
+        toks = torch.empty(n, dtype=torch.int32, device=DEV)
+        probs = torch.empty((n, vocab), dtype=torch.float32, device=DEV)
+        L.call("ms_sample", dl.data_ptr(), vocab, n, vocab, params.data_ptr(), None, 1,
+               toks.data_ptr(), probs.data_ptr(), None, None, None, L.stream_ptr())
+        got_p = probs.cpu().numpy()
+        got_t = toks.cpu().numpy()
+        for r in range(n):
+            u = float(philox.uniform(seeds[r], steps[r], 1))
+            tok, row = _ties_kept(logits[r], t, p, u)
+            np.testing.assert_allclose(got_p[r], row.probs, rtol=2e-5, atol=1e-7)
+            if got_t[r] != tok:
+                assert near_boundary(row, u), (vocab, si, r, got_t[r], tok)
+                mismatches += 1
+    assert mismatches <= 1
+    assert L.device_error() == 0
 
 
 def test_greedy_ties_pick_first_index() -> None:
@@ -118,13 +169,15 @@ def _accept_case(B: int, G: int, V: int, t: float, k, p, seed: int):
     *[(s, m, 4000) for s in [(1.0, None, None), (1.0, 50, None), (1.0, None, 0.9),
                              (0.8, 20, 0.95), (0.0, None, None)]
       for m in ("logits", "stats", "probs")],
-    *[(s, "stats", 32000) for s in [(1.0, 50, None), (1.0, None, 0.9), (0.8, 50, 0.9)]],
+    *[(s, "stats", 32000) for s in [(1.0, 50, None), (1.0, None, 0.9), (0.8, 50, 0.9),
+                                    (0.8, None, 0.9), (0.0, None, None), (1.3, None, None)]],
+    *[(s, "stats", 100000) for s in [(0.8, None, 0.9), (0.0, None, None), (1.0, 50, None)]],
 ])
 def test_spec_accept_matches_oracle(setting, draft_mode: str, V: int) -> None:
     """config-1-shaped (rows x gamma=5 x vocab) at a reduced row count."""
     L = _lib()
     t, k, p = setting
-    B, G = 48, 5
+    B, G = (48, 5) if V <= 32000 else (24, 5)
     tl, dl, seeds, steps, qrows, props = _accept_case(B, G, V, t, k, p, 99)
     params = _params([(t, k, p)] * B, seeds.tolist(), steps.tolist())
     d_tl = torch.from_numpy(tl.reshape(B * (G + 1), V)).to(DEV)
