@@ -210,6 +210,9 @@ class PagedKVCache:
         self._max_blocks = max(1, min(cache.num_blocks, -(-model.max_seq_len // self.block_size)))
         self._rows: dict[int, int] = {}
         self._free_rows: list[int] = []
+        # Bumped whenever a sequence gains or loses its table row, so callers
+        # may keep ``rows_of`` results while it is unchanged.
+        self.generation = 0
         self._table = np.zeros((8, self._max_blocks), dtype=np.int32)
         self._nblk = np.zeros(8, dtype=np.int32)
         self._ntok = np.zeros(8, dtype=np.int64)
@@ -272,9 +275,15 @@ class PagedKVCache:
         needed = (ntok + num_new_tokens + self.block_size - 1) // self.block_size
         return max(0, needed - nblk)
 
-    def blocks_needed_many(self, seq_ids: Sequence[int], counts: Sequence[int] | np.ndarray) -> int:
-        """Total extra blocks ``append_many(seq_ids, counts)`` would take (no change)."""
+    def blocks_needed_many(self, seq_ids: Sequence[int], counts: Sequence[int] | np.ndarray,
+                           rows: np.ndarray | None = None) -> int:
+        """Total extra blocks ``append_many(seq_ids, counts)`` would take (no change).
+        ``rows``: the sequences' ``rows_of`` result, when the caller has it."""
         counts = np.asarray(counts, dtype=np.int64)
+        if rows is not None:
+            bs = self.block_size
+            need = (self._ntok[rows] + counts + bs - 1) // bs - self._nblk[rows]
+            return int(np.maximum(need, 0).sum())
         get = self._rows.get
         rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
         known = rows >= 0
@@ -311,6 +320,7 @@ class PagedKVCache:
         self._rows[seq_id] = row
         self._nblk[row] = 0
         self._ntok[row] = 0
+        self.generation += 1
         return row
 
     def rows_of(self, seq_ids: Sequence[int]) -> np.ndarray:
@@ -322,13 +332,23 @@ class PagedKVCache:
             return np.fromiter((self._row_of(s) for s in seq_ids), dtype=np.int64,
                                count=len(seq_ids))
 
+    def rows_if_all_present(self, seq_ids: Sequence[int]) -> np.ndarray | None:
+        """``rows_of(seq_ids)`` when every sequence already has a row, else None
+        (nothing is created)."""
+        rows = self._rows
+        if not all(s in rows for s in seq_ids):
+            return None
+        return self._existing_rows(seq_ids)
+
     def _existing_rows(self, seq_ids: Sequence[int]) -> np.ndarray:
         """Rows of sequences that must already exist (KeyError otherwise)."""
         return np.fromiter(map(self._rows.__getitem__, seq_ids), dtype=np.int64,
                            count=len(seq_ids))
 
-    def num_tokens_many(self, seq_ids: Sequence[int]) -> np.ndarray:
+    def num_tokens_many(self, seq_ids: Sequence[int], rows: np.ndarray | None = None) -> np.ndarray:
         """``num_tokens`` of each sequence (0 for unknown ones), int64."""
+        if rows is not None:
+            return self._ntok[rows]
         get = self._rows.get
         rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
         out = np.zeros(len(seq_ids), dtype=np.int64)
@@ -348,16 +368,19 @@ class PagedKVCache:
         """Reserve slots for ``num_new_tokens`` and return their physical ids."""
         return self.append_many([seq_id], [num_new_tokens]).tolist()
 
-    def append_many(self, seq_ids: Sequence[int], counts: Sequence[int] | np.ndarray) -> np.ndarray:
+    def append_many(self, seq_ids: Sequence[int], counts: Sequence[int] | np.ndarray,
+                    rows: np.ndarray | None = None) -> np.ndarray:
         """Vectorised ``append``: slots of every new token, sequence by sequence.
 
         All-or-nothing: raises :class:`OutOfCacheMemory` before touching any
-        table if the pool cannot hold every sequence's new blocks.
+        table if the pool cannot hold every sequence's new blocks.  ``rows``:
+        the (distinct) sequences' ``rows_of`` result, when the caller has it.
         """
         counts = np.asarray(counts, dtype=np.int64)
-        if len(set(seq_ids)) != len(seq_ids):
-            raise ValueError("append_many: a sequence appears twice in one batch")
-        rows = self.rows_of(seq_ids)
+        if rows is None:
+            if len(set(seq_ids)) != len(seq_ids):
+                raise ValueError("append_many: a sequence appears twice in one batch")
+            rows = self.rows_of(seq_ids)
         if counts.size == 0:
             return np.zeros(0, dtype=np.int64)
         bs = self.block_size
@@ -394,6 +417,7 @@ class PagedKVCache:
         self._nblk[row] = 0
         self._ntok[row] = 0
         self._free_rows.append(row)
+        self.generation += 1
 
     def truncate(self, seq_id: int, num_tokens: int) -> None:
         """Shrink a sequence to ``num_tokens``, releasing blocks past the end."""
@@ -401,9 +425,11 @@ class PagedKVCache:
             raise KeyError(seq_id)
         self.truncate_many([seq_id], [num_tokens])
 
-    def truncate_many(self, seq_ids: Sequence[int], num_tokens: Sequence[int] | np.ndarray) -> None:
+    def truncate_many(self, seq_ids: Sequence[int], num_tokens: Sequence[int] | np.ndarray,
+                      rows: np.ndarray | None = None) -> None:
         """Vectorised ``truncate`` (speculative rollback, reference cache.py:210-222)."""
-        rows = self._existing_rows(seq_ids)
+        if rows is None:
+            rows = self._existing_rows(seq_ids)
         n = np.asarray(num_tokens, dtype=np.int64)
         if np.any(n > self._ntok[rows]):
             raise ValueError("truncate cannot grow a sequence")
@@ -426,9 +452,11 @@ class PagedKVCache:
             self.free(seq_id)
 
     # -- batch tables --------------------------------------------------------
-    def table_rows(self, seq_ids: Sequence[int]) -> tuple[np.ndarray, np.ndarray, int]:
+    def table_rows(self, seq_ids: Sequence[int],
+                   rows: np.ndarray | None = None) -> tuple[np.ndarray, np.ndarray, int]:
         """Host ``(B, max_blocks)`` int32 tables, ``(B,)`` token counts and the width."""
-        rows = self._existing_rows(seq_ids)
+        if rows is None:
+            rows = self._existing_rows(seq_ids)
         width = max(1, int(self._nblk[rows].max())) if len(rows) else 1
         return self._table[rows, :width], self._ntok[rows].copy(), width
 

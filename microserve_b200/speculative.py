@@ -166,6 +166,7 @@ class SpeculativeDecoder:
         self._staging_v = HostStaging(self.device)  # the verify batch's blob (phase B)
         self._buf = _Buffers(self.device)
         self.last_round_launches = 0
+        self._row_cache: tuple | None = None  # see _rows_for
         # Measurement hooks (set by benchmarks): when ``round_events`` is a
         # list, each round appends a (start, end) CUDA event pair around its
         # kernels; the last round's shapes and copy sizes are kept below.
@@ -188,9 +189,10 @@ class SpeculativeDecoder:
         if not requests:
             return []
         G, B, V = self.gamma, len(requests), self.target.cfg.vocab_size
-        for cfg in {id(r.sampling): r.sampling for r in requests}.values():
+        configs = list({id(r.sampling): r.sampling for r in requests}.values())
+        for cfg in configs:
             validate(cfg)
-        plan = self._plan(requests, target_cache, generators)
+        plan = self._plan(requests, target_cache, generators, configs)
         launches0 = _lib.launch_count()
         self._launch(plan, target_cache)
         self.last_round_launches = _lib.launch_count() - launches0
@@ -203,11 +205,33 @@ class SpeculativeDecoder:
         nacc = res[B * (G + 1) : B * (G + 2)].astype(np.int64)
         return self._finish(requests, target_cache, plan, tokens, nacc)
 
+    def _rows_for(self, ids: list[int], target_cache: PagedKVCache
+                  ) -> tuple[np.ndarray | None, np.ndarray | None]:
+        """Both caches' table rows of ``ids``, kept from round to round while
+        the request list and the caches' row assignments are unchanged; (None,
+        None) while a sequence has no row yet (its first round)."""
+        key = tuple(ids)
+        c = self._row_cache
+        if (c is not None and c[0] is target_cache and c[2] == target_cache.generation
+                and c[3] == self.draft_cache.generation and c[1] == key):
+            return c[4], c[5]
+        self._row_cache = None
+        if len(set(key)) != len(key):
+            return None, None  # append_many reports the duplicate
+        trows = target_cache.rows_if_all_present(ids)
+        drows = self.draft_cache.rows_if_all_present(ids)
+        if trows is None or drows is None:
+            return None, None
+        self._row_cache = (target_cache, key, target_cache.generation,
+                           self.draft_cache.generation, trows, drows)
+        return trows, drows
+
     def _plan(
         self,
         requests: list[Request],
         target_cache: PagedKVCache,
         generators: dict[int, torch.Generator],
+        configs: list[SamplingConfig] | None = None,
     ) -> dict[str, object]:
         """What the draft passes need, packed into one blob (phase A).
 
@@ -218,14 +242,15 @@ class SpeculativeDecoder:
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
         dcache = self.draft_cache
-        d_cached = dcache.num_tokens_many(ids)
-        t_cached = target_cache.num_tokens_many(ids)
+        trows, drows = self._rows_for(ids, target_cache)
+        d_cached = dcache.num_tokens_many(ids, drows)
+        t_cached = target_cache.num_tokens_many(ids, trows)
         n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests), np.int64, B)
         n0 = n_tok - d_cached
         npre = n_tok - t_cached
         if np.any(npre < 1):
             raise ValueError("every request needs at least one uncomputed token")
-        need = target_cache.blocks_needed_many(ids, npre + G)
+        need = target_cache.blocks_needed_many(ids, npre + G, trows)
         if need > target_cache.num_free_blocks:
             raise OutOfCacheMemory(f"need {need} blocks, {target_cache.num_free_blocks} free")
         # One walk over the token lists: the longer of the two suffixes, split
@@ -236,8 +261,8 @@ class SpeculativeDecoder:
         tail_end = np.cumsum(kmax)
 
         # The draft's slots for the whole round (all-or-nothing).
-        dslots = dcache.append_many(ids, n0 + (G - 1))
-        dtab, _, dw = dcache.table_rows(ids)
+        dslots = dcache.append_many(ids, n0 + (G - 1), drows)
+        dtab, _, dw = dcache.table_rows(ids, drows)
 
         # Draft pass 0: the catch-up tokens (usually 1 or 2 per request).
         dstart = np.zeros(B + 1, np.int64)
@@ -274,7 +299,12 @@ class SpeculativeDecoder:
 
         seeds = [generators[i].initial_seed() for i in ids]
         steps = [r.rng_step for r in requests]
-        params = make_params([r.sampling for r in requests], seeds, steps)
+        if configs is not None and len(configs) == 1:  # one config shared by every request
+            params = make_params(configs, [0], [0]).repeat(B)
+            params["seed"] = seeds
+            params["step"] = steps
+        else:
+            params = make_params([r.sampling for r in requests], seeds, steps)
 
         parts = [
             params.view(np.int32),
@@ -295,6 +325,7 @@ class SpeculativeDecoder:
             "ctx0": int(ctx0.max()), "ctx_j": [int(c.max()) for c in ctx_j],
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
             "n_tok": n_tok, "qv": qv, "segv": segv, "withinv": withinv,
+            "trows": trows, "drows": drows,
             "kv_draft": int(ctx0.sum()) + sum(int(c.sum()) for c in ctx_j),
         }
 
@@ -309,8 +340,9 @@ class SpeculativeDecoder:
         qv: np.ndarray = plan["qv"]  # type: ignore[assignment]
         segv: np.ndarray = plan["segv"]  # type: ignore[assignment]
         withinv: np.ndarray = plan["withinv"]  # type: ignore[assignment]
-        tslots = target_cache.append_many(ids, npre + G)
-        ttab, _, tw = target_cache.table_rows(ids)
+        trows = plan["trows"]
+        tslots = target_cache.append_many(ids, npre + G, trows)  # type: ignore[arg-type]
+        ttab, _, tw = target_cache.table_rows(ids, trows)  # type: ignore[arg-type]
         posv = t_cached[segv] + withinv
         ctxv = t_cached + npre + G
         rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
@@ -413,9 +445,9 @@ class SpeculativeDecoder:
         ids: list[int] = plan["ids"]  # type: ignore[assignment]
         n_tok: np.ndarray = plan["n_tok"]  # type: ignore[assignment]
         keep = n_tok + nacc
-        target_cache.truncate_many(ids, keep)
+        target_cache.truncate_many(ids, keep, plan["trows"])  # type: ignore[arg-type]
         d_len = plan["d_cached"] + plan["n0"] + (G - 1)  # type: ignore[operator]
-        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep))
+        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep), plan["drows"])  # type: ignore[arg-type]
         rows = tokens.tolist()
         nacc_l = nacc.tolist()
         keep_l = keep.tolist()
@@ -436,6 +468,7 @@ class SpeculativeDecoder:
         self.draft_cache.free(seq_id)
 
     def reset(self) -> None:
+        self._row_cache = None
         self.draft_cache.reset()
         self.num_proposed = 0
         self.num_accepted = 0

@@ -141,6 +141,85 @@ class TestCacheTables:
             assert free - c.num_free_blocks == need
             c.truncate_many(ids, [max(0, c.num_tokens(i) - int(rng.integers(0, 6))) for i in ids])
 
+    def test_row_based_calls_match_id_based_calls(self) -> None:
+        rng = np.random.default_rng(3)
+        a, b = host_cache(4, 128), host_cache(4, 128)
+        ids = [8, 3, 6, 1]
+        a.append_many(ids, [1, 2, 3, 4])
+        b.append_many(ids, [1, 2, 3, 4])
+        rows = a.rows_if_all_present(ids)
+        assert rows is not None and a.rows_if_all_present([8, 99]) is None
+        assert 99 not in a.tables  # the probe created no row
+        for _ in range(6):
+            counts = rng.integers(0, 7, len(ids))
+            assert a.blocks_needed_many(ids, counts, rows) == b.blocks_needed_many(ids, counts)
+            assert a.append_many(ids, counts, rows).tolist() == b.append_many(ids, counts).tolist()
+            assert np.array_equal(a.num_tokens_many(ids, rows), b.num_tokens_many(ids))
+            ta, la, wa = a.table_rows(ids, rows)
+            tb, lb, wb = b.table_rows(ids)
+            assert wa == wb and np.array_equal(ta, tb) and np.array_equal(la, lb)
+            keep = [max(0, b.num_tokens(i) - int(rng.integers(0, 5))) for i in ids]
+            a.truncate_many(ids, keep, rows)
+            b.truncate_many(ids, keep)
+            assert a.tables == b.tables
+        a.allocator.check_invariants()
+
+    def test_generation_tracks_row_changes(self) -> None:
+        c = host_cache(4, 64)
+        g0 = c.generation
+        c.append(1, 3)
+        assert c.generation == g0 + 1
+        c.append(1, 5)
+        c.truncate(1, 2)
+        assert c.generation == g0 + 1  # token counts do not move rows
+        c.free(1)
+        assert c.generation == g0 + 2
+        c.append(2, 1)  # takes the freed row
+        assert c.generation == g0 + 3
+
+    def test_decoder_row_cache_follows_the_caches(self) -> None:
+        from microserve_b200.speculative import SpeculativeDecoder
+
+        tc, dc = host_cache(4, 64), host_cache(4, 64)
+        dec = object.__new__(SpeculativeDecoder)
+        dec.draft_cache = dc
+        dec._row_cache = None
+        ids = [4, 7]
+        assert dec._rows_for(ids, tc) == (None, None)  # no rows yet: id-based calls
+        for c in (tc, dc):
+            c.append_many(ids, [2, 2])
+        tr, dr = dec._rows_for(ids, tc)
+        assert tr.tolist() == tc.rows_of(ids).tolist() and dr.tolist() == dc.rows_of(ids).tolist()
+        assert dec._rows_for(list(ids), tc)[0] is tr  # same request list: kept
+        tc.free(4)
+        tc.append(9, 1)  # sequence 9 takes sequence 4's row
+        tc.append(4, 2)
+        tr2, _ = dec._rows_for(ids, tc)
+        assert tr2.tolist() == tc.rows_of(ids).tolist() != tr.tolist()
+        assert dec._rows_for([4, 4], tc) == (None, None)  # duplicates: append_many reports them
+
+    def test_plan_blob_is_the_same_with_a_shared_config(self) -> None:
+        import torch
+
+        from microserve_b200.speculative import SpeculativeDecoder
+
+        sc = SamplingConfig(temperature=0.7, top_p=0.8, max_new_tokens=100)
+        blobs = []
+        for configs in (None, [sc]):
+            tc, dc = host_cache(4, 256), host_cache(4, 256)
+            dec = object.__new__(SpeculativeDecoder)
+            dec.gamma, dec.draft_cache, dec._row_cache = 3, dc, None
+            reqs, gens = [], {}
+            for i, n in enumerate([5, 9, 3]):
+                r = Request(10 + i, list(range(n)), sc)
+                r.rng_step = 4 + i
+                reqs.append(r)
+                gens[r.request_id] = torch.Generator().manual_seed(100 + i)
+                tc.append(r.request_id, n - 1)
+            plan = dec._plan(reqs, tc, gens, configs)
+            blobs.append(plan["blob"])
+        assert np.array_equal(blobs[0], blobs[1])
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
