@@ -1184,8 +1184,10 @@ __device__ __forceinline__ T* cl_map(T* p, int rank) {
 // Exchange state: the CTA's rank, the cluster size and which word set is next.
 // A set written at exchange k was last read before the barrier of exchange
 // k-1, so alternating two sets needs one barrier per exchange.
+template <int C>
 struct ClX {
-  int rank, C, par;
+  static constexpr int kC = C;
+  int rank, par;
   __device__ __forceinline__ unsigned long long* slot(ClSmem& s) const { return s.xch + 8 * par; }
 };
 
@@ -1251,7 +1253,8 @@ __device__ void cl_stage(const float* __restrict__ row, int lo, int n, float tem
 }
 
 // Row maximum and first argmax from every CTA's slice result.
-__device__ void cl_argmax(ClSmem& s, ClX& x, float mloc, int aloc, float& m, int& am) {
+template <int C>
+__device__ void cl_argmax(ClSmem& s, ClX<C>& x, float mloc, int aloc, float& m, int& am) {
   unsigned long long* slot = x.slot(s);
   if (threadIdx.x == 0) {
     slot[0] = __float_as_uint(mloc);
@@ -1260,7 +1263,8 @@ __device__ void cl_argmax(ClSmem& s, ClX& x, float mloc, int aloc, float& m, int
   cl_sync();
   float best = -INFINITY;
   int bi = 0x7fffffff;
-  for (int r = 0; r < x.C; ++r) {
+#pragma unroll
+  for (int r = 0; r < C; ++r) {
     const unsigned long long* rs = cl_map(slot, r);
     const float v = __uint_as_float((uint32_t)rs[0]);
     const int i = (int)(uint32_t)rs[1];
@@ -1275,12 +1279,14 @@ __device__ void cl_argmax(ClSmem& s, ClX& x, float mloc, int aloc, float& m, int
 }
 
 // Sum of every CTA's (block-uniform) float, in rank order.
-__device__ float cl_sum(ClSmem& s, ClX& x, float v) {
+template <int C>
+__device__ float cl_sum(ClSmem& s, ClX<C>& x, float v) {
   unsigned long long* slot = x.slot(s);
   if (threadIdx.x == 0) slot[0] = __float_as_uint(v);
   cl_sync();
   float t = 0.f;
-  for (int r = 0; r < x.C; ++r) t += __uint_as_float((uint32_t)cl_map(slot, r)[0]);
+#pragma unroll
+  for (int r = 0; r < C; ++r) t += __uint_as_float((uint32_t)cl_map(slot, r)[0]);
   x.par ^= 1;
   return t;
 }
@@ -1360,20 +1366,23 @@ __device__ void cl_sub_pass(const float* xs, int n, float m, int b1, ClSmem& s) 
 // bins [rank*nb/C, (rank+1)*nb/C) over all CTAs and writes the mass and count
 // of each into every CTA's hm / hn.  Bin b's upper edge lies (e0 + b * ew) /
 // kBinsPerUnit below the maximum.  Ends with a cluster barrier.
-__device__ void cl_combine_bins(ClSmem& s, const ClX& x, int nb, float e0, float ew) {
-  const int per = nb / x.C;
+template <int C>
+__device__ void cl_combine_bins(ClSmem& s, const ClX<C>& x, int nb, float e0, float ew) {
+  const int per = nb / C;
   for (int j = threadIdx.x; j < per; j += blockDim.x) {
     const int b = x.rank * per + j;
     double acc = 0.0;
     uint32_t cnt = 0;
-    for (int r = 0; r < x.C; ++r) {
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
       const uint32_t c = cl_map(s.hc, r)[b];
       const uint32_t d = cl_map(s.hd, r)[b];
       cnt += c;
       acc += (double)c - (double)d * (1.0 / kDefScale);
     }
     const float mass = (float)acc * __expf(-(e0 + (float)b * ew) * (1.f / kBinsPerUnit));
-    for (int r = 0; r < x.C; ++r) {
+#pragma unroll
+    for (int r = 0; r < C; ++r) {
       cl_map(s.hm, r)[b] = mass;
       cl_map(s.hn, r)[b] = cnt;
     }
@@ -1497,7 +1506,8 @@ __device__ bool cl_cross(ClSmem& s, int n, float m, double before, double target
 // Fills d.thresh, d.z, d.inv_z of a staged logits row (temperature > 0, no
 // top-k) whose d.m is the row maximum.  Returns false when the row needs the
 // single-CTA path; the answer is the same in every CTA of the cluster.
-__device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX& x) {
+template <int C>
+__device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX<C>& x) {
   const float m = d.m;
   d.thresh = -INFINITY;
   const bool want_p = top_p < 1.f;
@@ -1534,7 +1544,7 @@ __device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX
   int cnt[8], total = 0;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    cnt[r] = r < x.C ? (int)cl_map(slot, r)[0] : 0;
+    cnt[r] = r < C ? (int)cl_map(slot, r)[0] : 0;
     total += cnt[r];
   }
   x.par ^= 1;
@@ -1542,7 +1552,7 @@ __device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX
   int off = 0;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    if (r < x.C) {
+    if (r < C) {
       const unsigned long long* rk = cl_map(s.kl, r);
       for (int j = threadIdx.x; j < cnt[r]; j += blockDim.x) s.km[off + j] = rk[j];
       off += cnt[r];
@@ -1565,8 +1575,8 @@ __device__ bool cl_row_stats(Dist& d, float top_p, int n, int lo, ClSmem& s, ClX
 // places u * total in one CTA (the owner), then the owner's in-slice search.
 // Ends every DSMEM use with a cluster barrier, so CTAs may exit afterwards.
 // `mine` tells the one CTA that holds the drawn token.
-template <typename W>
-__device__ void cl_draw(const W& w, int n, int lo, float u, ClSmem& s, ClX& x, int& tok,
+template <int C, typename W>
+__device__ void cl_draw(const W& w, int n, int lo, float u, ClSmem& s, ClX<C>& x, int& tok,
                         bool& mine) {
   double tot;
   int last;
@@ -1583,7 +1593,7 @@ __device__ void cl_draw(const W& w, int n, int lo, float u, ClSmem& s, ClX& x, i
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
     T[r] = 0.0;
-    if (r < x.C) {
+    if (r < C) {
       const unsigned long long* rs = cl_map(slot, r);
       T[r] = __longlong_as_double((long long)rs[0]);
       total += T[r];
@@ -1597,7 +1607,7 @@ __device__ void cl_draw(const W& w, int n, int lo, float u, ClSmem& s, ClX& x, i
   double obase = 0.0, before = 0.0;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    if (r < x.C) {
+    if (r < C) {
       if (owner < 0 && T[r] > 0.0 && before <= target && target < before + T[r]) {
         owner = r;
         obase = before;
@@ -1627,10 +1637,10 @@ __device__ __noinline__ void accept_single(AcceptArgs a, int b, int B, RowSmem s
   accept_body(a, b, B, sm);
 }
 
-__device__ __forceinline__ ClX cl_begin(int C, int S, int V, int& lo, int& n) {
-  ClX x;
+template <int C>
+__device__ __forceinline__ ClX<C> cl_begin(int S, int V, int& lo, int& n) {
+  ClX<C> x;
   x.rank = (int)cg::this_cluster().block_rank();
-  x.C = C;
   x.par = 0;
   lo = min(V, x.rank * S);
   n = min(V, lo + S) - lo;
@@ -1646,7 +1656,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kClThreads, 2)
   cl_setup(s);
   const int V = a.V;
   int lo, n;
-  ClX x = cl_begin(C, S, V, lo, n);
+  ClX<C> x = cl_begin<C>(S, V, lo, n);
   const int r = blockIdx.x / C;
   const ms_sampling_params P = a.params[a.pidx ? a.pidx[r] : r];
   const bool greedy = P.temperature == 0.f;
@@ -1721,7 +1731,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kClThreads, 2)
   cl_setup(s);
   const int V = a.V, G = a.gamma;
   int lo, n;
-  ClX x = cl_begin(C, S, V, lo, n);
+  ClX<C> x = cl_begin<C>(S, V, lo, n);
   const int B = gridDim.x / C;
   const int b = blockIdx.x / C;
   const ms_sampling_params P = a.params[b];
