@@ -925,7 +925,7 @@ __device__ __forceinline__ void sample_row_body(const SampleArgs& a, int r, RowS
   }
 }
 
-__global__ void __launch_bounds__(512, 1) sample_rows_kernel(SampleArgs a, int stage) {
+__global__ void __launch_bounds__(1024, 1) sample_rows_kernel(SampleArgs a, int stage) {
   pdl_enter();
   RowSmem sm;
   setup_smem(sm, a.V, stage != 0);
@@ -1947,6 +1947,11 @@ int row_threads(int V) {
   return t;
 }
 
+// K8 at large vocabularies: 32 warps per SM hide the shared-memory and
+// atomic latency of the row passes (256 rows x 32000: 69 -> 57 us with top-p,
+// 46 -> 36 us without, against 512 threads).
+int sample_threads(int V) { return V >= 16384 ? 1024 : row_threads(V); }
+
 int launch_accept(AcceptArgs a, int B, void* stream) {
   a.err = device_error_word();
   const int threads = row_threads(a.V);
@@ -1975,7 +1980,7 @@ extern "C" int ms_sample(const float* logits, int64_t row_stride, int n_rows, in
   if (n_rows == 0) return MS_OK;
   MS_REQUIRE(logits && params && tokens, "ms_sample: null pointer");
   MS_REQUIRE(row_stride >= vocab, "ms_sample: row_stride < vocab");
-  const int threads = row_threads(vocab);
+  const int threads = sample_threads(vocab);
   const bool stage = vocab <= kMaxStagedV;
   const size_t smem = smem_bytes(threads, vocab, stage);
   cudaError_t e = cudaFuncSetAttribute(sample_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
