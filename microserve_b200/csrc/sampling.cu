@@ -73,7 +73,62 @@ struct Dist {
     const float xv = x(i);
     return xv >= thresh ? __expf(xv - m) * inv_z : 0.f;
   }
+  // prob(i) from the row's value v = row[i] already loaded.
+  __device__ __forceinline__ float prob_of(float v, int i) const {
+    if (mode == 1) return v;
+    if (mode == 2) return i == argmax ? 1.f : 0.f;
+    const float xv = divide ? __fdiv_rn(v, temp) : v;
+    return xv >= thresh ? __expf(xv - m) * inv_z : 0.f;
+  }
 };
+
+// The rejection residual max(0, p - q) over n elements whose p values come
+// from the staged x values xs[0, n) (p in mode 0 or 2, row indices lo + j);
+// q is read from global memory at qrow[0, n).  The residual replaces xs
+// (each thread overwrites only what it has just read); returns this
+// thread's partial sum.  Four float4 loads of q per thread are in flight at
+// once: the pass is bound by the latency of those loads.
+__device__ float residual_pass(float* xs, int n, int lo, const Dist& pv, const Dist& qv,
+                               const float* __restrict__ qrow) {
+  auto pval = [&](float x, int i) {
+    if (pv.mode == 2) return i == pv.argmax ? 1.f : 0.f;
+    return x >= pv.thresh ? __expf(x - pv.m) * pv.inv_z : 0.f;
+  };
+  float part = 0.f;
+  const bool vec = (reinterpret_cast<uintptr_t>(qrow) & 15) == 0;
+  const int n4 = vec ? n >> 2 : 0;
+  const float4* q4 = reinterpret_cast<const float4*>(qrow);
+  float4* x4 = reinterpret_cast<float4*>(xs);
+  for (int base = threadIdx.x; base < n4; base += 4 * blockDim.x) {
+    float4 qa[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x;
+      qa[u] = i < n4 ? __ldg(q4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = base + u * blockDim.x;
+      if (i < n4) {
+        const float4 xa = x4[i];
+        const int g = lo + 4 * i;
+        float4 o;
+        o.x = fmaxf(pval(xa.x, g) - qv.prob_of(qa[u].x, g), 0.f);
+        o.y = fmaxf(pval(xa.y, g + 1) - qv.prob_of(qa[u].y, g + 1), 0.f);
+        o.z = fmaxf(pval(xa.z, g + 2) - qv.prob_of(qa[u].z, g + 2), 0.f);
+        o.w = fmaxf(pval(xa.w, g + 3) - qv.prob_of(qa[u].w, g + 3), 0.f);
+        x4[i] = o;
+        part += (o.x + o.y) + (o.z + o.w);
+      }
+    }
+  }
+  for (int j = (n4 << 2) + threadIdx.x; j < n; j += blockDim.x) {
+    const float r = fmaxf(pval(xs[j], lo + j) - qv.prob_of(__ldg(qrow + j), lo + j), 0.f);
+    xs[j] = r;
+    part += r;
+  }
+  return part;
+}
 
 // ---- block reductions with broadcast ---------------------------------------
 __device__ float block_sum_b(float v, RowSmem& sm) {
@@ -1052,13 +1107,7 @@ __device__ __forceinline__ void accept_body(const AcceptArgs& a, int b, int B, R
     const bool in_smem = p.mode == 0 && sm.stage != nullptr && p.row == sm.stage;
     float part = 0.f;
     if (in_smem) {
-      float* res = sm.stage;
-#pragma unroll 4
-      for (int j = threadIdx.x; j < V; j += blockDim.x) {
-        const float r = fmaxf(pv.prob(j) - qv.prob(j), 0.f);
-        res[j] = r;
-        part += r;
-      }
+      part = residual_pass(sm.stage, V, 0, pv, qv, qv.row);
     } else {
 #pragma unroll 4
       for (int j = threadIdx.x; j < V; j += blockDim.x) part += fmaxf(pv.prob(j) - qv.prob(j), 0.f);
@@ -1801,21 +1850,7 @@ __global__ void __cluster_dims__(C, 1, 1) __launch_bounds__(kClThreads, 2)
     // Rejected: draw from normalise(max(0, p - q)), or from p if that is ~0;
     // the residual replaces the staged slice.
     const Dist pv = p, qv = q;
-    float part = 0.f;
-    float* res = s.xs;
-#pragma unroll 4
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      float pj;
-      if (pv.mode == 2) {
-        pj = lo + j == pv.argmax ? 1.f : 0.f;
-      } else {
-        const float v = res[j];
-        pj = v >= pv.thresh ? __expf(v - pv.m) * pv.inv_z : 0.f;
-      }
-      const float rj = fmaxf(pj - qv.prob(lo + j), 0.f);
-      res[j] = rj;
-      part += rj;
-    }
+    const float part = residual_pass(s.xs, n, lo, pv, qv, qv.row + lo);
     const float total = cl_sum(s, x, block_sum_b(part, s.row));
     const float u2 = a.draw_u ? a.draw_u[b] : philox_uniform(P.seed, P.step, MS_LANE_RESAMPLE);
     int tok;

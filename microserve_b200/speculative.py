@@ -163,6 +163,7 @@ class SpeculativeDecoder:
         self.num_proposed = 0
         self.num_accepted = 0
         self._staging = HostStaging(self.device)
+        self._staging_d = HostStaging(self.device)  # later draft passes, verify ids, params
         self._staging_v = HostStaging(self.device)  # the verify batch's blob (phase B)
         self._buf = _Buffers(self.device)
         self.last_round_launches = 0
@@ -277,6 +278,35 @@ class SpeculativeDecoder:
         slots0 = dslots[dstart[:-1][seg0] + within0]
         ctx0 = d_cached + n0
         rows0 = q0[1:] - 1
+        parts = [ids0, pos0, slots0, q0, ctx0, n0, dtab, rows0]  # order matches batch_from_host
+        blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
+        return {
+            "blob": blob, "spans": spans, "B": B, "dw": dw, "T0": T0,
+            "max_q0": int(n0.max()), "ctx0": int(ctx0.max()), "kv_draft0": int(ctx0.sum()),
+            "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
+            "n_tok": n_tok, "trows": trows, "drows": drows, "dslots": dslots, "dstart": dstart,
+            "tails": tails, "tail_end": tail_end, "requests": requests, "generators": generators,
+            "configs": configs,
+        }
+
+    def _plan_draft(self, plan: dict[str, object]) -> None:
+        """Phase A, second part, run on the host while draft pass 0 executes:
+        the later draft passes' metadata, the verify token ids with the places
+        the proposals go, and the sampling parameters, packed into a second
+        blob."""
+        G = self.gamma
+        B = int(plan["B"])  # type: ignore[arg-type]
+        requests: list[Request] = plan["requests"]  # type: ignore[assignment]
+        generators: dict[int, torch.Generator] = plan["generators"]  # type: ignore[assignment]
+        configs: list[SamplingConfig] | None = plan["configs"]  # type: ignore[assignment]
+        ids: list[int] = plan["ids"]  # type: ignore[assignment]
+        d_cached: np.ndarray = plan["d_cached"]  # type: ignore[assignment]
+        n0: np.ndarray = plan["n0"]  # type: ignore[assignment]
+        npre: np.ndarray = plan["npre"]  # type: ignore[assignment]
+        dslots: np.ndarray = plan["dslots"]  # type: ignore[assignment]
+        dstart: np.ndarray = plan["dstart"]  # type: ignore[assignment]
+        tails: np.ndarray = plan["tails"]  # type: ignore[assignment]
+        tail_end: np.ndarray = plan["tail_end"]  # type: ignore[assignment]
         # Draft passes 1..G-1: one token per request (the previous proposal).
         unit_qs = np.arange(B + 1)
         ones = np.ones(B, np.int64)
@@ -308,9 +338,6 @@ class SpeculativeDecoder:
 
         parts = [
             params.view(np.int32),
-            # draft pass 0 batch (order matches batch_from_host)
-            ids0, pos0, slots0, q0, ctx0, n0, dtab,
-            rows0,
             # shared unit batch arrays for passes >= 1
             unit_qs, ones,
             *[a for j in range(G - 1) for a in (pos_j[j], slots_j[j], ctx_j[j])],
@@ -319,15 +346,11 @@ class SpeculativeDecoder:
             *scat,
         ]
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
-        return {
-            "blob": blob, "spans": spans, "B": B, "dw": dw, "T0": T0, "Tv": Tv,
-            "max_q0": int(n0.max()), "max_qv": int((npre + G).max()),
-            "ctx0": int(ctx0.max()), "ctx_j": [int(c.max()) for c in ctx_j],
-            "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
-            "n_tok": n_tok, "qv": qv, "segv": segv, "withinv": withinv,
-            "trows": trows, "drows": drows,
-            "kv_draft": int(ctx0.sum()) + sum(int(c.sum()) for c in ctx_j),
-        }
+        plan.update(
+            blob_d=blob, spans_d=spans, Tv=Tv, max_qv=int((npre + G).max()),
+            ctx_j=[int(c.max()) for c in ctx_j], qv=qv, segv=segv, withinv=withinv,
+            kv_draft=int(plan["kv_draft0"]) + sum(int(c.sum()) for c in ctx_j),  # type: ignore[call-overload]
+        )
 
     def _plan_verify(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
         """Phase B, run on the host while the draft passes execute: the target
@@ -358,40 +381,42 @@ class SpeculativeDecoder:
         buf = self._buf
         dev_blob = self._staging.upload(plan["blob"])  # type: ignore[arg-type]
         spans: list[tuple[int, int]] = plan["spans"]  # type: ignore[assignment]
-        v = [dev_blob[o : o + n] for o, n in spans]
         stream = _lib.stream_ptr(self.device)
-        params = v[0]
-        k = 1
-        b0 = batch_from_host(dev_blob, spans[k : k + 7], B, int(plan["dw"]), int(plan["max_q0"]),
+        b0 = batch_from_host(dev_blob, spans[0:7], B, int(plan["dw"]), int(plan["max_q0"]),
                              int(plan["T0"]), int(plan["ctx0"]))  # type: ignore[arg-type]
-        dtab = v[k + 6].view(B, int(plan["dw"]))
-        k += 7
-        rows0 = v[k]
-        k += 1
-        unit_qs, ones = v[k], v[k + 1]
-        k += 2
-        batches: list[tuple[PagedBatch, torch.Tensor | None]] = [(b0, rows0)]
-        for j in range(1, G):
-            pos, slots, ctx = v[k], v[k + 1], v[k + 2]
-            k += 3
-            bj = PagedBatch(
-                input_ids=buf.proposals[j - 1], positions=pos, slot_mapping=slots,
-                block_tables=dtab, context_lens=ctx, q_lens=ones, q_start=unit_qs, max_q=1,
-                n_tokens=B, max_context=plan["ctx_j"][j - 1],  # type: ignore[index]
-            )
-            batches.append((bj, None))
-        idsv = v[k]
-        k += 1
-        scat = v[k : k + G]
+        dtab = b0.block_tables
+        o, n = spans[7]
+        rows0 = dev_blob[o : o + n]
         ev = None
         if self.round_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             ev[0].record()
+        self.draft.forward_paged(b0, self.draft_cache, logit_rows=rows0, out=buf.dlogits[0],
+                                 out_row_stride=V)
+        # The rest of the draft side is planned while draft pass 0 runs.
+        self._plan_draft(plan)
+        dblob = self._staging_d.upload(plan["blob_d"])  # type: ignore[arg-type]
+        w = [dblob[o : o + n] for o, n in plan["spans_d"]]  # type: ignore[union-attr]
+        params = w[0]
+        unit_qs, ones = w[1], w[2]
+        k = 3
+        batches: list[PagedBatch | None] = [None]
+        for j in range(1, G):
+            pos, slots, ctx = w[k], w[k + 1], w[k + 2]
+            k += 3
+            batches.append(PagedBatch(
+                input_ids=buf.proposals[j - 1], positions=pos, slot_mapping=slots,
+                block_tables=dtab, context_lens=ctx, q_lens=ones, q_start=unit_qs, max_q=1,
+                n_tokens=B, max_context=plan["ctx_j"][j - 1],  # type: ignore[index]
+            ))
+        idsv = w[k]
+        k += 1
+        scat = w[k : k + G]
 
-        for j, (bj, rows) in enumerate(batches):
+        for j, bj in enumerate(batches):
             out = buf.dlogits[j]
-            self.draft.forward_paged(bj, self.draft_cache, logit_rows=rows, out=out,
-                                     out_row_stride=V)
+            if bj is not None:
+                self.draft.forward_paged(bj, self.draft_cache, out=out, out_row_stride=V)
             _lib.call(
                 "ms_sample", out.data_ptr(), V, B, V, params.data_ptr(), None, _lib.LANE_DRAFT + j,
                 buf.proposals[j].data_ptr(), None, buf.dstats[j].data_ptr(),
@@ -413,7 +438,7 @@ class SpeculativeDecoder:
                                  # keys each pass's attention reads, summed over requests
                                  "kv_tokens_verify": int(plan["kv_verify"]),  # type: ignore[arg-type]
                                  "kv_tokens_draft": int(plan["kv_draft"])}  # type: ignore[arg-type]
-        self.last_h2d_bytes = int(plan["blob"].nbytes) + int(plan["blob_v"].nbytes)  # type: ignore[union-attr]
+        self.last_h2d_bytes = sum(int(plan[k].nbytes) for k in ("blob", "blob_d", "blob_v"))  # type: ignore[union-attr]
         self.last_d2h_bytes = B * (G + 2) * 4
         vev = None
         if self.verify_events is not None:

@@ -217,8 +217,10 @@ class TestCacheTables:
                 gens[r.request_id] = torch.Generator().manual_seed(100 + i)
                 tc.append(r.request_id, n - 1)
             plan = dec._plan(reqs, tc, gens, configs)
-            blobs.append(plan["blob"])
-        assert np.array_equal(blobs[0], blobs[1])
+            dec._plan_draft(plan)
+            blobs.append((plan["blob"], plan["blob_d"]))
+        assert np.array_equal(blobs[0][0], blobs[1][0])
+        assert np.array_equal(blobs[0][1], blobs[1][1])
 
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
