@@ -96,7 +96,10 @@ MS_API int ms_philox_uniforms(const uint64_t* seeds, const uint64_t* steps, int 
  * sample_from_probs, sample).  Optional outputs (nullable):
  *   probs (n_rows x vocab): the exact distribution drawn from;
  *   stats: per-row ms_row_stats;
- *   scatter_dst[scatter_idx[r]] = token (a second copy of the token). */
+ *   scatter_dst[scatter_idx[r]] = token (a second copy of the token).
+ * Vocabularies up to 40,960 take one CTA per row; larger ones a
+ * thread-block cluster of 4 or 8 CTAs per row (ms_spec_accept likewise,
+ * per request, when draft_stats is given). */
 MS_API int ms_sample(const float* logits, int64_t row_stride, int n_rows, int vocab,
               const ms_sampling_params* params, const int32_t* pidx, int lane,
               int32_t* tokens, float* probs, ms_row_stats* stats,
