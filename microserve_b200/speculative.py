@@ -242,6 +242,7 @@ class SpeculativeDecoder:
         """
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
+        gens = [generators[i] for i in ids]  # a missing generator fails before any change
         dcache = self.draft_cache
         trows, drows = self._rows_for(ids, target_cache)
         d_cached = dcache.num_tokens_many(ids, drows)
@@ -285,7 +286,7 @@ class SpeculativeDecoder:
             "max_q0": int(n0.max()), "ctx0": int(ctx0.max()), "kv_draft0": int(ctx0.sum()),
             "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
             "n_tok": n_tok, "trows": trows, "drows": drows, "dslots": dslots, "dstart": dstart,
-            "tails": tails, "tail_end": tail_end, "requests": requests, "generators": generators,
+            "tails": tails, "tail_end": tail_end, "requests": requests, "gens": gens,
             "configs": configs,
         }
 
@@ -297,9 +298,8 @@ class SpeculativeDecoder:
         G = self.gamma
         B = int(plan["B"])  # type: ignore[arg-type]
         requests: list[Request] = plan["requests"]  # type: ignore[assignment]
-        generators: dict[int, torch.Generator] = plan["generators"]  # type: ignore[assignment]
+        gens: list[torch.Generator] = plan["gens"]  # type: ignore[assignment]
         configs: list[SamplingConfig] | None = plan["configs"]  # type: ignore[assignment]
-        ids: list[int] = plan["ids"]  # type: ignore[assignment]
         d_cached: np.ndarray = plan["d_cached"]  # type: ignore[assignment]
         n0: np.ndarray = plan["n0"]  # type: ignore[assignment]
         npre: np.ndarray = plan["npre"]  # type: ignore[assignment]
@@ -327,7 +327,7 @@ class SpeculativeDecoder:
         idsv[is_prefix] = tails[tail_end[segp] - npre[segp] + withinv[is_prefix]]
         scat = [qv[:-1] + npre + j for j in range(G)]
 
-        seeds = [generators[i].initial_seed() for i in ids]
+        seeds = [g.initial_seed() for g in gens]
         steps = [r.rng_step for r in requests]
         if configs is not None and len(configs) == 1:  # one config shared by every request
             params = make_params(configs, [0], [0]).repeat(B)

@@ -222,6 +222,29 @@ class TestCacheTables:
         assert np.array_equal(blobs[0][0], blobs[1][0])
         assert np.array_equal(blobs[0][1], blobs[1][1])
 
+    def test_plan_without_a_generator_changes_nothing(self) -> None:
+        import torch
+
+        from microserve_b200.speculative import SpeculativeDecoder
+
+        sc = SamplingConfig(temperature=0.7, max_new_tokens=100)
+        tc, dc = host_cache(4, 256), host_cache(4, 256)
+        dec = object.__new__(SpeculativeDecoder)
+        dec.gamma, dec.draft_cache, dec._row_cache = 3, dc, None
+        reqs = [Request(20 + i, list(range(6)), sc) for i in range(3)]
+        for r in reqs:
+            tc.append(r.request_id, 5)
+            dc.append(r.request_id, 2)
+        gens = {r.request_id: torch.Generator().manual_seed(1) for r in reqs[:2]}
+        def state():
+            return ({k: (c.tables[k].blocks, c.tables[k].num_tokens) for c in (tc, dc) for k in c.tables},
+                    tc.num_free_blocks, dc.num_free_blocks)
+
+        before = state()
+        with pytest.raises(KeyError):
+            dec._plan(reqs, tc, gens, [sc])
+        assert state() == before
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
