@@ -245,6 +245,104 @@ class TestCacheTables:
             dec._plan(reqs, tc, gens, [sc])
         assert state() == before
 
+    def test_round_metadata_matches_a_per_request_construction(self) -> None:
+        """The three blobs of one speculative round (draft pass 0, the later
+        draft passes with the verify ids, the verify batch) against each
+        request's values built one by one from the cache tables
+        (reference speculative.py:115-155, :158-190 and batching.py:19-63)."""
+        import torch
+
+        from microserve_b200.speculative import SpeculativeDecoder
+
+        G, bs = 3, 4
+        sc = SamplingConfig(temperature=0.9, top_p=0.8, max_new_tokens=100)
+        tc, dc = host_cache(bs, 256), host_cache(bs, 256)
+        dec = object.__new__(SpeculativeDecoder)
+        dec.gamma, dec.draft_cache, dec._row_cache = G, dc, None
+        # (prompt length, generated tokens, target cached, draft cached)
+        shapes = [(9, 0, 8, 8), (5, 3, 7, 6), (6, 2, 7, 7), (11, 1, 10, 3), (3, 4, 6, 5)]
+        reqs, gens = [], {}
+        for i, (lp, lo, tcd, dcd) in enumerate(shapes):
+            r = Request(30 + i, [100 + 7 * i + k for k in range(lp)], sc)
+            r.output_ids = [900 + 3 * i + k for k in range(lo)]
+            r.rng_step = i
+            reqs.append(r)
+            gens[r.request_id] = torch.Generator().manual_seed(50 + i)
+            tc.append(r.request_id, tcd)
+            dc.append(r.request_id, dcd)
+        dcached = [dc.num_tokens(r.request_id) for r in reqs]
+        tcached = [tc.num_tokens(r.request_id) for r in reqs]
+        plan = dec._plan(reqs, tc, gens, [sc])
+        dec._plan_draft(plan)
+        dec._plan_verify(plan, tc)
+
+        def parts(blob_key: str, span_key: str) -> list[list[int]]:
+            blob = plan[blob_key]
+            return [blob[o : o + n].tolist() for o, n in plan[span_key]]
+
+        a0 = parts("blob", "spans")
+        ad = parts("blob_d", "spans_d")
+        av = parts("blob_v", "spans_v")
+        B = len(reqs)
+        ids0, pos0, slots0, q0, ctx0, n0, dtab, rows0 = a0
+        e = {k: [] for k in ("ids0", "pos0", "slots0", "q0", "ctx0", "n0", "rows0")}
+        e["q0"].append(0)
+        for r, dcd in zip(reqs, dcached):
+            toks = r.prompt_ids + r.output_ids
+            k = len(toks) - dcd
+            e["ids0"] += toks[dcd:]
+            e["pos0"] += list(range(dcd, dcd + k))
+            e["slots0"] += [dc.tables[r.request_id].slot(p_, bs) for p_ in range(dcd, dcd + k)]
+            e["q0"].append(e["q0"][-1] + k)
+            e["ctx0"].append(dcd + k)
+            e["n0"].append(k)
+            e["rows0"].append(e["q0"][-1] - 1)
+        assert (ids0, pos0, slots0, q0, ctx0, n0, rows0) == (
+            e["ids0"], e["pos0"], e["slots0"], e["q0"], e["ctx0"], e["n0"], e["rows0"])
+        width = len(dtab) // B
+        for b, r in enumerate(reqs):
+            blocks = dc.tables[r.request_id].blocks
+            assert dtab[b * width : b * width + len(blocks)] == blocks
+        # later draft passes: one token each, positions after the catch-up
+        assert ad[1] == list(range(B + 1)) and ad[2] == [1] * B
+        for j in range(1, G):
+            pos, slots, ctx = ad[3 * j], ad[3 * j + 1], ad[3 * j + 2]
+            want_pos = [dcd + k + j - 1 for dcd, k in zip(dcached, e["n0"])]
+            assert pos == want_pos
+            assert slots == [dc.tables[r.request_id].slot(p_, bs) for r, p_ in zip(reqs, want_pos)]
+            assert ctx == [p_ + 1 for p_ in want_pos]
+        # verify: uncomputed tokens then G proposal places per request
+        idsv, scat = ad[3 * G], ad[3 * G + 1 :]
+        posv, tslots, qv, ctxv, qlv, ttab, rowsv = av
+        want_ids, want_pos, want_slots, want_q, want_scat = [], [], [], [0], [[] for _ in range(G)]
+        for r, tcd in zip(reqs, tcached):
+            toks = r.prompt_ids + r.output_ids
+            npre = len(toks) - tcd
+            base = want_q[-1]
+            for j in range(G):
+                want_scat[j].append(base + npre + j)
+            want_ids += toks[tcd:] + [0] * G
+            want_pos += list(range(tcd, tcd + npre + G))
+            want_slots += [tc.tables[r.request_id].slot(p_, bs) for p_ in range(tcd, tcd + npre + G)]
+            want_q.append(base + npre + G)
+        assert idsv == want_ids and scat == want_scat
+        assert posv == want_pos and tslots == want_slots and qv == want_q
+        assert ctxv == [tcd + (q1 - q0_) for tcd, q0_, q1 in zip(tcached, want_q, want_q[1:])]
+        assert qlv == [q1 - q0_ for q0_, q1 in zip(want_q, want_q[1:])]
+        assert rowsv == [q - (G + 1) + i for q in want_q[1:] for i in range(G + 1)]
+        wt = len(ttab) // B
+        for b, r in enumerate(reqs):
+            blocks = tc.tables[r.request_id].blocks
+            assert ttab[b * wt : b * wt + len(blocks)] == blocks
+        # sampling parameters: one entry per request, its generator's seed and its step
+        from microserve_b200 import _lib
+
+        o, n = plan["spans_d"][0]
+        params = np.frombuffer(plan["blob_d"][o : o + n].tobytes(), dtype=_lib.SAMPLING_PARAMS_DTYPE)
+        assert params["seed"].tolist() == [gens[r.request_id].initial_seed() for r in reqs]
+        assert params["step"].tolist() == [r.rng_step for r in reqs]
+        assert np.allclose(params["temperature"], 0.9) and np.allclose(params["top_p"], 0.8)
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
