@@ -343,6 +343,46 @@ class TestCacheTables:
         assert params["step"].tolist() == [r.rng_step for r in reqs]
         assert np.allclose(params["temperature"], 0.9) and np.allclose(params["top_p"], 0.8)
 
+    def test_round_rollback_follows_the_reference(self) -> None:
+        """After a round, the target keeps n_tokens + accepted, the draft
+        min(its length, that), and each request gets its accepted prefix plus
+        one token (reference speculative.py:191-226)."""
+        import torch
+
+        from microserve_b200.speculative import SpeculativeDecoder
+
+        G, bs = 4, 4
+        sc = SamplingConfig(temperature=0.7, max_new_tokens=100)
+        tc, dc = host_cache(bs, 256), host_cache(bs, 256)
+        dec = object.__new__(SpeculativeDecoder)
+        dec.gamma, dec.draft_cache, dec._row_cache = G, dc, None
+        dec.num_proposed = dec.num_accepted = 0
+        reqs, gens = [], {}
+        for i, lp in enumerate([7, 12, 5, 9]):
+            r = Request(40 + i, list(range(lp)), sc)
+            reqs.append(r)
+            gens[r.request_id] = torch.Generator().manual_seed(i)
+            tc.append(r.request_id, lp - 1)
+            dc.append(r.request_id, lp - 1)
+        n_tok = [len(r.prompt_ids) for r in reqs]
+        plan = dec._plan(reqs, tc, gens, [sc])
+        dec._plan_draft(plan)
+        dec._plan_verify(plan, tc)
+        d_len = [dc.num_tokens(r.request_id) for r in reqs]
+        nacc = np.array([0, 4, 2, 1])
+        tokens = np.arange(len(reqs) * (G + 1), dtype=np.int32).reshape(len(reqs), G + 1) + 500
+        out = dec._finish(reqs, tc, plan, tokens, nacc)
+        for b, r in enumerate(reqs):
+            keep = n_tok[b] + int(nacc[b])
+            assert out[b] == tokens[b, : nacc[b] + 1].tolist()
+            assert tc.num_tokens(r.request_id) == keep == r.num_computed
+            assert dc.num_tokens(r.request_id) == min(d_len[b], keep)
+            assert len(tc.tables[r.request_id].blocks) == -(-keep // bs)
+            assert (r.num_draft_proposed, r.num_draft_accepted, r.rng_step) == (G, nacc[b], 1)
+        assert (dec.num_proposed, dec.num_accepted) == (G * len(reqs), int(nacc.sum()))
+        tc.allocator.check_invariants()
+        dc.allocator.check_invariants()
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
