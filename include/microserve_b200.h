@@ -151,6 +151,35 @@ typedef struct {
   void* const* v_pool;
 } ms_kv_cache;
 
+/* Host-side block-table bookkeeping (no GPU work).  The table is a dense
+ * int32 array, `stride` entries per row; row r holds ntok[r] tokens in
+ * nblk[r] blocks.  Rows of one call must be distinct.
+ *
+ * Blocks that appending counts[i] tokens to rows[i] takes beyond the blocks
+ * each row holds, summed; *max_blocks (nullable) = the widest row after it
+ * (reference cache.py:148-153 PagedKVCache.blocks_needed, over a batch). */
+MS_API int64_t ms_host_blocks_needed(const int64_t* rows, const int64_t* counts, int n,
+                                     const int64_t* ntok, const int32_t* nblk,
+                                     int block_size, int64_t* max_blocks);
+
+/* Append counts[i] tokens to rows[i]: the rows take the n_blocks new
+ * `blocks` in batch order, and out_slots receives the slot of every new
+ * token, row by row (reference cache.py:155-171 PagedKVCache.append, over a
+ * batch).  Checks the whole batch before changing anything. */
+MS_API int ms_host_append(const int64_t* rows, const int64_t* counts, int n, int64_t* ntok,
+                          int32_t* nblk, int32_t* table, int64_t stride, int block_size,
+                          const int32_t* blocks, int64_t n_blocks, int64_t* out_slots);
+
+/* Shrink rows[i] to num_tokens[i] tokens; the blocks past each new end go
+ * to out_blocks, row by row in table order.  Returns their number, -1 if a
+ * row would grow, -2 for bad sizes or too small an out_blocks; nothing
+ * changes on an error (reference cache.py:210-222 PagedKVCache.truncate,
+ * over a batch). */
+MS_API int64_t ms_host_truncate(const int64_t* rows, const int64_t* num_tokens, int n,
+                                int64_t* ntok, int32_t* nblk, const int32_t* table,
+                                int64_t stride, int block_size, int32_t* out_blocks,
+                                int64_t out_capacity);
+
 /* Scatter (T, n_kv_heads, d_head) float keys/values into one layer's pools
  * at `slots` (reference cache.py:225-234 PagedKVCache.write). */
 MS_API int ms_kv_write(const ms_kv_cache* cache, int layer, const int32_t* slots,

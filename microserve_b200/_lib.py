@@ -133,6 +133,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,
          c_void_p],
     ),
+    "ms_host_blocks_needed": (c_int64, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int,
+                                        c_void_p]),
+    "ms_host_append": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int64,
+                               c_int, c_void_p, c_int64, c_void_p]),
+    "ms_host_truncate": (c_int64, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p,
+                                   c_int64, c_int, c_void_p, c_int64]),
     "ms_kv_write": (c_int, [POINTER(MsKVCache), c_int, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "ms_kv_gather": (
         c_int,

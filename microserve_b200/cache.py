@@ -30,6 +30,11 @@ from . import _lib
 from .config import CacheConfig, ModelConfig
 
 
+def _addr(a: np.ndarray) -> int:
+    """Address of a contiguous numpy array's data (for the host helpers)."""
+    return a.__array_interface__["data"][0]
+
+
 class OutOfCacheMemory(RuntimeError):
     """Raised when the block pool cannot satisfy an allocation."""
 
@@ -214,6 +219,7 @@ class PagedKVCache:
         # may keep ``rows_of`` results while it is unchanged.
         self.generation = 0
         self._table = np.zeros((8, self._max_blocks), dtype=np.int32)
+        self._freed = np.empty(cache.num_blocks, dtype=np.int32)  # truncate_many's output
         self._nblk = np.zeros(8, dtype=np.int32)
         self._ntok = np.zeros(8, dtype=np.int64)
 
@@ -279,11 +285,14 @@ class PagedKVCache:
                            rows: np.ndarray | None = None) -> int:
         """Total extra blocks ``append_many(seq_ids, counts)`` would take (no change).
         ``rows``: the sequences' ``rows_of`` result, when the caller has it."""
-        counts = np.asarray(counts, dtype=np.int64)
+        counts = np.ascontiguousarray(counts, dtype=np.int64)
         if rows is not None:
-            bs = self.block_size
-            need = (self._ntok[rows] + counts + bs - 1) // bs - self._nblk[rows]
-            return int(np.maximum(need, 0).sum())
+            rows = np.ascontiguousarray(rows, dtype=np.int64)
+            if counts.shape != rows.shape:
+                raise ValueError("blocks_needed_many: one count per sequence")
+            return int(_lib.load().ms_host_blocks_needed(
+                _addr(rows), _addr(counts), len(rows), _addr(self._ntok), _addr(self._nblk),
+                self.block_size, None))
         get = self._rows.get
         rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
         known = rows >= 0
@@ -376,36 +385,33 @@ class PagedKVCache:
         table if the pool cannot hold every sequence's new blocks.  ``rows``:
         the (distinct) sequences' ``rows_of`` result, when the caller has it.
         """
-        counts = np.asarray(counts, dtype=np.int64)
+        counts = np.ascontiguousarray(counts, dtype=np.int64)
         if rows is None:
             if len(set(seq_ids)) != len(seq_ids):
                 raise ValueError("append_many: a sequence appears twice in one batch")
             rows = self.rows_of(seq_ids)
         if counts.size == 0:
             return np.zeros(0, dtype=np.int64)
-        bs = self.block_size
-        ntok = self._ntok[rows]
-        nblk = self._nblk[rows].astype(np.int64)
-        need = np.maximum(0, (ntok + counts + bs - 1) // bs - nblk)
-        total = int(need.sum())
+        rows = np.ascontiguousarray(rows, dtype=np.int64)
+        if counts.shape != rows.shape:
+            raise ValueError("append_many: one count per sequence")
+        lib = _lib.load()
+        widest = ctypes.c_int64(0)
+        total = int(lib.ms_host_blocks_needed(_addr(rows), _addr(counts), len(rows),
+                                              _addr(self._ntok), _addr(self._nblk),
+                                              self.block_size, ctypes.addressof(widest)))
         if total > self.allocator.num_free:
             raise OutOfCacheMemory(f"need {total} blocks, {self.allocator.num_free} free")
         if total:
-            self._ensure_columns(int((nblk + need).max()))
-            blocks = self.allocator.allocate_many(total)
-            # sequence i takes the next need[i] blocks, in batch order
-            owner = np.repeat(np.arange(len(rows)), need)
-            first = np.repeat(np.cumsum(need) - need, need)
-            self._table[rows[owner], nblk[owner] + (np.arange(total) - first)] = blocks
-            self._nblk[rows] = (nblk + need).astype(np.int32)
-        # positions ntok .. ntok+count-1 of each sequence, flattened
-        n_total = int(counts.sum())
-        seq_idx = np.repeat(np.arange(len(rows)), counts)
-        starts = np.repeat(np.cumsum(counts) - counts, counts)
-        positions = ntok[seq_idx] + (np.arange(n_total) - starts)
-        row_rep = rows[seq_idx]
-        slots = self._table[row_rep, positions // bs].astype(np.int64) * bs + positions % bs
-        self._ntok[rows] = ntok + counts
+            self._ensure_columns(int(widest.value))
+        # sequence i takes the next blocks it needs, in batch order
+        blocks = np.asarray(self.allocator.allocate_many(total), dtype=np.int32)
+        slots = np.empty(int(counts.sum()), dtype=np.int64)
+        rc = lib.ms_host_append(_addr(rows), _addr(counts), len(rows), _addr(self._ntok),
+                                _addr(self._nblk), _addr(self._table), self._table.shape[1],
+                                self.block_size, _addr(blocks), total, _addr(slots))
+        if rc != 0:
+            raise RuntimeError(lib.ms_last_error().decode())
         return slots
 
     def free(self, seq_id: int) -> None:
@@ -430,21 +436,28 @@ class PagedKVCache:
         """Vectorised ``truncate`` (speculative rollback, reference cache.py:210-222)."""
         if rows is None:
             rows = self._existing_rows(seq_ids)
-        n = np.asarray(num_tokens, dtype=np.int64)
-        if np.any(n > self._ntok[rows]):
+        rows = np.ascontiguousarray(rows, dtype=np.int64)
+        n = np.ascontiguousarray(num_tokens, dtype=np.int64)
+        if n.shape != rows.shape:
+            raise ValueError("truncate_many: one token count per sequence")
+        lib = _lib.load()
+        for _ in range(2):
+            freed = self._freed
+            k = int(lib.ms_host_truncate(
+                _addr(rows), _addr(n), len(rows), _addr(self._ntok), _addr(self._nblk),
+                _addr(self._table), self._table.shape[1], self.block_size, _addr(freed),
+                freed.size))
+            if k != -2:
+                break
+            # shared blocks can appear in several rows: make room for every entry
+            self._freed = np.empty(int(self._nblk[rows].sum()) + 1, dtype=np.int32)
+        if k == -1:
             raise ValueError("truncate cannot grow a sequence")
-        keep = (n + self.block_size - 1) // self.block_size
-        nblk = self._nblk[rows].astype(np.int64)
-        drop = np.maximum(nblk - keep, 0)
-        total = int(drop.sum())
-        if total:
+        if k < 0:
+            raise RuntimeError("truncate_many: bad sizes")
+        if k:
             # blocks past the new end, sequence by sequence, in table order
-            owner = np.repeat(np.arange(len(rows)), drop)
-            first = np.repeat(np.cumsum(drop) - drop, drop)
-            cols = keep[owner] + (np.arange(total) - first)
-            self.allocator.free_many(self._table[rows[owner], cols])
-        self._nblk[rows] = np.minimum(nblk, keep).astype(np.int32)
-        self._ntok[rows] = n
+            self.allocator.free_many(freed[:k])
 
     def reset(self) -> None:
         """Drop every sequence and return all blocks to the pool."""

@@ -383,6 +383,21 @@ class TestCacheTables:
         tc.allocator.check_invariants()
         dc.allocator.check_invariants()
 
+    def test_batched_truncate_and_append_change_nothing_on_error(self) -> None:
+        c = host_cache(4, 64)
+        c.append_many([1, 2, 3], [9, 5, 7])
+        snap = ({k: (c.tables[k].blocks, c.tables[k].num_tokens) for k in c.tables},
+                c.num_free_blocks)
+        with pytest.raises(ValueError, match="cannot grow"):
+            c.truncate_many([1, 2, 3], [4, 6, 2])  # sequence 2 would grow
+        with pytest.raises(OutOfCacheMemory):
+            c.append_many([1, 2, 3], [1, 1, 500])
+        with pytest.raises(ValueError):
+            c.truncate_many([1, 2], [3])
+        assert ({k: (c.tables[k].blocks, c.tables[k].num_tokens) for k in c.tables},
+                c.num_free_blocks) == snap
+        c.allocator.check_invariants()
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
