@@ -27,7 +27,7 @@ from __future__ import annotations
 
 import ctypes
 import itertools
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -138,6 +138,59 @@ class _Buffers:
         self.out_host = self.get("out_host", B * (G + 2), i32, pinned=True)
 
 
+def _empty(dtype: type = np.int64) -> np.ndarray:
+    return np.zeros(0, dtype)
+
+
+@dataclass
+class _RoundPlan:
+    """What a round's three host phases compute.  :meth:`SpeculativeDecoder._plan`
+    fills the first group (draft pass 0, before any launch), ``_plan_draft``
+    the second (while pass 0 runs), ``_plan_verify`` the third (while the
+    draft passes run).  Each ``blob*`` is one pinned upload, ``spans*`` the
+    (offset, size) of its parts."""
+
+    blob: np.ndarray
+    spans: list[tuple[int, int]]
+    B: int
+    dw: int
+    T0: int
+    max_q0: int
+    ctx0: int
+    kv_draft0: int
+    ids: list[int]
+    requests: list[Request]
+    gens: list[torch.Generator]
+    configs: list[SamplingConfig] | None
+    n_tok: np.ndarray
+    n0: np.ndarray
+    npre: np.ndarray
+    d_cached: np.ndarray
+    t_cached: np.ndarray
+    trows: np.ndarray | None
+    drows: np.ndarray | None
+    dslots: np.ndarray
+    dstart: np.ndarray
+    tails: np.ndarray
+    tail_end: np.ndarray
+    # later draft passes, verify token ids, sampling parameters
+    blob_d: np.ndarray = field(default_factory=lambda: _empty(np.int32))
+    spans_d: list[tuple[int, int]] = field(default_factory=list)
+    Tv: int = 0
+    max_qv: int = 0
+    ctx_j: list[int] = field(default_factory=list)
+    qv: np.ndarray = field(default_factory=_empty)
+    segv: np.ndarray = field(default_factory=_empty)
+    withinv: np.ndarray = field(default_factory=_empty)
+    kv_draft: int = 0
+    # the verify batch
+    blob_v: np.ndarray = field(default_factory=lambda: _empty(np.int32))
+    spans_v: list[tuple[int, int]] = field(default_factory=list)
+    tw: int = 0
+    ctxv: int = 0
+    kv_verify: int = 0
+
+
 class SpeculativeDecoder:
     """Batched draft-then-verify over decoding requests (reference speculative.py:89-261)."""
 
@@ -233,7 +286,7 @@ class SpeculativeDecoder:
         target_cache: PagedKVCache,
         generators: dict[int, torch.Generator],
         configs: list[SamplingConfig] | None = None,
-    ) -> dict[str, object]:
+    ) -> _RoundPlan:
         """What the draft passes need, packed into one blob (phase A).
 
         The round stays all-or-nothing: the target cache's room for the round
@@ -281,32 +334,31 @@ class SpeculativeDecoder:
         rows0 = q0[1:] - 1
         parts = [ids0, pos0, slots0, q0, ctx0, n0, dtab, rows0]  # order matches batch_from_host
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
-        return {
-            "blob": blob, "spans": spans, "B": B, "dw": dw, "T0": T0,
-            "max_q0": int(n0.max()), "ctx0": int(ctx0.max()), "kv_draft0": int(ctx0.sum()),
-            "n0": n0, "npre": npre, "d_cached": d_cached, "t_cached": t_cached, "ids": ids,
-            "n_tok": n_tok, "trows": trows, "drows": drows, "dslots": dslots, "dstart": dstart,
-            "tails": tails, "tail_end": tail_end, "requests": requests, "gens": gens,
-            "configs": configs,
-        }
+        return _RoundPlan(
+            blob=blob, spans=spans, B=B, dw=dw, T0=T0, max_q0=int(n0.max()),
+            ctx0=int(ctx0.max()), kv_draft0=int(ctx0.sum()), ids=ids, requests=requests,
+            gens=gens, configs=configs, n_tok=n_tok, n0=n0, npre=npre, d_cached=d_cached,
+            t_cached=t_cached, trows=trows, drows=drows, dslots=dslots, dstart=dstart,
+            tails=tails, tail_end=tail_end,
+        )
 
-    def _plan_draft(self, plan: dict[str, object]) -> None:
+    def _plan_draft(self, plan: _RoundPlan) -> None:
         """Phase A, second part, run on the host while draft pass 0 executes:
         the later draft passes' metadata, the verify token ids with the places
         the proposals go, and the sampling parameters, packed into a second
         blob."""
         G = self.gamma
-        B = int(plan["B"])  # type: ignore[arg-type]
-        requests: list[Request] = plan["requests"]  # type: ignore[assignment]
-        gens: list[torch.Generator] = plan["gens"]  # type: ignore[assignment]
-        configs: list[SamplingConfig] | None = plan["configs"]  # type: ignore[assignment]
-        d_cached: np.ndarray = plan["d_cached"]  # type: ignore[assignment]
-        n0: np.ndarray = plan["n0"]  # type: ignore[assignment]
-        npre: np.ndarray = plan["npre"]  # type: ignore[assignment]
-        dslots: np.ndarray = plan["dslots"]  # type: ignore[assignment]
-        dstart: np.ndarray = plan["dstart"]  # type: ignore[assignment]
-        tails: np.ndarray = plan["tails"]  # type: ignore[assignment]
-        tail_end: np.ndarray = plan["tail_end"]  # type: ignore[assignment]
+        B = plan.B
+        requests = plan.requests
+        gens = plan.gens
+        configs = plan.configs
+        d_cached = plan.d_cached
+        n0 = plan.n0
+        npre = plan.npre
+        dslots = plan.dslots
+        dstart = plan.dstart
+        tails = plan.tails
+        tail_end = plan.tail_end
         # Draft passes 1..G-1: one token per request (the previous proposal).
         unit_qs = np.arange(B + 1)
         ones = np.ones(B, np.int64)
@@ -346,44 +398,44 @@ class SpeculativeDecoder:
             *scat,
         ]
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
-        plan.update(
-            blob_d=blob, spans_d=spans, Tv=Tv, max_qv=int((npre + G).max()),
-            ctx_j=[int(c.max()) for c in ctx_j], qv=qv, segv=segv, withinv=withinv,
-            kv_draft=int(plan["kv_draft0"]) + sum(int(c.sum()) for c in ctx_j),  # type: ignore[call-overload]
-        )
+        plan.blob_d, plan.spans_d, plan.Tv = blob, spans, Tv
+        plan.max_qv = int((npre + G).max())
+        plan.ctx_j = [int(c.max()) for c in ctx_j]
+        plan.qv, plan.segv, plan.withinv = qv, segv, withinv
+        plan.kv_draft = plan.kv_draft0 + sum(int(c.sum()) for c in ctx_j)
 
-    def _plan_verify(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
+    def _plan_verify(self, plan: _RoundPlan, target_cache: PagedKVCache) -> None:
         """Phase B, run on the host while the draft passes execute: the target
         cache's slots (room checked in :meth:`_plan`) and the verify batch's
-        metadata, packed into a second blob."""
+        metadata, packed into a third blob."""
         G = self.gamma
-        ids: list[int] = plan["ids"]  # type: ignore[assignment]
-        npre: np.ndarray = plan["npre"]  # type: ignore[assignment]
-        t_cached: np.ndarray = plan["t_cached"]  # type: ignore[assignment]
-        qv: np.ndarray = plan["qv"]  # type: ignore[assignment]
-        segv: np.ndarray = plan["segv"]  # type: ignore[assignment]
-        withinv: np.ndarray = plan["withinv"]  # type: ignore[assignment]
-        trows = plan["trows"]
-        tslots = target_cache.append_many(ids, npre + G, trows)  # type: ignore[arg-type]
-        ttab, _, tw = target_cache.table_rows(ids, trows)  # type: ignore[arg-type]
+        ids = plan.ids
+        npre = plan.npre
+        t_cached = plan.t_cached
+        qv = plan.qv
+        segv = plan.segv
+        withinv = plan.withinv
+        trows = plan.trows
+        tslots = target_cache.append_many(ids, npre + G, trows)
+        ttab, _, tw = target_cache.table_rows(ids, trows)
         posv = t_cached[segv] + withinv
         ctxv = t_cached + npre + G
         rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
         parts = [posv, tslots, qv, ctxv, npre + G, ttab, rowsv]
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
-        plan.update(blob_v=blob, spans_v=spans, tw=tw, ctxv=int(ctxv.max()),
-                    kv_verify=int(ctxv.sum()))
+        plan.blob_v, plan.spans_v, plan.tw = blob, spans, tw
+        plan.ctxv, plan.kv_verify = int(ctxv.max()), int(ctxv.sum())
 
-    def _launch(self, plan: dict[str, object], target_cache: PagedKVCache) -> None:
+    def _launch(self, plan: _RoundPlan, target_cache: PagedKVCache) -> None:
         G, V = self.gamma, self.target.cfg.vocab_size
-        B = int(plan["B"])  # type: ignore[arg-type]
+        B = plan.B
         self._buf.round_views(B, G, V)
         buf = self._buf
-        dev_blob = self._staging.upload(plan["blob"])  # type: ignore[arg-type]
-        spans: list[tuple[int, int]] = plan["spans"]  # type: ignore[assignment]
+        dev_blob = self._staging.upload(plan.blob)
+        spans = plan.spans
         stream = _lib.stream_ptr(self.device)
-        b0 = batch_from_host(dev_blob, spans[0:7], B, int(plan["dw"]), int(plan["max_q0"]),
-                             int(plan["T0"]), int(plan["ctx0"]))  # type: ignore[arg-type]
+        b0 = batch_from_host(dev_blob, spans[0:7], B, plan.dw, plan.max_q0,
+                             plan.T0, plan.ctx0)
         dtab = b0.block_tables
         o, n = spans[7]
         rows0 = dev_blob[o : o + n]
@@ -395,8 +447,8 @@ class SpeculativeDecoder:
                                  out_row_stride=V)
         # The rest of the draft side is planned while draft pass 0 runs.
         self._plan_draft(plan)
-        dblob = self._staging_d.upload(plan["blob_d"])  # type: ignore[arg-type]
-        w = [dblob[o : o + n] for o, n in plan["spans_d"]]  # type: ignore[union-attr]
+        dblob = self._staging_d.upload(plan.blob_d)
+        w = [dblob[o : o + n] for o, n in plan.spans_d]
         params = w[0]
         unit_qs, ones = w[1], w[2]
         k = 3
@@ -407,7 +459,7 @@ class SpeculativeDecoder:
             batches.append(PagedBatch(
                 input_ids=buf.proposals[j - 1], positions=pos, slot_mapping=slots,
                 block_tables=dtab, context_lens=ctx, q_lens=ones, q_start=unit_qs, max_q=1,
-                n_tokens=B, max_context=plan["ctx_j"][j - 1],  # type: ignore[index]
+                n_tokens=B, max_context=plan.ctx_j[j - 1],
             ))
         idsv = w[k]
         k += 1
@@ -424,21 +476,21 @@ class SpeculativeDecoder:
             )
         # The target side is planned while the draft passes run on the GPU.
         self._plan_verify(plan, target_cache)
-        vblob = self._staging_v.upload(plan["blob_v"])  # type: ignore[arg-type]
-        w = [vblob[o : o + n] for o, n in plan["spans_v"]]  # type: ignore[union-attr]
-        tw = int(plan["tw"])  # type: ignore[arg-type]
+        vblob = self._staging_v.upload(plan.blob_v)
+        w = [vblob[o : o + n] for o, n in plan.spans_v]
+        tw = plan.tw
         bv = PagedBatch(
             input_ids=idsv, positions=w[0], slot_mapping=w[1], q_start=w[2], context_lens=w[3],
-            q_lens=w[4], block_tables=w[5].view(B, tw), max_q=int(plan["max_qv"]),  # type: ignore[arg-type]
-            n_tokens=int(plan["Tv"]), max_context=int(plan["ctxv"]),  # type: ignore[arg-type]
+            q_lens=w[4], block_tables=w[5].view(B, tw), max_q=plan.max_qv,
+            n_tokens=plan.Tv, max_context=plan.ctxv,
         )
         rowsv = w[6]
-        self.last_round_shape = {"B": B, "T0": int(plan["T0"]), "Tv": int(plan["Tv"]),  # type: ignore[arg-type]
+        self.last_round_shape = {"B": B, "T0": plan.T0, "Tv": plan.Tv,
                                  "gamma": G,
                                  # keys each pass's attention reads, summed over requests
-                                 "kv_tokens_verify": int(plan["kv_verify"]),  # type: ignore[arg-type]
-                                 "kv_tokens_draft": int(plan["kv_draft"])}  # type: ignore[arg-type]
-        self.last_h2d_bytes = sum(int(plan[k].nbytes) for k in ("blob", "blob_d", "blob_v"))  # type: ignore[union-attr]
+                                 "kv_tokens_verify": plan.kv_verify,
+                                 "kv_tokens_draft": plan.kv_draft}
+        self.last_h2d_bytes = plan.blob.nbytes + plan.blob_d.nbytes + plan.blob_v.nbytes
         self.last_d2h_bytes = B * (G + 2) * 4
         vev = None
         if self.verify_events is not None:
@@ -462,17 +514,17 @@ class SpeculativeDecoder:
         self,
         requests: list[Request],
         target_cache: PagedKVCache,
-        plan: dict[str, object],
+        plan: _RoundPlan,
         tokens: np.ndarray,
         nacc: np.ndarray,
     ) -> list[list[int]]:
         G = self.gamma
-        ids: list[int] = plan["ids"]  # type: ignore[assignment]
-        n_tok: np.ndarray = plan["n_tok"]  # type: ignore[assignment]
+        ids = plan.ids
+        n_tok = plan.n_tok
         keep = n_tok + nacc
-        target_cache.truncate_many(ids, keep, plan["trows"])  # type: ignore[arg-type]
-        d_len = plan["d_cached"] + plan["n0"] + (G - 1)  # type: ignore[operator]
-        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep), plan["drows"])  # type: ignore[arg-type]
+        target_cache.truncate_many(ids, keep, plan.trows)
+        d_len = plan.d_cached + plan.n0 + (G - 1)
+        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep), plan.drows)
         rows = tokens.tolist()
         nacc_l = nacc.tolist()
         keep_l = keep.tolist()

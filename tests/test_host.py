@@ -218,7 +218,7 @@ class TestCacheTables:
                 tc.append(r.request_id, n - 1)
             plan = dec._plan(reqs, tc, gens, configs)
             dec._plan_draft(plan)
-            blobs.append((plan["blob"], plan["blob_d"]))
+            blobs.append((plan.blob, plan.blob_d))
         assert np.array_equal(blobs[0][0], blobs[1][0])
         assert np.array_equal(blobs[0][1], blobs[1][1])
 
@@ -277,8 +277,8 @@ class TestCacheTables:
         dec._plan_verify(plan, tc)
 
         def parts(blob_key: str, span_key: str) -> list[list[int]]:
-            blob = plan[blob_key]
-            return [blob[o : o + n].tolist() for o, n in plan[span_key]]
+            blob = getattr(plan, blob_key)
+            return [blob[o : o + n].tolist() for o, n in getattr(plan, span_key)]
 
         a0 = parts("blob", "spans")
         ad = parts("blob_d", "spans_d")
@@ -337,8 +337,8 @@ class TestCacheTables:
         # sampling parameters: one entry per request, its generator's seed and its step
         from microserve_b200 import _lib
 
-        o, n = plan["spans_d"][0]
-        params = np.frombuffer(plan["blob_d"][o : o + n].tobytes(), dtype=_lib.SAMPLING_PARAMS_DTYPE)
+        o, n = plan.spans_d[0]
+        params = np.frombuffer(plan.blob_d[o : o + n].tobytes(), dtype=_lib.SAMPLING_PARAMS_DTYPE)
         assert params["seed"].tolist() == [gens[r.request_id].initial_seed() for r in reqs]
         assert params["step"].tolist() == [r.rng_step for r in reqs]
         assert np.allclose(params["temperature"], 0.9) and np.allclose(params["top_p"], 0.8)
