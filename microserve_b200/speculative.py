@@ -25,7 +25,6 @@ lane j, accept roll i on lane 64+i, the residual/bonus draw on lane 128.
 
 from __future__ import annotations
 
-import ctypes
 import itertools
 from dataclasses import dataclass, field
 
@@ -242,7 +241,7 @@ class SpeculativeDecoder:
         tokens (1..gamma+1) per request.  The caller appends them."""
         if not requests:
             return []
-        G, B, V = self.gamma, len(requests), self.target.cfg.vocab_size
+        G, B = self.gamma, len(requests)
         configs = list({id(r.sampling): r.sampling for r in requests}.values())
         for cfg in configs:
             validate(cfg)
