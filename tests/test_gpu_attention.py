@@ -51,7 +51,7 @@ def _case(dtype: str, hq: int, hkv: int, dh: int, bs: int, ctx: list[int], qlen:
               ctypes.byref(cb), hq, out.data_ptr(), _lib.stream_ptr())
     torch.cuda.synchronize()
     # reference
-    tables, lens = cache.build_block_tables(list(range(len(ctx))))
+    tables, _ = cache.build_block_tables(list(range(len(ctx))))
     K, V = cache.gather(0, tables, max(ctx))
     ref = torch.empty(T, hq, dh, device=DEV)
     qf = q.float().view(T, hq, dh)

@@ -452,7 +452,7 @@ class TestScheduler:
         assert [r.request_id for r in out.scheduled] == [1, 2]
 
     def test_speculative_reservation(self) -> None:
-        s, c = self._sched(max_batch_size=4, num_blocks=4)
+        s, _ = self._sched(max_batch_size=4, num_blocks=4)
         s.tokens_per_step = 6
         for i in range(3):
             s.add(Request(i, [1], SamplingConfig()))
