@@ -8,7 +8,7 @@
  * No entry point allocates device memory unless its comment says so; callers
  * own every buffer (weights, K/V pools, block tables, logits, outputs).
  *
- * The Python layer (microserve_b200/*.py) binds these with ctypes and keeps
+ * The Python layer (the microserve_b200 package) binds these with ctypes and keeps
  * the reference's Python API: each declaration cites the reference function
  * (path inside the MicroServe project, file:line) whose arithmetic it takes
  * over.

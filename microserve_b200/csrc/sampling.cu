@@ -1235,7 +1235,6 @@ __device__ __forceinline__ T* cl_map(T* p, int rank) {
 // k-1, so alternating two sets needs one barrier per exchange.
 template <int C>
 struct ClX {
-  static constexpr int kC = C;
   int rank, par;
   __device__ __forceinline__ unsigned long long* slot(ClSmem& s) const { return s.xch + 8 * par; }
 };
