@@ -425,6 +425,41 @@ class PagedKVCache:
         self._free_rows.append(row)
         self.generation += 1
 
+    def fork(self, parent_id: int, child_id: int) -> None:
+        """Let ``child_id`` share every block of ``parent_id`` (copy-on-write
+        prefix sharing, reference cache.py:180-187): the blocks gain a
+        reference, nothing is copied."""
+        if child_id in self._rows:
+            raise ValueError(f"sequence {child_id} already exists")
+        parent = self._rows[parent_id]
+        n = int(self._nblk[parent])
+        blocks = self._table[parent, :n].copy()
+        for block in blocks.tolist():
+            self.allocator.incref(block)
+        child = self._row_of(child_id)
+        self._table[child, :n] = blocks
+        self._nblk[child] = n
+        self._ntok[child] = self._ntok[parent]
+
+    def unshare_last_block(self, seq_id: int) -> None:
+        """Give ``seq_id`` its own copy of its last block when another
+        sequence still references it (reference cache.py:189-204), so that
+        appending to it leaves the other sequence's keys and values alone.
+        The block's K/V are copied for every layer in one device copy; a
+        cache without a device only updates its tables."""
+        row = self._rows[seq_id]
+        n = int(self._nblk[row])
+        if n == 0:
+            return
+        old = int(self._table[row, n - 1])
+        if self.allocator.refcount(old) == 1:
+            return
+        new = self.allocator.allocate()
+        if self.pool is not None:
+            self.pool[:, :, new].copy_(self.pool[:, :, old])
+        self._table[row, n - 1] = new
+        self.allocator.free(old)
+
     def truncate(self, seq_id: int, num_tokens: int) -> None:
         """Shrink a sequence to ``num_tokens``, releasing blocks past the end."""
         if seq_id not in self._rows:

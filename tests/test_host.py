@@ -398,6 +398,47 @@ class TestCacheTables:
                 c.num_free_blocks) == snap
         c.allocator.check_invariants()
 
+    def test_fork_shares_blocks(self) -> None:
+        # reference tests/test_cache.py:159-183
+        c = host_cache(4, 32)
+        c.append(0, 16)
+        free_before = c.num_free_blocks
+        c.fork(0, 1)
+        assert c.num_free_blocks == free_before
+        assert c.tables[0].blocks == c.tables[1].blocks
+        assert c.num_tokens(1) == 16
+        for block in c.tables[0].blocks:
+            assert c.allocator.refcount(block) == 2
+        blocks = list(c.tables[1].blocks)
+        c.free(0)
+        for block in blocks:
+            assert c.allocator.refcount(block) == 1
+        c.free(1)
+        c.allocator.check_invariants()
+        c.append(0, 4)
+        c.append(1, 4)
+        with pytest.raises(ValueError, match="already exists"):
+            c.fork(0, 1)
+
+    def test_unshare_last_block_and_rollback_of_shared_blocks(self) -> None:
+        c = host_cache(4, 32)
+        c.append(0, 10)
+        c.fork(0, 1)
+        old_tail = c.tables[1].blocks[-1]
+        c.unshare_last_block(1)
+        assert c.tables[1].blocks[:-1] == c.tables[0].blocks[:-1]
+        assert c.tables[1].blocks[-1] != old_tail
+        assert c.allocator.refcount(old_tail) == 1
+        c.unshare_last_block(1)  # already private: nothing changes
+        assert c.allocator.refcount(c.tables[1].blocks[-1]) == 1
+        # truncating both below the shared prefix releases each shared block once
+        c.truncate_many([0, 1], [1, 1])
+        assert c.allocator.refcount(c.tables[0].blocks[0]) == 2
+        c.free(0)
+        c.free(1)
+        c.allocator.check_invariants()
+        assert c.num_free_blocks == 32
+
     def test_vectorised_paths_match_single_calls(self) -> None:
         rng = np.random.default_rng(0)
         a, b = host_cache(4, 64), host_cache(4, 64)
