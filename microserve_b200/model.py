@@ -21,6 +21,7 @@ from __future__ import annotations
 import ctypes
 import math
 from dataclasses import dataclass
+from pathlib import Path
 from typing import Any
 
 import numpy as np
@@ -106,6 +107,20 @@ def split_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return v[:, 0].reshape(-1, d), v[:, 1].reshape(-1, d)
 
 
+def load_checkpoint(path: str | Path, dtype: str | None = None
+                    ) -> tuple[ModelConfig, dict[str, torch.Tensor]]:
+    """The config and state dict of a checkpoint in the reference's format
+    (reference model.py:356-373).  Read with ``weights_only=True``: plain
+    values and tensors load, any other pickled object is refused.  Keys this
+    build adds to ``ModelConfig`` (``n_kv_heads``, ``dtype``) keep their
+    defaults unless stored; ``dtype`` overrides the stored one."""
+    payload = torch.load(path, map_location="cpu", weights_only=True)
+    kw = dict(payload["config"])
+    if dtype is not None:
+        kw["dtype"] = dtype
+    return ModelConfig(**kw), payload["state_dict"]
+
+
 class Transformer:
     """Decoder on one CUDA device; ``forward_paged`` is the hot path."""
 
@@ -181,6 +196,23 @@ class Transformer:
         m.final_norm = get("norm.weight", torch.float32)
         m._finish()
         return m
+
+    # -- checkpoints (reference model.py:356-373) ------------------------------
+    def save(self, path: str | Path, extra: dict[str, Any] | None = None) -> None:
+        """Write the reference's checkpoint format: ``{"config": ...,
+        "state_dict": ..., **extra}`` with float32 weights."""
+        payload = {"config": dict(self.cfg.__dict__), "state_dict": self.state_dict(),
+                   **(extra or {})}
+        torch.save(payload, path)
+
+    @classmethod
+    def from_checkpoint(
+        cls, path: str | Path, device: str | torch.device = "cuda", dtype: str | None = None
+    ) -> Transformer:
+        """Load a checkpoint written by the reference's ``Transformer.save`` (or
+        :meth:`save`).  ``dtype`` overrides the stored compute dtype."""
+        cfg, state = load_checkpoint(path, dtype)
+        return cls.from_state_dict(cfg, state, device)
 
     def state_dict(self) -> dict[str, torch.Tensor]:
         """Reference-format float32 state dict on the host (for the checker)."""

@@ -272,6 +272,23 @@ def test_copy_on_write_keeps_the_shared_tail_data() -> None:
     cache.allocator.check_invariants()
 
 
+def test_checkpoint_round_trip(tmp_path) -> None:
+    """save / from_checkpoint (reference model.py:356-373) give the same logits."""
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    cfg = ModelConfig(vocab_size=65, n_layers=2, d_model=64, n_heads=4, d_ff=176, max_seq_len=256)
+    m = Transformer(cfg, DEV, seed=5)
+    m.save(tmp_path / "m.pt", extra={"step": 3})
+    m2 = Transformer.from_checkpoint(tmp_path / "m.pt", DEV)
+    prompts = [[1, 2, 3, 4, 5], [7, 8, 9]]
+    outs = []
+    for model in (m, m2):
+        cache = new_cache(model)
+        outs.append(run(model, cache, [0, 1], prompts, [0, 0]))
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
 def test_device_error_word_flags_bad_slots() -> None:
     """A slot outside the pool is skipped and reported, not written."""
     from microserve_b200 import _lib

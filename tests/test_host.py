@@ -548,3 +548,27 @@ class TestConfig:
         assert load_config(p) == cfg
         with pytest.raises(ValueError, match="unknown config key"):
             EngineConfig.from_dict({"bogus": 1})
+
+
+def test_checkpoint_in_the_reference_format_loads(tmp_path) -> None:
+    """A payload laid out as the reference's Transformer.save writes it
+    (reference model.py:356-362): config keys of the reference only, a
+    float32 state dict and extra entries."""
+    import torch
+
+    from microserve_b200.model import load_checkpoint
+
+    ref_cfg = dict(vocab_size=65, n_layers=2, d_model=64, n_heads=4, d_ff=176, max_seq_len=256,
+                   rope_theta=10000.0, norm_eps=1e-5, tie_weights=True, dropout=0.0)
+    state = {"embed.weight": torch.randn(65, 64), "norm.weight": torch.ones(64)}
+    path = tmp_path / "draft.pt"
+    torch.save({"config": ref_cfg, "state_dict": state, "step": 1200, "val_loss": 1.52}, path)
+    cfg, got = load_checkpoint(path)
+    assert (cfg.d_ff, cfg.n_kv_heads, cfg.dtype, cfg.d_head) == (176, 4, "float32", 16)
+    assert torch.equal(got["embed.weight"], state["embed.weight"])
+    cfg16, _ = load_checkpoint(path, dtype="bfloat16")
+    assert cfg16.dtype == "bfloat16"
+    # anything but plain values and tensors is refused
+    torch.save({"config": ref_cfg, "state_dict": state, "obj": object()}, tmp_path / "bad.pt")
+    with pytest.raises(Exception):
+        load_checkpoint(tmp_path / "bad.pt")
