@@ -20,7 +20,7 @@ the end-of-run counters are reduced over NCCL (SUM of tokens, MAX of time).
 Reported: ``value`` = emitted tokens of all ranks / max over ranks of the
 summed device time of the rounds' kernels (metadata already on the device);
 ``e2e`` = the same tokens / the time of the public ``SpeculativeDecoder.step``
-calls including host bookkeeping, the pinned host->device metadata copy and
+calls including host bookkeeping, the pinned host->device metadata copies and
 the device->host copy of the accepted tokens.  The GEMM roofline, the verify
 step time and the attention rate come from further rounds of the same
 workload after the timed ones, where CUDA events bracket every launch of the
