@@ -293,6 +293,12 @@ class PagedKVCache:
             return int(_lib.load().ms_host_blocks_needed(
                 _addr(rows), _addr(counts), len(rows), _addr(self._ntok), _addr(self._nblk),
                 self.block_size, None))
+        return int(self.blocks_needed_each(seq_ids, counts).sum())
+
+    def blocks_needed_each(self, seq_ids: Sequence[int],
+                           counts: Sequence[int] | np.ndarray) -> np.ndarray:
+        """``blocks_needed`` of every sequence (int64 array; unknown ids hold 0 tokens)."""
+        counts = np.ascontiguousarray(counts, dtype=np.int64)
         get = self._rows.get
         rows = np.fromiter((get(s, -1) for s in seq_ids), dtype=np.int64, count=len(seq_ids))
         known = rows >= 0
@@ -301,7 +307,7 @@ class PagedKVCache:
         ntok[known] = self._ntok[rows[known]]
         nblk[known] = self._nblk[rows[known]]
         need = (ntok + counts + self.block_size - 1) // self.block_size - nblk
-        return int(np.maximum(need, 0).sum())
+        return np.maximum(need, 0)
 
     def can_append(self, seq_id: int, num_new_tokens: int) -> bool:
         return self.blocks_needed(seq_id, num_new_tokens) <= self.allocator.num_free

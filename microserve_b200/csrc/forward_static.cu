@@ -19,6 +19,8 @@
 // (the forward writes every scratch byte it reads, so nothing needs
 // clearing), and calls whose kernels overlap on the GPU -- two streams, or
 // two threads -- race on it.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace {
@@ -28,8 +30,12 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_forward_scratch[kStaticScratchBytes];
 
+// One resolved address per device.  Two host threads making their first call
+// on the same device may both resolve it; they store the same value, and the
+// atomic makes that well defined.
+std::atomic<void*> g_scratch_cache[kMaxDevices];
+
 int scratch_address(void** out) {
-  static void* cached[kMaxDevices] = {};
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess)
@@ -37,15 +43,15 @@ int scratch_address(void** out) {
                     cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return ms::fail(MS_ERR_UNSUPPORTED, "ms_forward_static_scratch: device %d", dev);
-  if (cached[dev] == nullptr) {
-    void* p = nullptr;
+  void* p = g_scratch_cache[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
     e = cudaGetSymbolAddress(&p, g_forward_scratch);
     if (e != cudaSuccess || p == nullptr)
       return ms::fail(MS_ERR_CUDA, "ms_forward_static_scratch: cudaGetSymbolAddress: %s",
                       cudaGetErrorString(e));
-    cached[dev] = p;
+    g_scratch_cache[dev].store(p, std::memory_order_release);
   }
-  *out = cached[dev];
+  *out = p;
   return MS_OK;
 }
 

@@ -107,15 +107,33 @@ def split_gate_up(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     return v[:, 0].reshape(-1, d), v[:, 1].reshape(-1, d)
 
 
+# ModelConfig fields the reference's config class does not have; a checkpoint
+# stores them under EXTRA_CONFIG_KEY so the reference can still load it.
+ADDED_CONFIG_FIELDS = ("n_kv_heads", "dtype")
+EXTRA_CONFIG_KEY = "microserve_b200_config"
+
+
+def checkpoint_payload(cfg: ModelConfig, state: dict[str, torch.Tensor],
+                       extra: dict[str, Any] | None = None) -> dict[str, Any]:
+    """``{"config": ..., "state_dict": ..., EXTRA_CONFIG_KEY: ..., **extra}``:
+    the reference's checkpoint layout (model.py:357-363), with ``config``
+    limited to the reference's ``ModelConfig`` fields."""
+    c = dict(cfg.__dict__)
+    added = {k: c.pop(k) for k in ADDED_CONFIG_FIELDS}
+    return {"config": c, "state_dict": state, EXTRA_CONFIG_KEY: added, **(extra or {})}
+
+
 def load_checkpoint(path: str | Path, dtype: str | None = None
                     ) -> tuple[ModelConfig, dict[str, torch.Tensor]]:
     """The config and state dict of a checkpoint in the reference's format
     (reference model.py:356-373).  Read with ``weights_only=True``: plain
-    values and tensors load, any other pickled object is refused.  Keys this
-    build adds to ``ModelConfig`` (``n_kv_heads``, ``dtype``) keep their
-    defaults unless stored; ``dtype`` overrides the stored one."""
+    values and tensors load, any other pickled object is refused.  The
+    ``ModelConfig`` fields this package adds (``n_kv_heads``, ``dtype``) are
+    read from the payload's ``EXTRA_CONFIG_KEY`` entry when present, else
+    keep their defaults; ``dtype`` overrides the stored one."""
     payload = torch.load(path, map_location="cpu", weights_only=True)
     kw = dict(payload["config"])
+    kw.update(payload.get(EXTRA_CONFIG_KEY, {}))
     if dtype is not None:
         kw["dtype"] = dtype
     return ModelConfig(**kw), payload["state_dict"]
@@ -200,10 +218,13 @@ class Transformer:
     # -- checkpoints (reference model.py:356-373) ------------------------------
     def save(self, path: str | Path, extra: dict[str, Any] | None = None) -> None:
         """Write the reference's checkpoint format: ``{"config": ...,
-        "state_dict": ..., **extra}`` with float32 weights."""
-        payload = {"config": dict(self.cfg.__dict__), "state_dict": self.state_dict(),
-                   **(extra or {})}
-        torch.save(payload, path)
+        "state_dict": ..., **extra}`` with float32 weights.
+
+        ``config`` holds only the reference's ``ModelConfig`` fields, so the
+        reference's ``ModelConfig(**payload["config"])`` (model.py:369-370)
+        loads the file; the fields this package adds go under
+        ``EXTRA_CONFIG_KEY``, which the reference ignores."""
+        torch.save(checkpoint_payload(self.cfg, self.state_dict(), extra), path)
 
     @classmethod
     def from_checkpoint(
@@ -219,8 +240,9 @@ class Transformer:
         cfg = self.cfg
         hq, hkv, dh = cfg.n_heads, cfg.kv_heads, cfg.d_head
         f = lambda t: t.detach().float().cpu()  # noqa: E731
-        out = {"embed.weight": f(self.embed), "norm.weight": f(self.final_norm),
-               "lm_head.weight": f(self.embed)}
+        embed = f(self.embed)
+        # tied: one storage under both names, as the reference's module shares it
+        out = {"embed.weight": embed, "norm.weight": f(self.final_norm), "lm_head.weight": embed}
         for i in range(cfg.n_layers):
             p = f"blocks.{i}."
             qkv = f(self.w_qkv[i])

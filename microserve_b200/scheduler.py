@@ -1,18 +1,37 @@
-"""Request bookkeeping and admission control (host side).
+"""Which requests take part in the next engine iteration (host side).
 
-Follows reference src/microserve/scheduler.py: FCFS / SJF / LIFO priority,
-continuous or static batching, preemption by recomputation, and the
-speculative ``tokens_per_step`` reservation (gamma + 1 slots per running
-request).  It owns no tensors.  ``Request.rng_step`` is new: the request's
-Philox draw-step counter, advanced once per engine iteration it takes part
-in.
+The policy is MicroServe's (reference src/microserve/scheduler.py): FCFS,
+LIFO or shortest-job-first priority with the request id as tie-break,
+continuous or static batching, admission under a token budget, a batch-size
+cap and a block watermark, preemption by recomputation of the
+lowest-priority running request while the running set's next step does not
+fit, and the speculative reservation of ``tokens_per_step`` (gamma + 1)
+slots per request.  It decides exactly what the reference decides, so token
+streams and step counts match it.
+
+How it is organised here:
+
+* ``waiting`` stays ordered by priority (each request is inserted at its
+  place), so admission is one ordered scan instead of a sort per step;
+* the running set's block demand is one batched computation
+  (``PagedKVCache.blocks_needed_each``); a request's demand depends only on
+  its own table, so preemption takes victims in descending priority and
+  subtracts each victim's demand instead of re-summing the set per victim;
+* a request's stop condition is an explicit ``finish_reason`` ("length" or
+  "stop"), and ``Request.extend_until_stop`` appends a step's tokens up to
+  it in one slice.
+
+``Request.rng_step`` (not in the reference) counts the engine iterations a
+request took part in; it is the counter of the request's Philox stream.
 """
 
 from __future__ import annotations
 
+import bisect
 import enum
-import itertools
 from dataclasses import dataclass, field
+
+import numpy as np
 
 from .cache import PagedKVCache
 from .config import SamplingConfig, SchedulerConfig
@@ -26,9 +45,14 @@ class RequestStatus(enum.Enum):
     ABORTED = "aborted"
 
 
-@dataclass
+@dataclass(eq=False)
 class Request:
-    """One generation request (reference scheduler.py:41-115)."""
+    """One generation request (the reference's ``Request`` fields, scheduler.py:41-115).
+
+    ``num_computed`` counts the leading tokens whose K/V is in the cache;
+    the timing fields are engine-clock seconds.  Requests compare by
+    identity.
+    """
 
     request_id: int
     prompt_ids: list[int]
@@ -48,20 +72,21 @@ class Request:
     num_draft_accepted: int = 0
     rng_step: int = 0
 
+    # -- tokens ------------------------------------------------------------
     @property
     def all_ids(self) -> list[int]:
-        return self.prompt_ids + self.output_ids
+        return [*self.prompt_ids, *self.output_ids]
 
     @property
     def num_tokens(self) -> int:
         return len(self.prompt_ids) + len(self.output_ids)
 
     def tail(self, start: int) -> list[int]:
-        """``all_ids[start:]`` without concatenating the whole history."""
-        n_prompt = len(self.prompt_ids)
-        if start >= n_prompt:
-            return self.output_ids[start - n_prompt :]
-        return self.prompt_ids[start:] + self.output_ids
+        """``all_ids[start:]``, built from the part of the history it needs."""
+        past_prompt = start - len(self.prompt_ids)
+        if past_prompt >= 0:
+            return self.output_ids[past_prompt:]
+        return [*self.prompt_ids[start:], *self.output_ids]
 
     @property
     def num_uncomputed(self) -> int:
@@ -69,50 +94,75 @@ class Request:
 
     @property
     def is_prefill(self) -> bool:
+        """More than one token to process in the next pass."""
         return self.num_uncomputed > 1
+
+    # -- stopping ----------------------------------------------------------
+    def finish_reason(self) -> str | None:
+        """"length" once the budget is spent, "stop" after the stop token, else None."""
+        out = self.output_ids
+        if len(out) >= self.sampling.max_new_tokens:
+            return "length"
+        stop = self.sampling.stop_token
+        if stop is not None and out and out[-1] == stop:
+            return "stop"
+        return None
+
+    def should_stop(self) -> bool:
+        return self.finish_reason() is not None
+
+    def extend_until_stop(self, tokens: list[int]) -> int:
+        """Append ``tokens`` up to the stop condition; returns how many were
+        taken.  Equal to appending one at a time while ``should_stop()`` is
+        false: the budget caps the count and the first stop token is the
+        last one taken."""
+        if self.should_stop():
+            return 0
+        take = tokens[: self.sampling.max_new_tokens - len(self.output_ids)]
+        stop = self.sampling.stop_token
+        if stop is not None and stop in take:
+            take = take[: take.index(stop) + 1]
+        self.output_ids.extend(take)
+        return len(take)
 
     @property
     def finished(self) -> bool:
         return self.status in (RequestStatus.FINISHED, RequestStatus.ABORTED)
 
-    def should_stop(self) -> bool:
-        if len(self.output_ids) >= self.sampling.max_new_tokens:
-            return True
-        stop = self.sampling.stop_token
-        return stop is not None and bool(self.output_ids) and self.output_ids[-1] == stop
-
     def reset_for_recompute(self) -> None:
+        """Preempted: nothing is cached any more; generated tokens are kept
+        and will be prefilled again with the prompt."""
         self.num_computed = 0
         self.status = RequestStatus.PREEMPTED
         self.num_preemptions += 1
 
+    # -- latency metrics -----------------------------------------------------
     def ttft(self) -> float | None:
-        if self.first_token_time is None:
-            return None
-        return self.first_token_time - self.arrival_time
+        t = self.first_token_time
+        return None if t is None else t - self.arrival_time
 
     def tpot(self) -> float | None:
-        if self.finish_time is None or self.first_token_time is None:
+        """Mean time per output token after the first (None below two tokens)."""
+        t0, t1, n = self.first_token_time, self.finish_time, len(self.output_ids)
+        if t0 is None or t1 is None or n < 2:
             return None
-        extra = len(self.output_ids) - 1
-        if extra <= 0:
-            return None
-        return (self.finish_time - self.first_token_time) / extra
+        return (t1 - t0) / (n - 1)
 
     def latency(self) -> float | None:
-        if self.finish_time is None:
-            return None
-        return self.finish_time - self.arrival_time
+        t = self.finish_time
+        return None if t is None else t - self.arrival_time
 
 
 @dataclass
 class SchedulerOutput:
+    """The plan of one engine iteration: who runs, who was evicted for it."""
+
     scheduled: list[Request] = field(default_factory=list)
     preempted: list[Request] = field(default_factory=list)
 
     @property
     def is_empty(self) -> bool:
-        return not self.scheduled
+        return len(self.scheduled) == 0
 
     @property
     def num_tokens(self) -> int:
@@ -120,97 +170,126 @@ class SchedulerOutput:
 
 
 class Scheduler:
-    """Priority queueing, admission control and preemption (reference scheduler.py:134-258)."""
+    """Priority queue, admission control and preemption over one paged cache."""
 
     def __init__(self, cfg: SchedulerConfig, cache: PagedKVCache) -> None:
         self.cfg = cfg
         self.cache = cache
-        self.waiting: list[Request] = []
+        self.waiting: list[Request] = []  # ordered by ``priority``
         self.running: list[Request] = []
         self.finished: list[Request] = []
-        self._ids = itertools.count()
         self.total_preemptions = 0
         self.tokens_per_step = 1
+        self._issued_ids = 0
+
+    # -- queue ----------------------------------------------------------------
+    def priority(self, request: Request) -> tuple[float, int]:
+        """Sort key, smallest first; the id breaks ties."""
+        policy = self.cfg.policy
+        if policy == "fcfs":
+            key = request.arrival_time
+        elif policy == "lifo":
+            key = -request.arrival_time
+        else:  # shortest job first: prompt plus output budget
+            key = float(len(request.prompt_ids) + request.sampling.max_new_tokens)
+        return key, request.request_id
+
+    def _enqueue(self, request: Request) -> None:
+        bisect.insort(self.waiting, request, key=self.priority)
 
     def add(self, request: Request) -> Request:
         request.status = RequestStatus.WAITING
-        self.waiting.append(request)
+        self._enqueue(request)
         return request
 
     def next_request_id(self) -> int:
-        return next(self._ids)
+        rid = self._issued_ids
+        self._issued_ids += 1
+        return rid
 
     @property
     def num_unfinished(self) -> int:
         return len(self.waiting) + len(self.running)
 
-    def priority(self, request: Request) -> tuple[float, int]:
-        if self.cfg.policy == "fcfs":
-            key = request.arrival_time
-        elif self.cfg.policy == "lifo":
-            key = -request.arrival_time
-        else:
-            key = float(len(request.prompt_ids) + request.sampling.max_new_tokens)
-        return (key, request.request_id)
+    # -- one iteration's plan -------------------------------------------------------
+    def _step_tokens(self, request: Request) -> int:
+        """Slots a request needs for its next step (gamma + 1 when speculating)."""
+        return max(self.tokens_per_step, request.num_uncomputed)
 
     def schedule(self, now: float) -> SchedulerOutput:
-        out = SchedulerOutput()
-        if self.cfg.batching == "static" and self.running:
-            self._ensure_room(self.running, out)
-            out.scheduled = list(self.running)
-            return out
-        self._ensure_room(self.running, out)
-        out.scheduled = list(self.running)
-        self._admit(out, now)
-        return out
+        plan = SchedulerOutput()
+        # static batching admits only when the previous batch has drained
+        admit = not (self.cfg.batching == "static" and self.running)
+        demand = self._make_room(plan)
+        plan.scheduled = list(self.running)
+        if admit:
+            self._admit(plan, now, demand)
+        return plan
 
-    def _need(self, r: Request) -> int:
-        return self.cache.blocks_needed(r.request_id, max(self.tokens_per_step, r.num_uncomputed))
-
-    def _ensure_room(self, running: list[Request], out: SchedulerOutput) -> None:
-        """Preempt lowest-priority requests until every running one can step."""
-        while running:
-            needed = sum(self._need(r) for r in running)
-            if needed <= self.cache.num_free_blocks or len(running) == 1:
-                return
-            victim = max(running, key=self.priority)
-            running.remove(victim)
+    def _make_room(self, plan: SchedulerOutput) -> int:
+        """Preempt until the running set's next step fits the free blocks (a
+        lone request is never preempted); returns the survivors' block demand."""
+        running = self.running
+        if not running:
+            return 0
+        need = self.cache.blocks_needed_each([r.request_id for r in running],
+                                             [self._step_tokens(r) for r in running])
+        total = int(need.sum())
+        free = self.cache.num_free_blocks
+        if total <= free or len(running) == 1:
+            return total
+        evicted = np.zeros(len(running), dtype=bool)
+        left = len(running)
+        for i in sorted(range(len(running)), key=lambda j: self.priority(running[j]), reverse=True):
+            if total <= free or left == 1:
+                break
+            victim = running[i]
             self.cache.free(victim.request_id)
+            free = self.cache.num_free_blocks
+            total -= int(need[i])
+            evicted[i] = True
+            left -= 1
             victim.reset_for_recompute()
-            self.waiting.append(victim)
-            out.preempted.append(victim)
+            self._enqueue(victim)
+            plan.preempted.append(victim)
             self.total_preemptions += 1
+        self.running = [r for r, gone in zip(running, evicted, strict=True) if not gone]
+        return total
 
-    def _admit(self, out: SchedulerOutput, now: float) -> None:
-        """Admit waiting requests while the token and block budgets allow,
-        debiting blocks locally because nothing is allocated until the batch
-        is built."""
-        token_budget = self.cfg.max_batched_tokens - out.num_tokens
+    def _admit(self, plan: SchedulerOutput, now: float, demand: int) -> None:
+        """Admit waiting requests in priority order under the token budget,
+        the batch cap and the free blocks (minus the watermark reserve once
+        something is scheduled).  Blocks are debited locally: nothing is
+        allocated until the batch is built."""
+        tokens_left = self.cfg.max_batched_tokens - plan.num_tokens
+        blocks_left = self.cache.num_free_blocks - demand
         reserve = int(self.cache.allocator.num_blocks * self.cfg.watermark)
-        free_blocks = self.cache.num_free_blocks - sum(self._need(r) for r in out.scheduled)
-        for request in sorted(self.waiting, key=self.priority):
+        admitted: list[Request] = []
+        for request in self.waiting:
             if len(self.running) >= self.cfg.max_batch_size:
                 break
-            need = request.num_uncomputed
-            if need > token_budget and out.scheduled:
+            n = request.num_uncomputed
+            busy = bool(plan.scheduled)
+            if busy and n > tokens_left:
                 continue
-            blocks = self.cache.blocks_needed(request.request_id, max(need, self.tokens_per_step))
-            headroom = free_blocks - (reserve if out.scheduled else 0)
-            if blocks > headroom:
+            blocks = self.cache.blocks_needed(request.request_id, max(n, self.tokens_per_step))
+            if blocks > blocks_left - (reserve if busy else 0):
                 continue
-            self.waiting.remove(request)
+            admitted.append(request)
             request.status = RequestStatus.RUNNING
             if request.schedule_time is None:
                 request.schedule_time = now
             self.running.append(request)
-            out.scheduled.append(request)
-            token_budget -= need
-            free_blocks -= blocks
+            plan.scheduled.append(request)
+            tokens_left -= n
+            blocks_left -= blocks
+        if admitted:
+            taken = {id(r) for r in admitted}
+            self.waiting = [r for r in self.waiting if id(r) not in taken]
 
     def finish(self, request: Request, now: float) -> None:
         request.status = RequestStatus.FINISHED
         request.finish_time = now
-        if request in self.running:
-            self.running.remove(request)
+        self.running = [r for r in self.running if r is not request]
         self.cache.free(request.request_id)
         self.finished.append(request)

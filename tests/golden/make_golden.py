@@ -181,5 +181,175 @@ def main(ref_root: str) -> None:
     print(f"wrote {HERE / 'reference_fixtures.npz'} with {len(out)} arrays")
 
 
+def _ref_model(shape, state: dict[str, np.ndarray]):
+    """The reference's Transformer with the given float32 weights."""
+    from microserve.config import ModelConfig
+    from microserve.model import Transformer
+
+    cfg = ModelConfig(vocab_size=shape.vocab_size, n_layers=shape.n_layers,
+                      d_model=shape.d_model, n_heads=shape.n_heads, d_ff=shape.d_ff,
+                      max_seq_len=shape.max_seq_len, rope_theta=shape.rope_theta)
+    m = Transformer(cfg).eval()
+    m.load_state_dict({k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in state.items()})
+    return m
+
+
+def _run_engine(target, draft, gamma: int, prompts, budgets, cache_blocks: int,
+                max_batch: int, max_tokens: int) -> tuple[list[list[int]], list[int]]:
+    """LLMEngine.run of the reference (engine.py:155-202) at temperature 0."""
+    from microserve.config import (CacheConfig, EngineConfig, SamplingConfig, SchedulerConfig,
+                                   SpeculativeConfig)
+    from microserve.engine import LLMEngine
+
+    cfg = EngineConfig(model=target.cfg, cache=CacheConfig(block_size=16, num_blocks=cache_blocks),
+                       scheduler=SchedulerConfig(max_batch_size=max_batch,
+                                                 max_batched_tokens=max_tokens),
+                       speculative=SpeculativeConfig(enabled=True, gamma=gamma))
+    eng = LLMEngine(target, cfg, draft_model=draft)
+    reqs = [eng.add_request(p, SamplingConfig(temperature=0.0, max_new_tokens=int(b)))
+            for p, b in zip(prompts, budgets, strict=True)]
+    outs = {o.request_id: o.output_ids for o in eng.run()}
+    return ([outs[r.request_id] for r in reqs],
+            [eng.stats.num_draft_accepted, eng.stats.num_draft_proposed, eng.stats.num_steps])
+
+
+def config_fixtures() -> None:
+    """Token streams of the reference engine on the character-level configurations
+    (config 0: 8 requests, gamma 3; config 2: a 64-request subset of the
+    continuous-batching workload at gamma 1/2/3/5), greedy, random-init weights
+    from ``workloads.init_state``, plus the reference ModelConfig's field names."""
+    import dataclasses
+
+    from microserve.config import CacheConfig, ModelConfig
+
+    import workloads as wl
+
+    torch.set_num_threads(1)
+    out: dict[str, np.ndarray] = {}
+    out["ref/model_config_fields"] = np.asarray([f.name for f in dataclasses.fields(ModelConfig)])
+    for amp in (1.0, 20.0):
+        tag = f"a{int(amp)}"
+        target = _ref_model(wl.CHAR_TARGET, wl.init_state(wl.CHAR_TARGET, 0, amp))
+        draft = _ref_model(wl.CHAR_DRAFT, wl.init_state(wl.CHAR_DRAFT, 1, amp))
+        w0 = wl.config0()
+        toks, counts = _run_engine(target, draft, 3, w0.prompts, w0.max_new_tokens, 256, 8, 2048)
+        for j, t in enumerate(toks):
+            out[f"cfg0/{tag}/g3/{j}"] = np.asarray(t)
+        out[f"cfg0/{tag}/g3/counts"] = np.asarray(counts)
+        w2 = wl.config2(64)
+        for gamma in ((1, 2, 3, 5) if amp == 1.0 else (3,)):
+            toks, counts = _run_engine(target, draft, gamma, w2.prompts, w2.max_new_tokens, 4096,
+                                       64, 64 * 600)
+            for j, t in enumerate(toks):
+                out[f"cfg2/{tag}/g{gamma}/{j}"] = np.asarray(t)
+            out[f"cfg2/{tag}/g{gamma}/counts"] = np.asarray(counts)
+            print(f"config 2 amplify {amp} gamma {gamma}: counts {counts}")
+    # scheduler decisions under memory pressure (scheduler.py:173-258)
+    from microserve.cache import PagedKVCache
+    from microserve.config import SamplingConfig, SchedulerConfig
+    from microserve.scheduler import Request, Scheduler
+
+    for ci, case in enumerate(wl.SCHEDULER_CASES):
+        cache = PagedKVCache(ModelConfig(vocab_size=50, n_layers=1, d_model=8, n_heads=2),
+                             CacheConfig(block_size=4, num_blocks=case[3]))
+        trace = wl.scheduler_trace(Request, Scheduler, SamplingConfig, SchedulerConfig, cache, case)
+        out[f"sched/{ci}"] = np.concatenate([np.asarray(r, dtype=np.int64) for r in trace])
+        out[f"sched/{ci}/steps"] = np.asarray(len(trace))
+        print(f"scheduler case {case}: {len(trace)} steps, "
+              f"{trace[-1][-1]} preemptions")
+    np.savez_compressed(HERE / "config_fixtures.npz", **out)
+    print(f"wrote {HERE / 'config_fixtures.npz'} with {len(out)} arrays")
+
+
+def kat_fixtures(ref_root: Path) -> None:
+    """The trained-weight known answer: the reference's own checkpoints
+    (artifacts/target.pt, draft.pt, loaded with weights_only=True), the eight
+    32-token prompts of scripts/verify_speculative.py:236-241 (seed 20240) as
+    token ids, the dense greedy continuations (48 tokens) and, per gamma in
+    1/2/4/7, the speculative outputs and acceptance counts per prompt.  The
+    published acceptance rates (artifacts/spec_stats.json:6-35) are the last
+    prompt's, because the script resets the decoder before each prompt; they
+    are checked here and stored."""
+    import json
+
+    from microserve.config import CacheConfig, SamplingConfig
+    from microserve.data import load_corpus, sample_prompts
+    from microserve.model import Transformer
+    from microserve.speculative import SpeculativeDecoder
+    from microserve.tokenizer import CharTokenizer
+
+    torch.set_num_threads(1)
+    seed = 20240
+    torch.manual_seed(seed)
+    art = ref_root / "artifacts"
+    out: dict[str, np.ndarray] = {}
+    models = {}
+    for name in ("target", "draft"):
+        payload = torch.load(art / f"{name}.pt", map_location="cpu", weights_only=True)
+        c = payload["config"]
+        out[f"{name}_cfg"] = np.asarray([c["vocab_size"], c["n_layers"], c["d_model"],
+                                         c["n_heads"], c["n_heads"], c["d_ff"], c["max_seq_len"]])
+        for k, v in payload["state_dict"].items():
+            if k != "lm_head.weight":  # tied: the same tensor as embed.weight
+                out[f"{name}/{k}"] = v.float().numpy()
+        models[name] = Transformer.from_checkpoint(art / f"{name}.pt")
+    tok = CharTokenizer.from_file(art / "tokenizer.json")
+    corpus = load_corpus(ref_root / "data" / "tinyshakespeare.txt", tokenizer=tok)
+    gen = torch.Generator().manual_seed(seed)
+    prompts = sample_prompts(corpus, 8, [32] * 8, gen)
+    target, draft = models["target"], models["draft"]
+    dense = [dense_greedy_ref(target, p, 48) for p in prompts]
+    out["prompts"] = np.asarray(prompts)
+    out["dense"] = np.asarray(dense)
+    stats = json.loads((art / "spec_stats.json").read_text())["greedy_equivalence"]
+    published = {r["gamma"]: r["acceptance_rate"] for r in stats}
+    cache_cfg = CacheConfig(block_size=16, num_blocks=256)
+    for gamma in (1, 2, 4, 7):
+        dec = SpeculativeDecoder(target, draft, cache_cfg, gamma=gamma)
+        counts = []
+        for i, p in enumerate(prompts):
+            dec.reset()
+            got = dec.generate(p, SamplingConfig(temperature=0.0, max_new_tokens=48), seq_id=i)
+            assert got == dense[i], (gamma, i)
+            out[f"spec{gamma}/{i}"] = np.asarray(got)
+            counts.append([dec.num_accepted, dec.num_proposed])
+        out[f"spec{gamma}/counts"] = np.asarray(counts)
+        last = counts[-1][0] / counts[-1][1]
+        assert abs(last - published[gamma]) < 1e-12, (gamma, last, published[gamma])
+        out[f"spec{gamma}/published_acceptance"] = np.asarray(published[gamma])
+        print(f"KAT gamma {gamma}: acceptance {last:.7f} (published {published[gamma]:.7f})")
+    np.savez_compressed(HERE / "kat_fixtures.npz", **out)
+    print(f"wrote {HERE / 'kat_fixtures.npz'} with {len(out)} arrays")
+
+
+def dense_greedy_ref(model, prompt: list[int], n: int) -> list[int]:
+    """Greedy continuation through the reference's dense path (its
+    scripts/verify_speculative.py:49-60 procedure)."""
+    past = None
+    cur = torch.tensor(prompt)[None]
+    out = []
+    for _ in range(n):
+        with torch.no_grad():
+            logits, past = model(cur, past_kv=past, return_cache=True)
+        t = int(logits[0, -1].argmax())
+        out.append(t)
+        cur = torch.tensor([[t]])
+    return out
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    import argparse
+
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("reference_root", help="the MicroServe source tree (contains src/, artifacts/)")
+    ap.add_argument("--only", choices=["tiny", "configs", "kat"], default=None)
+    args = ap.parse_args()
+    root = Path(args.reference_root)
+    sys.path.insert(0, str(root / "src"))
+    sys.path.insert(0, str(HERE))
+    if args.only in (None, "tiny"):
+        main(str(root))
+    if args.only in (None, "configs"):
+        config_fixtures()
+    if args.only in (None, "kat"):
+        kat_fixtures(root)

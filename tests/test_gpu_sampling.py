@@ -9,6 +9,8 @@ import torch
 from oracle import philox
 from oracle.sampling import Row, draw, filter_row, near_boundary, sample_row, verify
 
+from .spec_check import RequestRound, explain
+
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
@@ -201,15 +203,22 @@ def test_spec_accept_matches_oracle(setting, draft_mode: str, V: int) -> None:
            L.stream_ptr())
     got_tok = out.cpu().numpy().reshape(B, G + 1)
     got_n = nacc.cpu().numpy()
-    bad = 0
+    odd = {}
     for b in range(B):
         prow = [filter_row(tl[b, i], t, k, p) for i in range(G + 1)]
         ua = philox.uniform(seeds[b], steps[b], 64 + np.arange(G))
         ud = float(philox.uniform(seeds[b], steps[b], 128))
         toks, n = verify(prow, qrows[b], props[:, b].tolist(), ua, ud)
-        if got_n[b] != n or got_tok[b, : n + 1].tolist() != toks:
-            bad += 1
-    assert bad <= max(1, B // 40), f"{bad} of {B} requests differ"
+        got = got_tok[b, : got_n[b] + 1].tolist()
+        if got != toks:
+            # allowed only at a decision boundary: |u - p/q| < 1e-5 or a draw
+            # within float rounding of a CDF step (same logits on both sides)
+            rr = RequestRound(int(seeds[b]), int(steps[b]), qrows[b], prow,
+                              props[:, b].tolist(), toks, n)
+            why = explain(rr, props[:, b].tolist(), got, tol=1e-5)
+            assert why is not None, (b, got, toks)
+            odd[b] = why
+    assert len(odd) <= 1, odd
 
 
 def test_verify_proposals_api_cases() -> None:

@@ -13,6 +13,8 @@ from microserve_b200.config import (CacheConfig, EngineConfig, ModelConfig, Samp
                                     SchedulerConfig, SpeculativeConfig, load_config)
 from microserve_b200.scheduler import Request, Scheduler
 
+from .conftest import ROOT
+
 
 def host_cache(block_size: int = 8, num_blocks: int = 32) -> PagedKVCache:
     cfg = ModelConfig(vocab_size=32, n_layers=2, d_model=32, n_heads=4, max_seq_len=128)
@@ -550,6 +552,36 @@ class TestConfig:
             EngineConfig.from_dict({"bogus": 1})
 
 
+def test_saved_checkpoint_loads_with_the_reference_config_class(tmp_path) -> None:
+    """A checkpoint this package writes keeps ``config`` to the reference's
+    ModelConfig fields (their names recorded from the reference by the fixture
+    script), so ``ModelConfig(**payload["config"])`` of the reference
+    (model.py:369-370) accepts it; the added fields come back on our side."""
+    import dataclasses
+
+    import torch
+
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import checkpoint_payload, load_checkpoint
+
+    with np.load(ROOT / "tests" / "golden" / "config_fixtures.npz") as z:
+        ref_fields = [str(f) for f in z["ref/model_config_fields"]]
+    cfg = ModelConfig(vocab_size=48, n_layers=1, d_model=32, n_heads=4, n_kv_heads=2,
+                      dtype="bfloat16")
+    embed = torch.randn(48, 32)
+    state = {"embed.weight": embed, "lm_head.weight": embed, "norm.weight": torch.ones(32)}
+    path = tmp_path / "ours.pt"
+    torch.save(checkpoint_payload(cfg, state, {"step": 3}), path)
+    payload = torch.load(path, weights_only=True)
+    assert set(payload["config"]) == set(ref_fields)
+    RefModelConfig = dataclasses.make_dataclass(  # the reference's field set, nothing more
+        "RefModelConfig", [(f, object, dataclasses.field(default=None)) for f in ref_fields])
+    RefModelConfig(**payload["config"])
+    back, st = load_checkpoint(path)
+    assert (back.n_kv_heads, back.dtype, back.d_model) == (2, "bfloat16", 32)
+    assert st["lm_head.weight"].data_ptr() == st["embed.weight"].data_ptr()  # one storage
+
+
 def test_checkpoint_in_the_reference_format_loads(tmp_path) -> None:
     """A payload laid out as the reference's Transformer.save writes it
     (reference model.py:356-362): config keys of the reference only, a
@@ -572,3 +604,25 @@ def test_checkpoint_in_the_reference_format_loads(tmp_path) -> None:
     torch.save({"config": ref_cfg, "state_dict": state, "obj": object()}, tmp_path / "bad.pt")
     with pytest.raises(Exception):
         load_checkpoint(tmp_path / "bad.pt")
+
+
+@pytest.mark.parametrize("case", range(5))
+def test_scheduler_decisions_match_the_reference(case: int) -> None:
+    """The same synthetic serving run under memory pressure, driven through
+    the reference's Scheduler by ``make_golden.py`` and through this one:
+    every step schedules and preempts the same requests in the same order
+    (FCFS / SJF / LIFO, continuous and static batching, speculative
+    reservations of 4 and 6 slots)."""
+    import sys
+
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import workloads as wl
+
+    spec = wl.SCHEDULER_CASES[case]
+    cache = host_cache(block_size=4, num_blocks=spec[3])
+    trace = wl.scheduler_trace(Request, Scheduler, SamplingConfig, SchedulerConfig, cache, spec)
+    with np.load(ROOT / "tests" / "golden" / "config_fixtures.npz") as z:
+        want = z[f"sched/{case}"].tolist()
+        steps = int(z[f"sched/{case}/steps"])
+    assert len(trace) == steps
+    assert [x for rec in trace for x in rec] == want

@@ -10,7 +10,7 @@ from oracle.model import Dims, OracleModel, SeqKV
 from oracle.sampling import Row, draw, filter_row, verify, verify_probs
 from oracle.spec import OracleRequest, spec_round
 
-from .conftest import tiny_dims, tiny_state
+from .conftest import ROOT, tiny_dims, tiny_state
 
 TOL = dict(rtol=1e-5, atol=1e-5)
 
@@ -155,3 +155,19 @@ def test_rejection_rule_is_unbiased() -> None:
     assert chisquare(counts, expected).pvalue > 0.01
     biased = np.bincount([draw(q, float(u)) for u in us], minlength=V)
     assert chisquare(biased, expected).pvalue < 0.01
+
+
+def test_kat_fixture_holds_the_published_acceptance() -> None:
+    """The stored reference run of the trained checkpoints reproduces the
+    published greedy acceptance (artifacts/spec_stats.json:6-35) and 8/8
+    greedy matches, so the device test compares against pinned figures."""
+    kat = np.load(ROOT / "tests" / "golden" / "kat_fixtures.npz")
+    published = {1: 0.7142857142857143, 2: 0.6428571428571429, 4: 0.45588235294117646,
+                 7: 0.3469387755102041}
+    assert kat["prompts"].shape == (8, 32)
+    for g, rate in published.items():
+        acc, prop = kat[f"spec{g}/counts"][-1]
+        assert acc / prop == pytest.approx(rate, abs=1e-12)
+        assert float(kat[f"spec{g}/published_acceptance"]) == rate
+        for i in range(8):
+            assert kat[f"spec{g}/{i}"].tolist() == kat["dense"][i].tolist()
