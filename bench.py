@@ -69,12 +69,19 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--requests", type=int, default=256, help="requests per GPU")
+    ap.add_argument("--requests", type=int, default=256, help="requests per GPU (weak scaling)")
+    ap.add_argument("--total-requests", type=int, default=0,
+                    help="strong scaling: one set of this many requests split over the GPUs, "
+                         "served in waves of what fits in HBM")
     ap.add_argument("--ctx-min", type=int, default=512)
     ap.add_argument("--ctx-max", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--cpu-requests", type=int, default=2, help="CPU sample: requests per round")
-    ap.add_argument("--cpu-rounds", type=int, default=2, help="CPU sample: rounds (my arm)")
+    ap.add_argument("--cpu-requests", type=int, default=4,
+                    help="cpu_baseline of the GPU arm: requests in the reference's sample")
+    ap.add_argument("--cpu-requests-ref", type=int, default=0,
+                    help="--impl reference: fix the sample size (default: sized by time and memory)")
+    ap.add_argument("--ref-seconds", type=float, default=120.0,
+                    help="--impl reference: target seconds for the warm-up and timed steps")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--small", action="store_true", help="tiny model (for profiling captures)")
     ap.add_argument("--model", choices=["1b", "8b"], default="1b",
@@ -174,6 +181,72 @@ def gemm_flops_per_round(shape: dict[str, int], tcfg, dcfg) -> float:
     return draft + per_pass(tcfg, shape["Tv"], B * (G + 1))
 
 
+class RequestSet:
+    """The requests one rank serves, with their global ids.
+
+    Weak scaling (default): every rank has its own ``--requests`` requests
+    (contexts and token ids from a per-rank seed).  Strong scaling
+    (``--total-requests T``): one set of T requests, the same on every rank,
+    partitioned by ``distributed.shard_requests`` (longest-processing-time on
+    context plus the tokens the timed rounds can add); a request's token ids
+    and its generator seed depend only on its global id, so its stream is
+    the same for any number of GPUs."""
+
+    def __init__(self, args: argparse.Namespace, rank: int, world: int, vocab: int) -> None:
+        from microserve_b200 import distributed
+
+        self.strong = bool(args.total_requests)
+        if self.strong:
+            total = args.total_requests
+            ctx_all = contexts(total, args.ctx_min, args.ctx_max, args.seed * 1000)
+            cost = (ctx_all + args.steps * (GAMMA + 1)).astype(float).tolist()
+            self.ids = np.asarray(distributed.shard_requests(cost, world, rank), dtype=np.int64)
+            self.ctx = ctx_all[self.ids]
+            self.total = total
+        else:
+            rng_seed = args.seed * 1000 + rank
+            self.ctx = contexts(args.requests, args.ctx_min, args.ctx_max, rng_seed)
+            self.ids = rank * args.requests + np.arange(args.requests, dtype=np.int64)
+            self.total = args.requests * world
+            tok_rng = np.random.default_rng(rng_seed + 7)
+            self._prompts = [tok_rng.integers(0, vocab, int(c)).tolist() for c in self.ctx]
+            self._seeds = [rng_seed * 100003 + i for i in range(args.requests)]
+        self.args = args
+        self.vocab = vocab
+
+    def __len__(self) -> int:
+        return len(self.ids)
+
+    def prompt(self, k: int) -> list[int]:
+        if not self.strong:
+            return self._prompts[k]
+        rng = np.random.default_rng([self.args.seed, int(self.ids[k])])
+        return rng.integers(0, self.vocab, int(self.ctx[k])).tolist()
+
+    def seed(self, k: int) -> int:
+        if not self.strong:
+            return self._seeds[k]
+        return self.args.seed * 100003 + int(self.ids[k])
+
+
+def plan_waves(ctx: np.ndarray, per_req_blocks: np.ndarray, cap_blocks: int, max_batch: int
+               ) -> list[np.ndarray]:
+    """Consecutive groups of the rank's requests that fit the cache together:
+    admission with a waiting queue, a wave entering when the previous one
+    has finished its rounds."""
+    waves, cur, used = [], [], 0
+    for k in range(len(ctx)):
+        b = int(per_req_blocks[k])
+        if cur and (used + b > cap_blocks or len(cur) >= max_batch):
+            waves.append(np.asarray(cur))
+            cur, used = [], 0
+        cur.append(k)
+        used += b
+    if cur:
+        waves.append(np.asarray(cur))
+    return waves
+
+
 def run_gpu(args: argparse.Namespace) -> None:
     import torch
 
@@ -191,41 +264,59 @@ def run_gpu(args: argparse.Namespace) -> None:
     tcfg, dcfg = model_cfgs(args.small)
     target = Transformer(tcfg, dev, seed=args.seed)
     draft = Transformer(dcfg, dev, seed=args.seed + 1)
+    reqset = RequestSet(args, info.rank, info.world_size, tcfg.vocab_size)
 
-    B = args.requests
-    rng_seed = args.seed * 1000 + info.rank
-    ctx = contexts(B, args.ctx_min, args.ctx_max, rng_seed)
-    # warm-up, timed, GEMM-profile (as many as timed) and attention-rate rounds
+    # Cache blocks per request: its context plus every round this run makes
+    # (warm-up, timed, GEMM-profile and attention-rate rounds).
     rounds_total = args.warmup + 2 * args.steps + 2
-    per_req_blocks = (ctx + rounds_total * (GAMMA + 1) + 2 * BLOCK) // BLOCK + 1
-    nblocks = int(per_req_blocks.sum()) + 64
+    per_req_blocks = (reqset.ctx + rounds_total * (GAMMA + 1) + 2 * BLOCK) // BLOCK + 1
+    # Resident requests: as many as the free HBM holds (K/V of both models,
+    # logits rows of a round), the rest wait for the next wave.
+    kv_block_bytes = BLOCK * 2 * 2 * (tcfg.n_layers * tcfg.kv_heads * tcfg.d_head
+                                      + dcfg.n_layers * dcfg.kv_heads * dcfg.d_head)
+    logit_bytes = (2 * GAMMA + 1) * tcfg.vocab_size * 4
+    free_b, _ = torch.cuda.mem_get_info(dev)
+    budget = 0.85 * free_b - 4e9  # workspace, sampler scratch, allocator slack
+    mean_blocks = float(per_req_blocks.mean()) if len(reqset) else 1.0
+    max_batch = max(1, int(budget / (mean_blocks * kv_block_bytes + logit_bytes)))
+    cap_blocks = max(int(per_req_blocks.max()) if len(reqset) else 1,
+                     int((budget - max_batch * logit_bytes) / kv_block_bytes))
+    waves = plan_waves(reqset.ctx, per_req_blocks, cap_blocks, max_batch)
+    nblocks = max(int(per_req_blocks[w].sum()) for w in waves) + 64
     ccfg = CacheConfig(BLOCK, nblocks, "bfloat16")
     tcache = PagedKVCache(tcfg, ccfg, dev)
     dec = SpeculativeDecoder(target, draft, ccfg, gamma=GAMMA, device=dev)
-    # interleave block allocation across requests (non-contiguous tables)
-    tok_rng = np.random.default_rng(rng_seed + 7)
-    sc = SamplingConfig(temperature=0.8, top_p=0.9, max_new_tokens=1 << 30)
-    reqs, gens = [], {}
-    for i in range(B):
-        prompt = tok_rng.integers(0, tcfg.vocab_size, int(ctx[i])).tolist()
-        r = Request(i, prompt, sc)
-        r.num_computed = len(prompt) - 1
-        reqs.append(r)
-        gens[i] = torch.Generator().manual_seed(rng_seed * 100003 + i)
-    remaining = (ctx - 1).copy()
-    while remaining.max() > 0:
-        step = np.minimum(remaining, BLOCK)
-        live = [i for i in range(B) if step[i] > 0]
-        tcache.append_many(live, step[live])
-        dec.draft_cache.append_many(live, step[live])
-        remaining -= step
-    g = torch.Generator(device=dev).manual_seed(rng_seed)
-    for pool in (tcache.pool, dec.draft_cache.pool):
+    g = torch.Generator(device=dev).manual_seed(args.seed * 1000 + info.rank)
+    for pool in (tcache.pool, dec.draft_cache.pool):  # synthetic K/V for every context
         for lyr in range(pool.shape[1]):
             pool[:, lyr].normal_(generator=g)
-    torch.cuda.synchronize()
+    sc = SamplingConfig(temperature=0.8, top_p=0.9, max_new_tokens=1 << 30)
 
-    def one_round() -> int:
+    def admit(wave: np.ndarray) -> tuple[list, dict]:
+        """Take a wave into the caches: its contexts' slots are reserved
+        (interleaved, 16 tokens at a time: non-contiguous tables) and hold
+        the synthetic K/V already in the pools."""
+        tcache.reset()
+        dec.reset()
+        reqs, gens = [], {}
+        for k in wave.tolist():
+            prompt = reqset.prompt(k)
+            r = Request(int(reqset.ids[k]), prompt, sc)
+            r.num_computed = len(prompt) - 1
+            reqs.append(r)
+            gens[r.request_id] = torch.Generator().manual_seed(reqset.seed(k))
+        ids = np.asarray([r.request_id for r in reqs])
+        remaining = reqset.ctx[wave] - 1
+        while remaining.max() > 0:
+            step = np.minimum(remaining, BLOCK)
+            live = step > 0
+            tcache.append_many(ids[live].tolist(), step[live])
+            dec.draft_cache.append_many(ids[live].tolist(), step[live])
+            remaining -= step
+        torch.cuda.synchronize(dev)
+        return reqs, gens
+
+    def one_round(reqs: list, gens: dict) -> int:
         out = dec.step(reqs, tcache, gens)
         n = 0
         for r, toks in zip(reqs, out, strict=True):
@@ -233,35 +324,42 @@ def run_gpu(args: argparse.Namespace) -> None:
             n += len(toks)
         return n
 
-    for _ in range(args.warmup):
-        one_round()
-    acc0, prop0 = dec.num_accepted, dec.num_proposed
-    dec.round_events = []
-    launches0 = _lib.launch_count()
     clocks = ClockSampler(info.local_rank) if info.rank == 0 else None
+    emitted = accepted = proposed = 0
+    h2d = d2h = launches = 0
+    dev_ms = e2e_ms = 0.0
     distributed.barrier()
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(dev)
     if clocks:
         clocks.start()
-    start = torch.cuda.Event(enable_timing=True)
-    end = torch.cuda.Event(enable_timing=True)
-    start.record()
-    emitted = 0
-    h2d = d2h = 0
-    for _ in range(args.steps):
-        emitted += one_round()
-        h2d += dec.last_h2d_bytes
-        d2h += dec.last_d2h_bytes
-    end.record()
-    torch.cuda.synchronize()
-    launches = _lib.launch_count() - launches0
+    for wave in waves:
+        reqs, gens = admit(wave)
+        for _ in range(args.warmup):
+            one_round(reqs, gens)
+        acc0, prop0 = dec.num_accepted, dec.num_proposed
+        dec.round_events = []
+        launches0 = _lib.launch_count()
+        torch.cuda.synchronize(dev)
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            emitted += one_round(reqs, gens)
+            h2d += dec.last_h2d_bytes
+            d2h += dec.last_d2h_bytes
+        end.record()
+        torch.cuda.synchronize(dev)
+        launches += _lib.launch_count() - launches0
+        e2e_ms += start.elapsed_time(end)
+        dev_ms += sum(a.elapsed_time(b) for a, b in dec.round_events)
+        dec.round_events = None
+        accepted += dec.num_accepted - acc0
+        proposed += dec.num_proposed - prop0
     distributed.barrier()
+    torch.cuda.synchronize(dev)
     clk = clocks.stop() if clocks else None
-    e2e_ms = start.elapsed_time(end)
-    dev_ms = sum(a.elapsed_time(b) for a, b in dec.round_events)
-    dec.round_events = None
-    # GEMM roofline and verify-step time: as many further rounds of the same
-    # workload with a CUDA-event pair around every GEMM launch (and around the
+    # GEMM roofline and verify-step time: as many further rounds of the last
+    # wave with a CUDA-event pair around every GEMM launch (and around the
     # verify pass).  They stay out of the timed rounds: ~250 event records a
     # round there added ~1.1 ms per round (and broke the programmatic
     # dependent launches between kernels).
@@ -269,9 +367,9 @@ def run_gpu(args: argparse.Namespace) -> None:
     flops = 0.0
     _lib.call("ms_profile_start", 1)
     for _ in range(args.steps):
-        one_round()
+        one_round(reqs, gens)
         flops += gemm_flops_per_round(dec.last_round_shape, tcfg, dcfg)
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(dev)
     gemm_ms = _c_double()
     gemm_n = _c_int64()
     _lib.call("ms_profile_stop", _byref(gemm_ms), _byref(gemm_n))
@@ -285,16 +383,16 @@ def run_gpu(args: argparse.Namespace) -> None:
     kv_bytes = 0.0
     _lib.call("ms_profile_start", 2)
     for _ in range(attn_rounds):
-        one_round()
+        one_round(reqs, gens)
         sh = dec.last_round_shape
         kv_bytes += sh["kv_tokens_verify"] * tcfg.n_layers * 2 * tcfg.kv_heads * tcfg.d_head * 2
         kv_bytes += sh["kv_tokens_draft"] * dcfg.n_layers * 2 * dcfg.kv_heads * dcfg.d_head * 2
-    torch.cuda.synchronize()
+    torch.cuda.synchronize(dev)
     attn_ms = _c_double()
     attn_n = _c_int64()
     _lib.call("ms_profile_stop", _byref(attn_ms), _byref(attn_n))
-    counters = {"emitted": emitted, "accepted": dec.num_accepted - acc0,
-                "proposed": dec.num_proposed - prop0}
+    counters = {"emitted": emitted, "accepted": accepted, "proposed": proposed,
+                "requests": len(reqset), "waves": len(waves)}
     tot, dev_ms_max = distributed.reduce_stats(counters, dev_ms / 1e3)
     _, e2e_s_max = distributed.reduce_stats({}, e2e_ms / 1e3)
     if info.rank != 0:
@@ -303,6 +401,11 @@ def run_gpu(args: argparse.Namespace) -> None:
 
     peaks = _peaks()
     achieved = flops / (gemm_ms.value / 1e3) / 1e12 if gemm_ms.value > 0 else 0.0
+    rounds_timed = args.steps * len(waves)
+    workload = WORKLOAD if not args.small else WORKLOAD + " [small: 2+1 layers]"
+    if reqset.strong:
+        workload = workload.replace(f"{args.requests} req/GPU",
+                                    f"{reqset.total} requests split over the GPUs")
     line = {
         "metric": METRIC,
         "value": tot["emitted"] / dev_ms_max,
@@ -310,15 +413,18 @@ def run_gpu(args: argparse.Namespace) -> None:
         "n_gpus": info.world_size,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": dev_ms_max * 1e3 / args.steps,
+        "ms_per_step": dev_ms_max * 1e3 / rounds_timed,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if reqset.strong else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (random-init weights, uniform token ids, synthetic K/V contexts)",
         "config": {
-            "workload": WORKLOAD if not args.small else WORKLOAD + " [small: 2+1 layers]",
-            "requests_per_gpu": B, "gamma": GAMMA, "block_size": BLOCK,
+            "workload": workload,
+            "requests_total": reqset.total,
+            "requests_rank0": len(reqset), "waves_rank0": len(waves),
+            "resident_max": int(max(len(w) for w in waves)),
+            "gamma": GAMMA, "block_size": BLOCK,
             "ctx_range": [args.ctx_min, args.ctx_max],
             "target": TARGET if not args.small else dict(TARGET, n_layers=2),
             "draft_layers": dcfg.n_layers, "temperature": 0.8, "top_p": 0.9,
@@ -345,9 +451,9 @@ def run_gpu(args: argparse.Namespace) -> None:
         "e2e": {
             "value": tot["emitted"] / e2e_s_max,
             "unit": "tok/s",
-            "h2d_bytes_per_step": h2d // args.steps,
-            "d2h_bytes_per_step": d2h // args.steps,
-            "ms_per_step": e2e_s_max * 1e3 / args.steps,
+            "h2d_bytes_per_step": h2d // rounds_timed,
+            "d2h_bytes_per_step": d2h // rounds_timed,
+            "ms_per_step": e2e_s_max * 1e3 / rounds_timed,
         },
         "gpu_launches": int(launches),
         "roofline": {
@@ -367,7 +473,7 @@ def run_gpu(args: argparse.Namespace) -> None:
         "clocks": clk,
     }
     if not args.no_cpu_baseline and info.world_size == 1:
-        line["cpu_baseline"] = cpu_baseline(args, rounds=args.cpu_rounds)
+        line["cpu_baseline"] = cpu_baseline(args)
     print(json.dumps(line), flush=True)
     distributed.shutdown()
 
@@ -400,13 +506,202 @@ def _peaks() -> dict[str, object]:
     return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
 
 
-# -- CPU side (the oracle restatement of the reference path) ----------------------------
-def cpu_workload(args: argparse.Namespace, n_req: int, seed: int):
-    """Host-generated random weights of the same architecture and a sample of
-    requests with synthetic K/V histories (float32, the reference's dtype)."""
-    from oracle.model import Dims, OracleModel, SeqKV
-    from oracle.spec import OracleRequest
+# -- CPU side: the reference's own implementation of the path -------------------------------
+REF_DIR = ROOT / "baseline" / "_ref"
 
+
+def reference_installed() -> bool:
+    return (REF_DIR / "microserve" / "speculative.py").exists()
+
+
+class ReferenceRun:
+    """The unmodified reference (``baseline/_ref``: its ``SpeculativeDecoder``,
+    ``Transformer``, ``PagedKVCache`` and samplers, float32 on the CPU) on a
+    sample of the benchmark workload: the first ``n`` requests of rank 0's
+    request set (the same contexts and token ids as the GPU arm), the same
+    model shapes with the same initialisation recipe (the reference's own
+    init, weights rounded to bf16 values), grouped-query attention expressed
+    as the reference's multi-head attention with each K/V head's projection
+    rows repeated over its query group, and synthetic K/V histories written
+    into its cache pools.  One step = one ``SpeculativeDecoder.step`` over the
+    sample; emitted tokens are appended as the engine does."""
+
+    def __init__(self, args: argparse.Namespace, n_req: int, threads: int) -> None:
+        import torch
+
+        if str(REF_DIR) not in sys.path:
+            sys.path.insert(0, str(REF_DIR))
+        from microserve.cache import PagedKVCache
+        from microserve.config import CacheConfig, ModelConfig, SamplingConfig
+        from microserve.model import Transformer
+        from microserve.scheduler import Request
+        from microserve.speculative import SpeculativeDecoder
+
+        torch.set_num_threads(threads)
+        self.threads = torch.get_num_threads()
+        torch.manual_seed(args.seed)
+        t, d = dict(TARGET), dict(DRAFT)
+        if args.small:
+            t.update(n_layers=2)
+            d.update(n_layers=1)
+
+        def build(c: dict) -> object:
+            cfg = ModelConfig(vocab_size=c["vocab_size"], n_layers=c["n_layers"],
+                              d_model=c["d_model"], n_heads=c["n_heads"], d_ff=c["d_ff"],
+                              max_seq_len=MAX_SEQ, rope_theta=c["rope_theta"])
+            m = Transformer(cfg).eval()
+            dh, group = c["d_model"] // c["n_heads"], c["n_heads"] // c["n_kv_heads"]
+            with torch.no_grad():
+                for blk in m.blocks:
+                    for lin in (blk.attn.k_proj, blk.attn.v_proj):
+                        w = lin.weight
+                        kv = w[: c["n_kv_heads"] * dh].view(c["n_kv_heads"], dh, -1)
+                        w.copy_(kv.repeat_interleave(group, 0).reshape(w.shape))
+                for prm in m.parameters():
+                    prm.copy_(prm.bfloat16().float())
+            return m
+
+        self.target, self.draft = build(t), build(d)
+        ctx = contexts(args.requests, args.ctx_min, args.ctx_max, args.seed * 1000)[:n_req]
+        rounds = args.warmup + args.steps + 2
+        blocks = int(((ctx + rounds * (GAMMA + 1) + 2 * BLOCK) // BLOCK + 1).sum()) + 16
+        ccfg = CacheConfig(block_size=BLOCK, num_blocks=blocks)
+        self.cache = PagedKVCache(self.target.cfg, ccfg)
+        self.dec = SpeculativeDecoder(self.target, self.draft, ccfg, gamma=GAMMA)
+        tok_rng = np.random.default_rng(args.seed * 1000 + 7)
+        sc = SamplingConfig(temperature=0.8, top_p=0.9, max_new_tokens=1 << 30)
+        self.reqs, self.gens = [], {}
+        for i in range(n_req):
+            prompt = tok_rng.integers(0, t["vocab_size"], int(ctx[i])).tolist()
+            r = Request(request_id=i, prompt_ids=prompt, sampling=sc)
+            r.num_computed = len(prompt) - 1
+            self.cache.append(i, len(prompt) - 1)
+            self.dec.draft_cache.append(i, len(prompt) - 1)
+            self.reqs.append(r)
+            self.gens[i] = torch.Generator().manual_seed(args.seed * 100003 + i)
+        bank = torch.randn(1 << 20, generator=torch.Generator().manual_seed(args.seed))
+        for c in (self.cache, self.dec.draft_cache):
+            for pool in (*c.k_cache, *c.v_cache):
+                flat = pool.view(-1)
+                reps = flat.numel() // bank.numel()
+                flat[: reps * bank.numel()].view(reps, -1).copy_(bank.expand(reps, -1))
+                flat[reps * bank.numel():].copy_(bank[: flat.numel() - reps * bank.numel()])
+        self.n = n_req
+        self.accepted = 0
+        self.proposed = 0
+
+    @staticmethod
+    def bytes_per_request(args: argparse.Namespace) -> float:
+        """Host memory one request takes: its share of both float32 caches
+        (multi-head layout) and of the padded gather of a pass."""
+        t = TARGET
+        per_tok = 2 * t["d_model"] * 4 * (t["n_layers"] + DRAFT["n_layers"])
+        return per_tok * (args.ctx_max + 64) * 1.5
+
+    def rounds(self, k: int) -> tuple[int, float]:
+        """``k`` steps; returns (emitted tokens, seconds)."""
+        emitted = 0
+        acc0, prop0 = self.dec.num_accepted, self.dec.num_proposed
+        t0 = time.perf_counter()
+        for _ in range(k):
+            out = self.dec.step(self.reqs, self.cache, self.gens)
+            for r, toks in zip(self.reqs, out, strict=True):
+                r.output_ids.extend(toks)
+                emitted += len(toks)
+        secs = time.perf_counter() - t0
+        self.accepted += self.dec.num_accepted - acc0
+        self.proposed += self.dec.num_proposed - prop0
+        return emitted, secs
+
+
+def _available_ram() -> float:
+    try:
+        import psutil
+
+        return float(psutil.virtual_memory().available)
+    except ImportError:
+        return float(os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE"))
+
+
+def cpu_baseline(args: argparse.Namespace) -> dict[str, object]:
+    """The reference's CPU path on a bounded sample (a few requests x 2 steps,
+    all host cores), reported beside the GPU number; the numpy restatement
+    when the reference is not installed."""
+    n = max(1, args.cpu_requests)
+    if not reference_installed():
+        return cpu_baseline_port(args, n)
+    run = ReferenceRun(args, n, os.cpu_count() or 1)
+    run.rounds(1)
+    emitted, secs = run.rounds(2)
+    return {"value": emitted / secs, "unit": "tok/s", "cores": run.threads, "kind": "reference",
+            "sample": f"{n} of the workload's requests x 2 steps of the unmodified reference "
+                      f"SpeculativeDecoder (float32, CPU), {secs:.1f} s"}
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    """``--impl reference``: the reference's own CPU implementation of the
+    speculative step, on this host's cores, for the same metric and workload.
+
+    The sample is the first n requests of the workload, n the largest that
+    fits half of the free host memory and keeps the warm-up and timed steps
+    near two minutes (from a timed probe step of a few requests), at most the
+    workload's request count.  Rank 0 runs it; other ranks exit."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    cores = os.cpu_count() or 1
+    if not reference_installed():
+        print(json.dumps({"impl": "reference", "metric": METRIC,
+                          "unavailable": "baseline/_ref is not installed"}), flush=True)
+        return
+    probe_n = min(4, args.requests)
+    probe = ReferenceRun(args, probe_n, cores)
+    probe.rounds(1)
+    _, secs = probe.rounds(1)
+    per_req_s = secs / probe_n
+    budget_s = float(args.ref_seconds)
+    by_time = int(budget_s / max(1e-6, per_req_s * (args.warmup + args.steps)))
+    by_ram = int(0.5 * _available_ram() / ReferenceRun.bytes_per_request(args))
+    n = max(1, min(args.requests, by_time, by_ram))
+    del probe
+    if args.cpu_requests_ref:
+        n = min(args.requests, args.cpu_requests_ref)
+    run = ReferenceRun(args, n, cores)
+    run.rounds(args.warmup)
+    emitted, secs = run.rounds(args.steps)
+    value = emitted / secs
+    # the reference's published setting: one thread, one step of a small sample
+    one = ReferenceRun(args, min(n, 4), 1)
+    e1, s1 = one.rounds(1)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (random-init weights, uniform token ids, synthetic K/V contexts)",
+        "impl": "reference",
+        "config": {"workload": WORKLOAD, "requests_sampled": n, "requests_in_workload": args.requests,
+                   "same_config": n == args.requests, "gamma": GAMMA, "block_size": BLOCK,
+                   "ctx_range": [args.ctx_min, args.ctx_max], "temperature": 0.8, "top_p": 0.9},
+        "acceptance_rate": run.accepted / max(1, run.proposed),
+        "per_request_tok_s": value / n,
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": run.threads, "kind": "reference",
+                         "sample": f"first {n} of {args.requests} requests of the workload, "
+                                   f"{args.steps} steps of the unmodified reference "
+                                   "SpeculativeDecoder.step (float32 on the CPU, GQA as "
+                                   "repeated K/V heads)",
+                         "single_thread": {"value": e1 / s1, "unit": "tok/s", "threads": 1,
+                                           "sample": f"{min(n, 4)} requests x 1 step"}},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# -- the numpy restatement, when the reference is not installed ----------------------------
+def cpu_baseline_port(args: argparse.Namespace, n_req: int) -> dict[str, object]:
+    """The oracle restatement of the same round on a few requests (kind "port")."""
+    from oracle.model import Dims, OracleModel
+    from oracle.spec import OracleRequest, spec_round
+
+    seed = args.seed + 99
     rng = np.random.default_rng(seed)
 
     def state(cfg: dict) -> dict[str, np.ndarray]:
@@ -428,77 +723,35 @@ def cpu_workload(args: argparse.Namespace, n_req: int, seed: int):
             st[p + "ffn_norm.weight"] = np.ones(d, np.float32)
         return st
 
-    t = dict(TARGET)
-    dr = dict(DRAFT)
+    t, dr = dict(TARGET), dict(DRAFT)
     if args.small:
         t.update(n_layers=2)
         dr.update(n_layers=1)
     dims = lambda c: Dims(c["vocab_size"], c["d_model"], c["n_layers"], c["n_heads"],  # noqa: E731
-                          c["n_kv_heads"], c["d_ff"], 4096, c["rope_theta"])
-    target = OracleModel(dims(t), state(t))
-    draft = OracleModel(dims(dr), state(dr))
+                          c["n_kv_heads"], c["d_ff"], MAX_SEQ, c["rope_theta"])
+    target, draft = OracleModel(dims(t), state(t)), OracleModel(dims(dr), state(dr))
     ctx = contexts(n_req, args.ctx_min, args.ctx_max, seed + 1)
     reqs = []
     for i in range(n_req):
-        prompt = rng.integers(0, t["vocab_size"], int(ctx[i])).tolist()
-        r = OracleRequest(i, prompt, 0.8, None, 0.9, seed=seed * 7 + i)
+        r = OracleRequest(i, rng.integers(0, t["vocab_size"], int(ctx[i])).tolist(), 0.8, None,
+                          0.9, seed=seed * 7 + i)
         dh = t["d_model"] // t["n_heads"]
         for kv, cfg in ((r.target_kv, t), (r.draft_kv, dr)):
             shape = (int(ctx[i]) - 1, cfg["n_kv_heads"], dh)
             kv.k = [rng.standard_normal(shape, dtype=np.float32) for _ in range(cfg["n_layers"])]
             kv.v = [rng.standard_normal(shape, dtype=np.float32) for _ in range(cfg["n_layers"])]
         reqs.append(r)
-    _ = SeqKV
-    return target, draft, reqs
-
-
-def cpu_rounds(target, draft, reqs, rounds: int) -> tuple[int, float]:
-    from oracle.spec import spec_round
-
     emitted = 0
     t0 = time.perf_counter()
-    for _ in range(rounds):
+    for _ in range(2):
         tr = spec_round(target, draft, GAMMA, reqs)
         for r, toks in zip(reqs, tr.emitted, strict=True):
             r.output_ids.extend(toks)
             emitted += len(toks)
-    return emitted, time.perf_counter() - t0
-
-
-def cpu_baseline(args: argparse.Namespace, rounds: int) -> dict[str, object]:
-    target, draft, reqs = cpu_workload(args, args.cpu_requests, args.seed + 99)
-    emitted, secs = cpu_rounds(target, draft, reqs, rounds)
-    return {
-        "value": emitted / secs,
-        "unit": "tok/s",
-        "cores": os.cpu_count(),
-        "kind": "port",
-        "sample": f"{args.cpu_requests} requests x {rounds} rounds of the same workload, "
-                  f"numpy float32 oracle (multithreaded BLAS), {secs:.1f} s",
-    }
-
-
-def run_reference(args: argparse.Namespace) -> None:
-    """The reference's CPU path (its numpy restatement) on this host's cores."""
-    info_rank = int(os.environ.get("RANK", "0"))
-    if info_rank != 0:
-        return
-    target, draft, reqs = cpu_workload(args, args.cpu_requests, args.seed + 99)
-    cpu_rounds(target, draft, reqs, args.warmup)  # warm-up rounds append their tokens too
-    emitted, secs = cpu_rounds(target, draft, reqs, args.steps)
-    value = emitted / secs
-    line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": secs * 1e3 / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "sample_requests_per_step": args.cpu_requests},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"{args.cpu_requests} requests per step, numpy float32 "
-                                   "restatement of the reference path"},
-        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
+    secs = time.perf_counter() - t0
+    return {"value": emitted / secs, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{n_req} requests x 2 steps, numpy float32 restatement of the reference "
+                      f"path (the reference is not installed), {secs:.1f} s"}
 
 
 # -- kernel micro-benchmarks (one GPU; not the headline metric) --------------------------

@@ -114,3 +114,54 @@ def test_a_rank_that_dies_fails_the_survivors_collective() -> None:
     survivor = [r for r in results if r[0] == 0]
     assert survivor, results
     assert survivor[0][1] not in ("no error",) and not survivor[0][1].startswith("setup"), survivor
+
+
+def test_strong_scaling_request_sets_do_not_depend_on_the_gpu_count() -> None:
+    """bench.py --total-requests: every request lands on exactly one rank for
+    any world size, and its token ids, context and generator seed depend
+    only on its global id -- the premise of identical streams at any N."""
+    import argparse
+    import sys
+
+    import numpy as np
+
+    from .conftest import ROOT
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    args = argparse.Namespace(total_requests=96, requests=256, ctx_min=8, ctx_max=300, seed=3,
+                              steps=4)
+    want = {}
+    for world in (1, 2, 4, 8):
+        seen = {}
+        for rank in range(world):
+            rs = bench.RequestSet(args, rank, world, 500)
+            for k, gid in enumerate(rs.ids.tolist()):
+                assert gid not in seen
+                seen[gid] = (rs.prompt(k), rs.seed(k), int(rs.ctx[k]))
+        assert sorted(seen) == list(range(96))
+        if not want:
+            want = seen
+        assert seen == want
+        loads = [sum(len(seen[g][0]) for g in bench.RequestSet(args, r, world, 500).ids.tolist())
+                 for r in range(world)]
+        assert max(loads) <= 1.25 * np.mean(loads) + 300  # LPT keeps the ranks balanced
+
+
+def test_waves_cover_every_request_once_within_the_cache() -> None:
+    import sys
+
+    import numpy as np
+
+    from .conftest import ROOT
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    rng = np.random.default_rng(0)
+    blocks = rng.integers(1, 40, 300)
+    waves = bench.plan_waves(np.zeros(300), blocks, cap_blocks=500, max_batch=64)
+    assert np.concatenate(waves).tolist() == list(range(300))
+    for w in waves:
+        assert blocks[w].sum() <= 500 and len(w) <= 64

@@ -153,3 +153,36 @@ def test_sampled_rounds_match_oracle_draw_for_draw(golden, setting) -> None:
             oreqs[i].output_ids.extend(tr.emitted[j])
             assert cache.num_tokens(i) == reqs[i].num_tokens - 1
     assert len(diverged) <= 1, diverged
+
+
+def test_streams_do_not_depend_on_how_requests_are_sharded(golden) -> None:
+    """Eight sampled requests served by one decoder, and split over two
+    decoders by the longest-processing-time partition of two ranks: every
+    request's stream is the same, because its Philox stream is keyed by its
+    own generator seed and round counter, never by its batch or rank."""
+    from microserve_b200 import distributed
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.scheduler import Request
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 32, int(n)).tolist() for n in rng.integers(2, 30, 8)]
+    sc = SamplingConfig(temperature=0.8, top_p=0.95, max_new_tokens=64)
+
+    def serve(ids: list[int]) -> dict[int, list[int]]:
+        dec = SpeculativeDecoder(target, draft, _cache_cfg(8, 96), gamma=3)
+        cache = PagedKVCache(target.cfg, _cache_cfg(8, 96), DEV)
+        reqs = [Request(g, list(prompts[g]), sc) for g in ids]
+        gens = {g: torch.Generator().manual_seed(700 + g) for g in ids}
+        for _ in range(5):
+            for r, toks in zip(reqs, dec.step(reqs, cache, gens), strict=True):
+                r.output_ids.extend(toks)
+        return {r.request_id: r.output_ids for r in reqs}
+
+    one = serve(list(range(8)))
+    two: dict[int, list[int]] = {}
+    for rank in range(2):
+        two.update(serve(distributed.shard_requests([float(len(p)) for p in prompts], 2, rank)))
+    assert two == one
