@@ -113,8 +113,14 @@ class SchedulerConfig:
     max_batched_tokens: int = 2048
     watermark: float = 0.01
     preemption_mode: str = "recompute"
+    # Chunked prefill (an addition): a prefilling request processes at most
+    # this many of its uncomputed tokens per step; None = the whole prompt
+    # in one pass, as the reference does.
+    prefill_chunk: int | None = None
 
     def __post_init__(self) -> None:
+        if self.prefill_chunk is not None and self.prefill_chunk < 1:
+            raise ValueError("prefill_chunk must be at least 1")
         if self.policy not in {"fcfs", "sjf", "lifo"}:
             raise ValueError(f"unknown scheduling policy {self.policy!r}")
         if self.batching not in {"continuous", "static"}:

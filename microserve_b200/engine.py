@@ -126,6 +126,8 @@ class LLMEngine:
         self._meta_upload = HostStaging(self.device)
         self._param_upload = HostStaging(self.device)
         self._q_start = np.zeros(1, dtype=np.int32)  # the last built pass's row offsets
+        self.lookahead = True  # let the decoder draft the next round ahead (same streams)
+        self._no_rows = torch.zeros(1, dtype=torch.int32, device=self.device)[:0]  # no logits
         self.spec = None
         if draft_model is not None and self.config.speculative.enabled:
             from .speculative import SpeculativeDecoder
@@ -197,6 +199,9 @@ class LLMEngine:
         batch = plan.scheduled
         if self._round_fits(plan):
             assert self.spec is not None
+            # drafting the next round ahead pays off only if the batch stays
+            # the same, which requests still waiting for admission make unlikely
+            self.spec.lookahead = self.lookahead and not self.scheduler.waiting
             tokens = self.spec.step(batch, self.cache, self._generators)
             self.stats.num_spec_rounds += 1
             self.stats.num_draft_proposed = self.spec.num_proposed
@@ -232,25 +237,36 @@ class LLMEngine:
         return done
 
     def _ordinary_pass(self, batch: list[Request]) -> list[list[int]]:
-        """One paged forward over every request's uncomputed tokens, then one
-        draw per request from its last row (reference engine.py:204-220)."""
+        """One paged forward over every request's uncomputed tokens (or the
+        next chunk of them), then one draw from the last row of each request
+        whose tokens are now all computed (reference engine.py:204-220).  A
+        request whose prefill continues in a later chunk draws nothing and
+        keeps its round counter, so its stream equals the unchunked one."""
         meta = self.build_batch(batch)
-        last_rows = (self._q_start[1:] - 1).astype(np.int32)
-        seeds = [self._generators[r.request_id].initial_seed() for r in batch]
-        params = make_params([r.sampling for r in batch], seeds, [r.rng_step for r in batch])
+        done = [i for i, r in enumerate(batch) if r.num_uncomputed == 0]
+        out: list[list[int]] = [[] for _ in batch]
+        if not done:
+            self.model.forward_paged(meta, self.cache, logit_rows=self._no_rows)
+            return out
+        fin = [batch[i] for i in done]
+        last_rows = (self._q_start[1:] - 1).astype(np.int32)[done]
+        seeds = [self._generators[r.request_id].initial_seed() for r in fin]
+        params = make_params([r.sampling for r in fin], seeds, [r.rng_step for r in fin])
         blob, spans = pack_int32([params.view(np.int32), last_rows])
         dev = self._param_upload.upload(blob)
         (p_off, _), (r_off, r_len) = spans
         rows = dev[r_off : r_off + r_len]
         logits = self.model.forward_paged(meta, self.cache, logit_rows=rows)
         V = self.model.cfg.vocab_size
-        drawn = torch.empty(len(batch), dtype=torch.int32, device=self.device)
-        _lib.call("ms_sample", logits.data_ptr(), V, len(batch), V, dev[p_off:].data_ptr(), None,
+        drawn = torch.empty(len(fin), dtype=torch.int32, device=self.device)
+        _lib.call("ms_sample", logits.data_ptr(), V, len(fin), V, dev[p_off:].data_ptr(), None,
                   _lib.LANE_SAMPLE, drawn.data_ptr(), None, None, None, None,
                   _lib.stream_ptr(self.device))
-        for r in batch:
+        for r in fin:
             r.rng_step += 1
-        return [[t] for t in drawn.cpu().tolist()]
+        for i, t in zip(done, drawn.cpu().tolist(), strict=True):
+            out[i] = [t]
+        return out
 
     def build_batch(self, batch: list[Request]) -> PagedBatch:
         """Reserve cache slots for every request's uncomputed tokens and upload
@@ -258,7 +274,7 @@ class LLMEngine:
         ``RuntimeError`` for a request with nothing to do and
         ``OutOfCacheMemory`` when a request's tokens do not fit."""
         ids = [r.request_id for r in batch]
-        todo = [r.num_uncomputed for r in batch]
+        todo = [self.scheduler.step_len(r) for r in batch]
         for r, n in zip(batch, todo, strict=True):
             if n <= 0:
                 raise RuntimeError(f"request {r.request_id} has nothing to do")
@@ -269,7 +285,8 @@ class LLMEngine:
         starts = [r.num_computed for r in batch]
         try:
             parts, width, max_q, n_tokens = host_batch_arrays(
-                self.cache, ids, [r.tail(s) for r, s in zip(batch, starts, strict=True)], starts)
+                self.cache, ids, [r.tail(s)[:n] for r, s, n in zip(batch, starts, todo,
+                                                                   strict=True)], starts)
         except OutOfCacheMemory as e:
             raise OutOfCacheMemory(f"{e}; raise cache.num_blocks") from e
         for r, n in zip(batch, todo, strict=True):

@@ -156,6 +156,7 @@ class Transformer:
         self.dtype_code = _lib.DTYPE_CODES[cfg.dtype]
         self.dtype = _lib.TORCH_DTYPES[self.dtype_code]
         self._ws: torch.Tensor | None = None
+        self._empty_rows: torch.Tensor | None = None
         if init:
             self._random_init(seed)
 
@@ -293,6 +294,11 @@ class Transformer:
         return sum(t.numel() * t.element_size() for t in ts)
 
     # -- forward ---------------------------------------------------------------
+    def _no_rows(self) -> torch.Tensor:
+        if self._empty_rows is None:
+            self._empty_rows = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self._empty_rows[:0]
+
     def workspace(self, n_tokens: int, n_rows: int, attn_scratch: int = 0) -> torch.Tensor:
         """Grow-only device workspace: ms_forward's carve plus ``attn_scratch``
         bytes for the attention's split-KV partials."""
@@ -318,6 +324,10 @@ class Transformer:
         preallocated buffer whose rows are ``out_row_stride`` apart.
         """
         n_rows = batch.n_tokens if logit_rows is None else int(logit_rows.numel())
+        if logit_rows is not None and n_rows == 0:
+            # no logits wanted: a non-null row list of length 0 (a null list
+            # would mean "every row")
+            logit_rows = self._no_rows()
         if out is None:
             out = torch.empty((n_rows, self.cfg.vocab_size), dtype=torch.float32, device=self.device)
             out_row_stride = 0

@@ -19,7 +19,10 @@ How it is organised here:
   subtracts each victim's demand instead of re-summing the set per victim;
 * a request's stop condition is an explicit ``finish_reason`` ("length" or
   "stop"), and ``Request.extend_until_stop`` appends a step's tokens up to
-  it in one slice.
+  it in one slice;
+* with ``SchedulerConfig.prefill_chunk`` (chunked prefill, not in the
+  reference) a prefilling request is charged only the chunk it processes
+  next, for the token budget and for its blocks.
 
 ``Request.rng_step`` (not in the reference) counts the engine iterations a
 request took part in; it is the counter of the request's Philox stream.
@@ -212,9 +215,16 @@ class Scheduler:
         return len(self.waiting) + len(self.running)
 
     # -- one iteration's plan -------------------------------------------------------
+    def step_len(self, request: Request) -> int:
+        """Tokens a request processes in its next pass: all its uncomputed
+        ones, or at most ``prefill_chunk`` of them with chunked prefill."""
+        n = request.num_uncomputed
+        chunk = self.cfg.prefill_chunk
+        return n if chunk is None else min(n, chunk)
+
     def _step_tokens(self, request: Request) -> int:
         """Slots a request needs for its next step (gamma + 1 when speculating)."""
-        return max(self.tokens_per_step, request.num_uncomputed)
+        return max(self.tokens_per_step, self.step_len(request))
 
     def schedule(self, now: float) -> SchedulerOutput:
         plan = SchedulerOutput()
@@ -261,14 +271,14 @@ class Scheduler:
         the batch cap and the free blocks (minus the watermark reserve once
         something is scheduled).  Blocks are debited locally: nothing is
         allocated until the batch is built."""
-        tokens_left = self.cfg.max_batched_tokens - plan.num_tokens
+        tokens_left = self.cfg.max_batched_tokens - sum(self.step_len(r) for r in plan.scheduled)
         blocks_left = self.cache.num_free_blocks - demand
         reserve = int(self.cache.allocator.num_blocks * self.cfg.watermark)
         admitted: list[Request] = []
         for request in self.waiting:
             if len(self.running) >= self.cfg.max_batch_size:
                 break
-            n = request.num_uncomputed
+            n = self.step_len(request)
             busy = bool(plan.scheduled)
             if busy and n > tokens_left:
                 continue

@@ -141,6 +141,11 @@ def _empty(dtype: type = np.int64) -> np.ndarray:
     return np.zeros(0, dtype)
 
 
+class _NotAhead(Exception):
+    """The lookahead cannot plan this batch ahead (a request's uncached
+    tokens are not all among the round's new tokens)."""
+
+
 @dataclass
 class _RoundPlan:
     """What a round's three host phases compute.  :meth:`SpeculativeDecoder._plan`
@@ -188,10 +193,42 @@ class _RoundPlan:
     tw: int = 0
     ctxv: int = 0
     kv_verify: int = 0
+    # device views the verify side reads: sampling parameters, verify token ids
+    dev_params: torch.Tensor | None = None
+    dev_idsv: torch.Tensor | None = None
+
+
+@dataclass
+class _Lookahead:
+    """The draft side of the next round, launched as soon as a round's results
+    were read: what it assumed about the caller's next ``step`` call."""
+
+    plan: _RoundPlan
+    ids: tuple[int, ...]
+    n_tok: np.ndarray  # every request's token count once this round's tokens are appended
+    last: list[int]  # every request's last token then
+    samplings: list[SamplingConfig]
+    seeds: list[int]
+    target_cache: PagedKVCache
+    t_cached: np.ndarray  # the target cache's token counts it planned on
+    events: tuple[torch.cuda.Event, torch.cuda.Event] | None
 
 
 class SpeculativeDecoder:
-    """Batched draft-then-verify over decoding requests (reference speculative.py:89-261)."""
+    """Batched draft-then-verify over decoding requests (reference speculative.py:89-261).
+
+    Lookahead (``lookahead = True``, the default): when a round's results
+    show that no request stops with them (budget and stop token checked
+    here), the next round's draft passes for the same requests are planned
+    and launched before ``step`` returns, so the caller's bookkeeping and the
+    next call's target-side planning run while the GPU drafts.  The next
+    ``step`` uses them only if its requests are the same, in the same order,
+    each with exactly the round's tokens appended (and the same sampling
+    settings, seeds and target cache state); otherwise the draft cache's
+    slots the lookahead took are given back and the round is planned from
+    scratch.  Draws are a function of (seed, round counter, lane), so the
+    token streams are the same either way.  The target cache, which the
+    scheduler's admission reads, is never touched ahead of time."""
 
     def __init__(
         self,
@@ -229,6 +266,10 @@ class SpeculativeDecoder:
         self.last_round_shape: dict[str, int] = {}
         self.last_h2d_bytes = 0
         self.last_d2h_bytes = 0
+        self.lookahead = True
+        self._pending: _Lookahead | None = None
+        self.lookahead_hits = 0
+        self.lookahead_misses = 0
 
     # -- one round ------------------------------------------------------------
     def step(
@@ -245,9 +286,25 @@ class SpeculativeDecoder:
         configs = list({id(r.sampling): r.sampling for r in requests}.values())
         for cfg in configs:
             validate(cfg)
-        plan = self._plan(requests, target_cache, generators, configs)
         launches0 = _lib.launch_count()
-        self._launch(plan, target_cache)
+        ahead, self._pending = self._pending, None
+        plan = None
+        if ahead is not None:
+            if self._lookahead_holds(ahead, requests, target_cache, generators):
+                plan, ev = ahead.plan, ahead.events
+                self.lookahead_hits += 1
+            else:
+                self._drop(ahead)
+                self.lookahead_misses += 1
+        if plan is None:
+            plan = self._plan(requests, target_cache, generators, configs)
+            ev = self._round_start_events()
+            self._launch_draft(plan)
+        try:
+            self._launch_verify(plan, target_cache, ev)
+        except OutOfCacheMemory:
+            self._drop_draft_slots(plan.ids, plan.d_cached)
+            raise
         self.last_round_launches = _lib.launch_count() - launches0
         buf = self._buf
         n_out = B * (G + 2)
@@ -256,7 +313,94 @@ class SpeculativeDecoder:
         res = buf.out_host[:n_out].numpy()
         tokens = res[: B * (G + 1)].reshape(B, G + 1)
         nacc = res[B * (G + 1) : B * (G + 2)].astype(np.int64)
-        return self._finish(requests, target_cache, plan, tokens, nacc)
+        results = self._finish(requests, target_cache, plan, tokens, nacc)
+        if self.lookahead:
+            self._pending = self._launch_ahead(requests, target_cache, generators, configs,
+                                               results)
+        return results
+
+    # -- lookahead -----------------------------------------------------------------
+    def _launch_ahead(self, requests: list[Request], target_cache: PagedKVCache,
+                      generators: dict[int, torch.Generator],
+                      configs: list[SamplingConfig] | None,
+                      results: list[list[int]]) -> _Lookahead | None:
+        """Plan and launch the next round's draft passes for the same requests,
+        assuming the caller appends every token of ``results`` -- unless some
+        request stops with them (its budget or its stop token), the pool has
+        no room, or the batch is not a plain decoding batch."""
+        for r, toks in zip(requests, results, strict=True):
+            if len(r.output_ids) + len(toks) >= r.sampling.max_new_tokens:
+                return None
+            stop = r.sampling.stop_token
+            if stop is not None and stop in toks:
+                return None
+        n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) + len(t)
+                             for r, t in zip(requests, results, strict=True)), np.int64,
+                            len(requests))
+
+        def tails(kmax: np.ndarray) -> np.ndarray:
+            # the next round's uncached tokens are all among this round's
+            out = []
+            for toks, k in zip(results, kmax.tolist(), strict=True):
+                if k > len(toks):
+                    raise _NotAhead
+                out.append(toks[len(toks) - k :])
+            return np.fromiter(itertools.chain.from_iterable(out), np.int32, int(kmax.sum()))
+
+        try:
+            plan = self._plan(requests, target_cache, generators, configs, n_tok=n_tok,
+                              tails_of=tails)
+        except (OutOfCacheMemory, _NotAhead):
+            return None
+        ev = self._round_start_events()
+        self._launch_draft(plan)
+        return _Lookahead(
+            plan=plan, ids=tuple(plan.ids), n_tok=n_tok,
+            last=[t[-1] for t in results], samplings=[r.sampling for r in requests],
+            seeds=[generators[i].initial_seed() for i in plan.ids], target_cache=target_cache,
+            t_cached=plan.t_cached.copy(), events=ev)
+
+    def _lookahead_holds(self, ahead: _Lookahead, requests: list[Request],
+                         target_cache: PagedKVCache,
+                         generators: dict[int, torch.Generator]) -> bool:
+        """Did the caller do what the lookahead assumed?"""
+        if target_cache is not ahead.target_cache or len(requests) != len(ahead.ids):
+            return False
+        for i, r in enumerate(requests):
+            if r.request_id != ahead.ids[i] or r.sampling is not ahead.samplings[i]:
+                return False
+            if len(r.prompt_ids) + len(r.output_ids) != ahead.n_tok[i]:
+                return False
+            last = r.output_ids[-1] if r.output_ids else r.prompt_ids[-1]
+            if last != ahead.last[i]:
+                return False
+            gen = generators.get(r.request_id)
+            if gen is None or gen.initial_seed() != ahead.seeds[i]:
+                return False
+        rows = target_cache.rows_if_all_present(list(ahead.ids))
+        if rows is None:
+            return False
+        return bool(np.array_equal(target_cache.num_tokens_many(list(ahead.ids), rows),
+                                   ahead.t_cached))
+
+    def _drop(self, ahead: _Lookahead) -> None:
+        """Give back the draft slots an unused lookahead reserved.  Its kernels
+        may still be in flight; they precede, on the stream, every later use
+        of those slots."""
+        self._drop_draft_slots(ahead.plan.ids, ahead.plan.d_cached)
+
+    def _drop_draft_slots(self, ids: list[int], d_cached: np.ndarray) -> None:
+        keep = [(s, int(n)) for s, n in zip(ids, d_cached.tolist(), strict=True)
+                if s in self.draft_cache.tables and self.draft_cache.num_tokens(s) >= n]
+        if keep:
+            self.draft_cache.truncate_many([s for s, _ in keep], [n for _, n in keep])
+
+    def _round_start_events(self) -> tuple[torch.cuda.Event, torch.cuda.Event] | None:
+        if self.round_events is None:
+            return None
+        ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+        ev[0].record()
+        return ev
 
     def _rows_for(self, ids: list[int], target_cache: PagedKVCache
                   ) -> tuple[np.ndarray | None, np.ndarray | None]:
@@ -285,12 +429,17 @@ class SpeculativeDecoder:
         target_cache: PagedKVCache,
         generators: dict[int, torch.Generator],
         configs: list[SamplingConfig] | None = None,
+        n_tok: np.ndarray | None = None,
+        tails_of: object = None,
     ) -> _RoundPlan:
         """What the draft passes need, packed into one blob (phase A).
 
         The round stays all-or-nothing: the target cache's room for the round
         is checked here, before the draft cache reserves anything, and its
         slots are taken in :meth:`_plan_verify` while the draft passes run.
+        ``n_tok`` and ``tails_of(k) -> the last k[b] tokens of every request``
+        describe the requests when they are not read from ``requests`` (the
+        lookahead plans for tokens not appended yet).
         """
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
@@ -299,7 +448,9 @@ class SpeculativeDecoder:
         trows, drows = self._rows_for(ids, target_cache)
         d_cached = dcache.num_tokens_many(ids, drows)
         t_cached = target_cache.num_tokens_many(ids, trows)
-        n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests), np.int64, B)
+        if n_tok is None:
+            n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests),
+                                np.int64, B)
         n0 = n_tok - d_cached
         npre = n_tok - t_cached
         if np.any(npre < 1):
@@ -310,8 +461,11 @@ class SpeculativeDecoder:
         # One walk over the token lists: the longer of the two suffixes, split
         # into the draft's catch-up tokens and the target's uncomputed ones.
         kmax = np.maximum(n0, npre)
-        tails = np.fromiter(itertools.chain.from_iterable(_tails(requests, kmax)), np.int32,
-                            int(kmax.sum()))
+        if tails_of is None:
+            tails = np.fromiter(itertools.chain.from_iterable(_tails(requests, kmax)), np.int32,
+                                int(kmax.sum()))
+        else:
+            tails = tails_of(kmax)
         tail_end = np.cumsum(kmax)
 
         # The draft's slots for the whole round (all-or-nothing).
@@ -425,7 +579,10 @@ class SpeculativeDecoder:
         plan.blob_v, plan.spans_v, plan.tw = blob, spans, tw
         plan.ctxv, plan.kv_verify = int(ctxv.max()), int(ctxv.sum())
 
-    def _launch(self, plan: _RoundPlan, target_cache: PagedKVCache) -> None:
+    def _launch_draft(self, plan: _RoundPlan) -> None:
+        """Upload phase A, launch draft pass 0, plan the rest of the draft side
+        while it runs, then the later passes and every pass's draw (which
+        writes the proposal into the next pass and into the verify batch)."""
         G, V = self.gamma, self.target.cfg.vocab_size
         B = plan.B
         self._buf.round_views(B, G, V)
@@ -438,10 +595,6 @@ class SpeculativeDecoder:
         dtab = b0.block_tables
         o, n = spans[7]
         rows0 = dev_blob[o : o + n]
-        ev = None
-        if self.round_events is not None:
-            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            ev[0].record()
         self.draft.forward_paged(b0, self.draft_cache, logit_rows=rows0, out=buf.dlogits[0],
                                  out_row_stride=V)
         # The rest of the draft side is planned while draft pass 0 runs.
@@ -463,7 +616,6 @@ class SpeculativeDecoder:
         idsv = w[k]
         k += 1
         scat = w[k : k + G]
-
         for j, bj in enumerate(batches):
             out = buf.dlogits[j]
             if bj is not None:
@@ -473,14 +625,23 @@ class SpeculativeDecoder:
                 buf.proposals[j].data_ptr(), None, buf.dstats[j].data_ptr(),
                 idsv.data_ptr(), scat[j].data_ptr(), stream,
             )
-        # The target side is planned while the draft passes run on the GPU.
+        plan.dev_params, plan.dev_idsv = params, idsv
+
+    def _launch_verify(self, plan: _RoundPlan, target_cache: PagedKVCache,
+                       ev: tuple[torch.cuda.Event, torch.cuda.Event] | None) -> None:
+        """Plan the target side (its slots are taken here), then the verify pass
+        and the fused accept kernel."""
+        G, V = self.gamma, self.target.cfg.vocab_size
+        B = plan.B
+        buf = self._buf
+        stream = _lib.stream_ptr(self.device)
         self._plan_verify(plan, target_cache)
         vblob = self._staging_v.upload(plan.blob_v)
         w = [vblob[o : o + n] for o, n in plan.spans_v]
         tw = plan.tw
         bv = PagedBatch(
-            input_ids=idsv, positions=w[0], slot_mapping=w[1], q_start=w[2], context_lens=w[3],
-            q_lens=w[4], block_tables=w[5].view(B, tw), max_q=plan.max_qv,
+            input_ids=plan.dev_idsv, positions=w[0], slot_mapping=w[1], q_start=w[2],
+            context_lens=w[3], q_lens=w[4], block_tables=w[5].view(B, tw), max_q=plan.max_qv,
             n_tokens=plan.Tv, max_context=plan.ctxv,
         )
         rowsv = w[6]
@@ -502,8 +663,8 @@ class SpeculativeDecoder:
             self.verify_events.append(vev)
         _lib.call(
             "ms_spec_accept", buf.vlogits.data_ptr(), V, buf.dlogits.data_ptr(), V,
-            buf.dstats.data_ptr(), 0, buf.proposals.data_ptr(), params.data_ptr(), B, G, V,
-            buf.out.data_ptr(), buf.out[B * (G + 1) :].data_ptr(), stream,
+            buf.dstats.data_ptr(), 0, buf.proposals.data_ptr(), plan.dev_params.data_ptr(), B,
+            G, V, buf.out.data_ptr(), buf.out[B * (G + 1) :].data_ptr(), stream,
         )
         if ev is not None and self.round_events is not None:
             ev[1].record()
@@ -544,6 +705,7 @@ class SpeculativeDecoder:
         self.draft_cache.free(seq_id)
 
     def reset(self) -> None:
+        self._pending = None
         self._row_cache = None
         self.draft_cache.reset()
         self.num_proposed = 0

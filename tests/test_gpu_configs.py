@@ -430,3 +430,32 @@ def test_sampling_filters_at_128256_are_not_degenerate() -> None:
     rng = np.random.default_rng(0)
     row = filter_row((rng.standard_normal(128256) * 2).astype(np.float32), 0.8, None, 0.9)
     assert (row.e > 0).sum() > 100
+
+
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_chunked_prefill_keeps_the_streams(temperature: float) -> None:
+    """Config-0 models and workload with SchedulerConfig.prefill_chunk = 24:
+    prompts of 8-256 tokens are prefilled over several engine steps, mixed
+    with other requests' decode steps; every request's tokens equal those of
+    the unchunked engine (greedy and sampled: a request draws only when its
+    prompt is complete, on the same round counter)."""
+    from microserve_b200.config import (CacheConfig, EngineConfig, SamplingConfig,
+                                        SchedulerConfig, SpeculativeConfig)
+    from microserve_b200.engine import LLMEngine
+
+    target, draft, _, _ = _char_models(20.0)
+    w = _wl().config0()
+    outs = []
+    for chunk in (None, 24):
+        cfg = EngineConfig(model=target.cfg, cache=CacheConfig(block_size=16, num_blocks=256),
+                           scheduler=SchedulerConfig(max_batch_size=8, max_batched_tokens=96,
+                                                     prefill_chunk=chunk),
+                           speculative=SpeculativeConfig(enabled=True, gamma=3))
+        eng = LLMEngine(target, cfg, draft_model=draft)
+        sc = SamplingConfig(temperature=temperature, max_new_tokens=20)
+        reqs = [eng.add_request(p, sc) for p in w.prompts]
+        done = {o.request_id: o.output_ids for o in eng.run()}
+        outs.append([done[r.request_id] for r in reqs])
+        if chunk is not None:
+            assert eng.stats.num_steps > 8  # the prompts really took several steps
+    assert outs[0] == outs[1]

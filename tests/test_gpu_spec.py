@@ -186,3 +186,43 @@ def test_streams_do_not_depend_on_how_requests_are_sharded(golden) -> None:
     for rank in range(2):
         two.update(serve(distributed.shard_requests([float(len(p)) for p in prompts], 2, rank)))
     assert two == one
+
+
+def test_lookahead_keeps_the_streams_and_gives_back_its_slots(golden) -> None:
+    """The next round's draft passes launched ahead of the caller (lookahead)
+    change nothing observable: streams equal a decoder without it, also when
+    the caller's next call differs from what the lookahead assumed (a request
+    dropped, a request added); the draft pool is whole again after free()."""
+    from microserve_b200.cache import PagedKVCache
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.scheduler import Request
+    from microserve_b200.speculative import SpeculativeDecoder
+
+    target, draft = device_model(golden, "target"), device_model(golden, "draft")
+    rng = np.random.default_rng(21)
+    prompts = [rng.integers(0, 32, int(n)).tolist() for n in rng.integers(2, 20, 6)]
+    sc = SamplingConfig(temperature=0.9, top_k=20, max_new_tokens=200)
+    # call pattern: the batch changes at calls 3 (request 5 leaves) and 5 (it returns)
+    batches = [[0, 1, 2, 3, 4, 5]] * 3 + [[0, 1, 2, 3, 4]] * 2 + [[0, 1, 2, 3, 4, 5]] * 3
+
+    def serve(lookahead: bool):
+        dec = SpeculativeDecoder(target, draft, _cache_cfg(8, 128), gamma=3)
+        dec.lookahead = lookahead
+        cache = PagedKVCache(target.cfg, _cache_cfg(8, 128), DEV)
+        reqs = [Request(i, list(p), sc) for i, p in enumerate(prompts)]
+        gens = {i: torch.Generator().manual_seed(900 + i) for i in range(len(prompts))}
+        for ids in batches:
+            for i, toks in zip(ids, dec.step([reqs[i] for i in ids], cache, gens), strict=True):
+                reqs[i].output_ids.extend(toks)
+        outs = [r.output_ids for r in reqs]
+        for i in range(len(prompts)):
+            cache.free(i)
+            dec.free(i)
+        assert dec.draft_cache.num_free_blocks == dec.draft_cache.cfg.num_blocks
+        assert cache.num_free_blocks == cache.cfg.num_blocks
+        return outs, dec
+
+    plain, _ = serve(False)
+    ahead, dec = serve(True)
+    assert ahead == plain
+    assert dec.lookahead_hits >= 4 and dec.lookahead_misses >= 2

@@ -626,3 +626,24 @@ def test_scheduler_decisions_match_the_reference(case: int) -> None:
         steps = int(z[f"sched/{case}/steps"])
     assert len(trace) == steps
     assert [x for rec in trace for x in rec] == want
+
+
+def test_chunked_prefill_charges_only_the_next_chunk() -> None:
+    """With prefill_chunk the token budget and the block demand count the
+    chunk a prefilling request processes next, not its whole prompt."""
+    cache = host_cache(block_size=4, num_blocks=64)
+    s = Scheduler(SchedulerConfig(max_batch_size=8, max_batched_tokens=40, prefill_chunk=16),
+                  cache)
+    for i in range(4):
+        s.add(Request(i, [1] * 30, SamplingConfig()))
+    out = s.schedule(0.0)
+    # 16 + 16 fit the 40-token budget, a third chunk does not
+    assert [r.request_id for r in out.scheduled] == [0, 1]
+    assert [s.step_len(r) for r in out.scheduled] == [16, 16]
+    plain = Scheduler(SchedulerConfig(max_batch_size=8, max_batched_tokens=40),
+                      host_cache(block_size=4, num_blocks=64))
+    for i in range(4):
+        plain.add(Request(i, [1] * 30, SamplingConfig()))
+    assert [r.request_id for r in plain.schedule(0.0).scheduled] == [0]
+    with pytest.raises(ValueError):
+        SchedulerConfig(prefill_chunk=0)
