@@ -171,3 +171,28 @@ def test_kat_fixture_holds_the_published_acceptance() -> None:
         assert float(kat[f"spec{g}/published_acceptance"]) == rate
         for i in range(8):
             assert kat[f"spec{g}/{i}"].tolist() == kat["dense"][i].tolist()
+
+
+def test_oracle_reproduces_the_trained_weight_known_answer() -> None:
+    """The oracle's greedy speculative rounds on the reference's trained
+    checkpoints reproduce the reference's run for the published prompt (the
+    last of the eight) at gamma 4: the same 48 tokens and the same accepted
+    and proposed counts (artifacts/spec_stats.json:20-26 publishes
+    0.4558824 for it)."""
+    kat = np.load(ROOT / "tests" / "golden" / "kat_fixtures.npz")
+
+    def model(which: str) -> OracleModel:
+        v, L, d, h, hkv, ff, msl = (int(x) for x in kat[f"{which}_cfg"])
+        pre = which + "/"
+        st = {k[len(pre):]: kat[k] for k in kat.files if k.startswith(pre)}
+        return OracleModel(Dims(v, d, L, h, hkv, ff, msl), st)
+
+    target, draft = model("target"), model("draft")
+    prompt = kat["prompts"][7].tolist()
+    req = OracleRequest(0, prompt, 0.0, None, None, seed=0)
+    while len(req.output_ids) < 48:
+        tr = spec_round(target, draft, 4, [req])
+        req.output_ids.extend(tr.emitted[0][: 48 - len(req.output_ids)])
+    assert req.output_ids == kat["spec4/7"].tolist()
+    assert [req.num_accepted, req.num_proposed] == kat["spec4/counts"][7].tolist()
+    assert req.num_accepted / req.num_proposed == pytest.approx(0.45588235294117646, abs=1e-12)
