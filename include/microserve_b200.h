@@ -128,6 +128,34 @@ MS_API int ms_spec_accept(const float* target_logits, int64_t target_stride,
                    int n_requests, int gamma, int vocab, int32_t* out_tokens,
                    int32_t* out_num_accepted, void* stream);
 
+/* The draft side of the next speculative round, planned on the device from
+ * this round's results, so the next round's draft passes can start before
+ * the host reads them: build_paged_batch + PagedKVCache.append for the
+ * draft cache (reference batching.py:19-63, cache.py:159-171) after the
+ * rollback of SpeculativeDecoder._rollback (speculative.py:213-226).
+ * Inputs per request b: out_tokens (B x (gamma+1)) and num_accepted (B)
+ * from ms_spec_accept; n_tok[b], its token count before this round;
+ * last_tok[b], its last token before this round; draft_tables (B x
+ * table_width block ids) covering n_tok[b] + 2*gamma tokens; params_in
+ * (B).  Output: `chain` (ms_spec_chain_size ints), laid out as
+ *   ids0[2B] pos0[2B] slots0[2B] q_start0[B+1] ctx0[B] q_lens0[B] rows0[B]
+ *   pos[(gamma-1)B] slots[(gamma-1)B] ctx[(gamma-1)B] q_start1[B+1] ones[B]
+ *   verify_ids[B(gamma+1)]:
+ * draft pass 0 takes each request's last two tokens (2B rows, logits from
+ * row 2b+1; the first row's K/V goes to a spare reserved slot when it is
+ * already cached), pass j >= 1 one token per request at pos[(j-1)B+b];
+ * verify_ids[b(gamma+1)] is the next verify pass's first token (the
+ * proposals are scattered after it).  params_out = params_in with step + 1
+ * (may alias params_in).  Slots outside the tables set the device error
+ * word and are written as -1. */
+MS_API int64_t ms_spec_chain_size(int n_requests, int gamma);
+MS_API int ms_spec_chain_plan(const int32_t* out_tokens, const int32_t* num_accepted,
+                              const int32_t* n_tok, const int32_t* last_tok,
+                              const int32_t* draft_tables, int table_width, int block_size,
+                              int num_blocks, const ms_sampling_params* params_in,
+                              int n_requests, int gamma, int32_t* chain,
+                              ms_sampling_params* params_out, void* stream);
+
 /* verify_proposals on probability rows (reference speculative.py:44-86)
  * with explicit uniforms: accept_u (gamma x B, position-major), draw_u (B).
  * Target rows b*(gamma+1)+i; draft rows and proposals at i*B+b. */

@@ -128,6 +128,12 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int,
          c_int, c_void_p, c_void_p, c_void_p],
     ),
+    "ms_spec_chain_size": (c_int64, [c_int, c_int]),
+    "ms_spec_chain_plan": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int,
+         c_int, c_void_p, c_void_p, c_void_p],
+    ),
     "ms_verify_probs": (
         c_int,
         [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p,

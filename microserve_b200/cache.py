@@ -472,15 +472,46 @@ class PagedKVCache:
             raise KeyError(seq_id)
         self.truncate_many([seq_id], [num_tokens])
 
+    def reserve_many(self, seq_ids: Sequence[int], capacity: Sequence[int] | np.ndarray,
+                     rows: np.ndarray | None = None) -> bool:
+        """Give every sequence blocks for ``capacity[i]`` tokens without
+        changing its token count (later appends within it take no block).
+        All-or-nothing: False, and no change, if the pool is short."""
+        if rows is None:
+            rows = self._existing_rows(seq_ids)
+        rows = np.ascontiguousarray(rows, dtype=np.int64)
+        cap = np.ascontiguousarray(capacity, dtype=np.int64)
+        have = self._nblk[rows].astype(np.int64)
+        need = np.maximum(0, (cap + self.block_size - 1) // self.block_size - have)
+        total = int(need.sum())
+        if total == 0:
+            return True
+        if total > self.allocator.num_free:
+            return False
+        self._ensure_columns(int((have + need).max()))
+        blocks = np.asarray(self.allocator.allocate_many(total), dtype=np.int32)
+        first = np.repeat(np.cumsum(need) - need, need)
+        cols = np.repeat(have, need) + (np.arange(total) - first)
+        self._table[np.repeat(rows, need), cols] = blocks
+        self._nblk[rows] = (have + need).astype(np.int32)
+        return True
+
     def truncate_many(self, seq_ids: Sequence[int], num_tokens: Sequence[int] | np.ndarray,
-                      rows: np.ndarray | None = None) -> None:
-        """Vectorised ``truncate`` (speculative rollback, reference cache.py:210-222)."""
+                      rows: np.ndarray | None = None, keep_blocks: bool = False) -> None:
+        """Vectorised ``truncate`` (speculative rollback, reference cache.py:210-222).
+        ``keep_blocks``: only the token counts shrink; the blocks past the
+        new ends stay with their sequences as reserved capacity."""
         if rows is None:
             rows = self._existing_rows(seq_ids)
         rows = np.ascontiguousarray(rows, dtype=np.int64)
         n = np.ascontiguousarray(num_tokens, dtype=np.int64)
         if n.shape != rows.shape:
             raise ValueError("truncate_many: one token count per sequence")
+        if keep_blocks:
+            if np.any(n > self._ntok[rows]) or np.any(n < 0):
+                raise ValueError("truncate cannot grow a sequence")
+            self._ntok[rows] = n
+            return
         lib = _lib.load()
         for _ in range(2):
             freed = self._freed

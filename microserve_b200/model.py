@@ -329,7 +329,9 @@ class Transformer:
             # would mean "every row")
             logit_rows = self._no_rows()
         if out is None:
-            out = torch.empty((n_rows, self.cfg.vocab_size), dtype=torch.float32, device=self.device)
+            # (at least one row, so the pointer is never null when no logits are wanted)
+            out = torch.empty((max(n_rows, 1), self.cfg.vocab_size), dtype=torch.float32,
+                              device=self.device)[:n_rows]
             out_row_stride = 0
         cb = batch.c_struct()
         cc = cache.c_struct()

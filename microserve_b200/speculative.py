@@ -141,11 +141,6 @@ def _empty(dtype: type = np.int64) -> np.ndarray:
     return np.zeros(0, dtype)
 
 
-class _NotAhead(Exception):
-    """The lookahead cannot plan this batch ahead (a request's uncached
-    tokens are not all among the round's new tokens)."""
-
-
 @dataclass
 class _RoundPlan:
     """What a round's three host phases compute.  :meth:`SpeculativeDecoder._plan`
@@ -196,39 +191,57 @@ class _RoundPlan:
     # device views the verify side reads: sampling parameters, verify token ids
     dev_params: torch.Tensor | None = None
     dev_idsv: torch.Tensor | None = None
+    # the next round's chain: inputs appended to the verify blob (n_tok,
+    # last token, draft tables covering n_tok + 2 gamma tokens)
+    chain_reserved: bool = False
+    chain_span: int = -1
+    chain_dw: int = 0
+    dev_blob_v: torch.Tensor | None = None
+    target_cache: PagedKVCache | None = None
 
 
 @dataclass
 class _Lookahead:
-    """The draft side of the next round, launched as soon as a round's results
-    were read: what it assumed about the caller's next ``step`` call."""
+    """The next round's draft passes, launched on the device right after a
+    round's accept kernel (planned there by ``ms_spec_chain_plan``), and what
+    they assumed about the caller's next ``step`` call."""
 
-    plan: _RoundPlan
     ids: tuple[int, ...]
-    n_tok: np.ndarray  # every request's token count once this round's tokens are appended
-    last: list[int]  # every request's last token then
+    requests: list[Request]
+    gens: list[torch.Generator]
+    configs: list[SamplingConfig] | None
     samplings: list[SamplingConfig]
     seeds: list[int]
     target_cache: PagedKVCache
-    t_cached: np.ndarray  # the target cache's token counts it planned on
+    max_ctx: int  # an upper bound of the next round's draft contexts
+    params: torch.Tensor  # the next round's sampling parameters (device)
+    idsv: torch.Tensor  # the next round's verify token ids (device)
     events: tuple[torch.cuda.Event, torch.cuda.Event] | None
+    # filled once the round's results are read
+    n_tok: np.ndarray = field(default_factory=_empty)  # token counts with the round's tokens
+    last: list[int] = field(default_factory=list)  # last tokens then
+    t_cached: np.ndarray = field(default_factory=_empty)  # target counts after the rollback
 
 
 class SpeculativeDecoder:
     """Batched draft-then-verify over decoding requests (reference speculative.py:89-261).
 
-    Lookahead (``lookahead = True``, the default): when a round's results
-    show that no request stops with them (budget and stop token checked
-    here), the next round's draft passes for the same requests are planned
-    and launched before ``step`` returns, so the caller's bookkeeping and the
-    next call's target-side planning run while the GPU drafts.  The next
-    ``step`` uses them only if its requests are the same, in the same order,
-    each with exactly the round's tokens appended (and the same sampling
-    settings, seeds and target cache state); otherwise the draft cache's
-    slots the lookahead took are given back and the round is planned from
-    scratch.  Draws are a function of (seed, round counter, lane), so the
-    token streams are the same either way.  The target cache, which the
-    scheduler's admission reads, is never touched ahead of time."""
+    Lookahead (``lookahead = True``, the default): when no request can stop
+    in a round (its budget exceeds the round's gamma + 1 tokens, no stop
+    token), the next round's draft side is planned on the device from the
+    accepted counts (``ms_spec_chain_plan``) and its draft passes are
+    launched right after the accept kernel, before the host reads the
+    results: while they run, the host reads this round's tokens, rolls the
+    caches back, returns, and the caller's next ``step`` plans and launches
+    the verify pass, so the GPU does not wait for the host between rounds.
+    The draft cache reserves the blocks those passes write (its token count
+    moves only when the host confirms them).  The next ``step`` uses the
+    passes only if its requests are the same, in the same order, each with
+    exactly the round's tokens appended (and the same sampling settings,
+    seeds and target cache state); otherwise they are ignored and the round
+    is planned on the host.  Draws are a function of (seed, round counter,
+    lane), so the token streams are the same either way.  The target cache,
+    which the scheduler's admission reads, is never touched ahead of time."""
 
     def __init__(
         self,
@@ -268,6 +281,8 @@ class SpeculativeDecoder:
         self.last_d2h_bytes = 0
         self.lookahead = True
         self._pending: _Lookahead | None = None
+        self._scat: torch.Tensor | None = None
+        self._scat_key: tuple[int, int] | None = None
         self.lookahead_hits = 0
         self.lookahead_misses = 0
 
@@ -291,74 +306,151 @@ class SpeculativeDecoder:
         plan = None
         if ahead is not None:
             if self._lookahead_holds(ahead, requests, target_cache, generators):
-                plan, ev = ahead.plan, ahead.events
+                plan, ev = self._chained_plan(ahead, target_cache), ahead.events
                 self.lookahead_hits += 1
             else:
-                self._drop(ahead)
                 self.lookahead_misses += 1
         if plan is None:
             plan = self._plan(requests, target_cache, generators, configs)
             ev = self._round_start_events()
             self._launch_draft(plan)
+        chain = self.lookahead and self._no_request_can_stop(requests)
         try:
-            self._launch_verify(plan, target_cache, ev)
+            self._launch_verify(plan, target_cache, ev, chain)
         except OutOfCacheMemory:
             self._drop_draft_slots(plan.ids, plan.d_cached)
             raise
-        self.last_round_launches = _lib.launch_count() - launches0
         buf = self._buf
         n_out = B * (G + 2)
         buf.out_host[:n_out].copy_(buf.out[:n_out], non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        copied = torch.cuda.Event()
+        copied.record(torch.cuda.current_stream(self.device))
+        if plan.chain_reserved:
+            self._pending = self._launch_chain(plan)
+        self.last_round_launches = _lib.launch_count() - launches0
+        copied.synchronize()
         res = buf.out_host[:n_out].numpy()
         tokens = res[: B * (G + 1)].reshape(B, G + 1)
         nacc = res[B * (G + 1) : B * (G + 2)].astype(np.int64)
         results = self._finish(requests, target_cache, plan, tokens, nacc)
-        if self.lookahead:
-            self._pending = self._launch_ahead(requests, target_cache, generators, configs,
-                                               results)
+        if self._pending is not None:
+            la = self._pending
+            la.n_tok = plan.n_tok + nacc + 1
+            la.last = [row[-1] for row in results]
+            la.t_cached = plan.n_tok + nacc
         return results
 
     # -- lookahead -----------------------------------------------------------------
-    def _launch_ahead(self, requests: list[Request], target_cache: PagedKVCache,
-                      generators: dict[int, torch.Generator],
-                      configs: list[SamplingConfig] | None,
-                      results: list[list[int]]) -> _Lookahead | None:
-        """Plan and launch the next round's draft passes for the same requests,
-        assuming the caller appends every token of ``results`` -- unless some
-        request stops with them (its budget or its stop token), the pool has
-        no room, or the batch is not a plain decoding batch."""
-        for r, toks in zip(requests, results, strict=True):
-            if len(r.output_ids) + len(toks) >= r.sampling.max_new_tokens:
-                return None
-            stop = r.sampling.stop_token
-            if stop is not None and stop in toks:
-                return None
-        n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) + len(t)
-                             for r, t in zip(requests, results, strict=True)), np.int64,
-                            len(requests))
+    def _no_request_can_stop(self, requests: list[Request]) -> bool:
+        """No request can finish with this round's tokens (at most gamma + 1)."""
+        room = self.gamma + 1
+        return all(r.sampling.stop_token is None
+                   and len(r.output_ids) + room < r.sampling.max_new_tokens for r in requests)
 
-        def tails(kmax: np.ndarray) -> np.ndarray:
-            # the next round's uncached tokens are all among this round's
-            out = []
-            for toks, k in zip(results, kmax.tolist(), strict=True):
-                if k > len(toks):
-                    raise _NotAhead
-                out.append(toks[len(toks) - k :])
-            return np.fromiter(itertools.chain.from_iterable(out), np.int32, int(kmax.sum()))
-
-        try:
-            plan = self._plan(requests, target_cache, generators, configs, n_tok=n_tok,
-                              tails_of=tails)
-        except (OutOfCacheMemory, _NotAhead):
-            return None
+    def _launch_chain(self, plan: _RoundPlan) -> _Lookahead:
+        """Plan the next round's draft side on the device from this round's
+        accepted counts and launch its draft passes (same requests)."""
+        G, V = self.gamma, self.target.cfg.vocab_size
+        B = plan.B
+        buf = self._buf
+        stream = _lib.stream_ptr(self.device)
         ev = self._round_start_events()
-        self._launch_draft(plan)
+        chain, params, scat = self._chain_buffers(B)
+        o, n = plan.spans_v[plan.chain_span]
+        cin = plan.dev_blob_v[o : o + n]
+        n_tok, last, dtab = cin[:B], cin[B : 2 * B], cin[2 * B :]
+        dc = self.draft_cache
+        _lib.call("ms_spec_chain_plan", buf.out.data_ptr(), buf.out[B * (G + 1):].data_ptr(),
+                  n_tok.data_ptr(), last.data_ptr(), dtab.data_ptr(), plan.chain_dw, dc.block_size,
+                  dc.cfg.num_blocks, plan.dev_params.data_ptr(), B, G, chain.data_ptr(),
+                  params.data_ptr(), stream)
+        off = 0
+
+        def take(k: int) -> torch.Tensor:
+            nonlocal off
+            v = chain[off : off + k]
+            off += k
+            return v
+
+        ids0, pos0, slots0 = take(2 * B), take(2 * B), take(2 * B)
+        qs0, ctx0, ql0, rows0 = take(B + 1), take(B), take(B), take(B)
+        pos, slots, ctx = take((G - 1) * B), take((G - 1) * B), take((G - 1) * B)
+        unit_qs, ones, idsv = take(B + 1), take(B), take((G + 1) * B)
+        tables = dtab.view(B, plan.chain_dw)
+        max_ctx = int(plan.n_tok.max()) + G + 1
+        b0 = PagedBatch(input_ids=ids0, positions=pos0, slot_mapping=slots0, q_start=qs0,
+                        context_lens=ctx0, q_lens=ql0, block_tables=tables, max_q=2,
+                        n_tokens=2 * B, max_context=max_ctx)
+        self.draft.forward_paged(b0, dc, logit_rows=rows0, out=buf.dlogits[0], out_row_stride=V)
+        for j in range(G):
+            out = buf.dlogits[j]
+            if j:
+                bj = PagedBatch(input_ids=buf.proposals[j - 1], positions=pos[(j - 1) * B : j * B],
+                                slot_mapping=slots[(j - 1) * B : j * B], block_tables=tables,
+                                context_lens=ctx[(j - 1) * B : j * B], q_lens=ones,
+                                q_start=unit_qs, max_q=1, n_tokens=B, max_context=max_ctx + j)
+                self.draft.forward_paged(bj, dc, out=out, out_row_stride=V)
+            _lib.call("ms_sample", out.data_ptr(), V, B, V, params.data_ptr(), None,
+                      _lib.LANE_DRAFT + j, buf.proposals[j].data_ptr(), None,
+                      buf.dstats[j].data_ptr(), idsv.data_ptr(), scat[j].data_ptr(), stream)
         return _Lookahead(
-            plan=plan, ids=tuple(plan.ids), n_tok=n_tok,
-            last=[t[-1] for t in results], samplings=[r.sampling for r in requests],
-            seeds=[generators[i].initial_seed() for i in plan.ids], target_cache=target_cache,
-            t_cached=plan.t_cached.copy(), events=ev)
+            ids=tuple(plan.ids), requests=plan.requests, gens=plan.gens, configs=plan.configs,
+            samplings=[r.sampling for r in plan.requests],
+            seeds=[g.initial_seed() for g in plan.gens], target_cache=plan.target_cache,
+            max_ctx=max_ctx, params=params, idsv=idsv, events=ev)
+
+    def _chain_buffers(self, B: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """Device buffers of the chained round: its metadata, its sampling
+        parameters, and where each draft pass's proposals go in the verify
+        ids (constant: request b's verify rows start at b * (gamma + 1))."""
+        G = self.gamma
+        n = int(_lib.load().ms_spec_chain_size(B, G))
+        chain = self._buf.get("chain", n, torch.int32)
+        params = self._buf.get("chain_params", B * _lib.SAMPLING_PARAMS_DTYPE.itemsize,
+                               torch.uint8)
+        key = (B, G)
+        if self._scat_key != key:
+            idx = (np.arange(B)[None, :] * (G + 1) + 1 + np.arange(G)[:, None]).astype(np.int32)
+            self._scat = torch.from_numpy(idx).to(self.device)
+            self._scat_key = key
+        return chain, params, self._scat
+
+    def _chained_plan(self, ahead: _Lookahead, target_cache: PagedKVCache) -> _RoundPlan:
+        """The host's side of a round whose draft passes ran ahead: the draft
+        cache takes the tokens those passes wrote (inside the reserved
+        blocks, so the slots are the ones the device used), and the verify
+        batch is laid out as the device did (one uncached token per request,
+        then the proposals)."""
+        G = self.gamma
+        ids = list(ahead.ids)
+        B = len(ids)
+        trows, drows = self._rows_for(ids, target_cache)
+        dc = self.draft_cache
+        d_cached = dc.num_tokens_many(ids, drows)
+        n_tok = ahead.n_tok
+        grow = n_tok + G - 1 - d_cached
+        if dc.blocks_needed_many(ids, grow, drows) != 0:
+            raise RuntimeError("lookahead: the draft passes ran outside the reserved blocks")
+        dc.append_many(ids, grow, drows)
+        t_cached = target_cache.num_tokens_many(ids, trows)
+        npre = n_tok - t_cached
+        qv = np.arange(B + 1, dtype=np.int64) * (G + 1)
+        segv = np.repeat(np.arange(B), G + 1)
+        withinv = np.tile(np.arange(G + 1), B)
+        n0 = n_tok - d_cached
+        empty = _empty(np.int32)
+        plan = _RoundPlan(
+            blob=empty, spans=[], B=B, dw=0, T0=2 * B, max_q0=2, ctx0=ahead.max_ctx,
+            kv_draft0=int(n_tok.sum()), ids=ids, requests=ahead.requests, gens=ahead.gens,
+            configs=ahead.configs, n_tok=n_tok, n0=n0, npre=npre, d_cached=d_cached,
+            t_cached=t_cached, trows=trows, drows=drows, dslots=_empty(), dstart=_empty(),
+            tails=empty, tail_end=_empty(),
+        )
+        plan.Tv, plan.max_qv = B * (G + 1), G + 1
+        plan.qv, plan.segv, plan.withinv = qv, segv, withinv
+        plan.kv_draft = int(n_tok.sum()) * G + B * (G - 1) * G // 2
+        plan.dev_params, plan.dev_idsv = ahead.params, ahead.idsv
+        return plan
 
     def _lookahead_holds(self, ahead: _Lookahead, requests: list[Request],
                          target_cache: PagedKVCache,
@@ -378,18 +470,14 @@ class SpeculativeDecoder:
             if gen is None or gen.initial_seed() != ahead.seeds[i]:
                 return False
         rows = target_cache.rows_if_all_present(list(ahead.ids))
-        if rows is None:
+        drows = self.draft_cache.rows_if_all_present(list(ahead.ids))
+        if rows is None or drows is None:
             return False
         return bool(np.array_equal(target_cache.num_tokens_many(list(ahead.ids), rows),
                                    ahead.t_cached))
 
-    def _drop(self, ahead: _Lookahead) -> None:
-        """Give back the draft slots an unused lookahead reserved.  Its kernels
-        may still be in flight; they precede, on the stream, every later use
-        of those slots."""
-        self._drop_draft_slots(ahead.plan.ids, ahead.plan.d_cached)
-
     def _drop_draft_slots(self, ids: list[int], d_cached: np.ndarray) -> None:
+        """Give back the draft slots a round took before it failed."""
         keep = [(s, int(n)) for s, n in zip(ids, d_cached.tolist(), strict=True)
                 if s in self.draft_cache.tables and self.draft_cache.num_tokens(s) >= n]
         if keep:
@@ -429,17 +517,12 @@ class SpeculativeDecoder:
         target_cache: PagedKVCache,
         generators: dict[int, torch.Generator],
         configs: list[SamplingConfig] | None = None,
-        n_tok: np.ndarray | None = None,
-        tails_of: object = None,
     ) -> _RoundPlan:
         """What the draft passes need, packed into one blob (phase A).
 
         The round stays all-or-nothing: the target cache's room for the round
         is checked here, before the draft cache reserves anything, and its
         slots are taken in :meth:`_plan_verify` while the draft passes run.
-        ``n_tok`` and ``tails_of(k) -> the last k[b] tokens of every request``
-        describe the requests when they are not read from ``requests`` (the
-        lookahead plans for tokens not appended yet).
         """
         G, B = self.gamma, len(requests)
         ids = [r.request_id for r in requests]
@@ -448,9 +531,8 @@ class SpeculativeDecoder:
         trows, drows = self._rows_for(ids, target_cache)
         d_cached = dcache.num_tokens_many(ids, drows)
         t_cached = target_cache.num_tokens_many(ids, trows)
-        if n_tok is None:
-            n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests),
-                                np.int64, B)
+        n_tok = np.fromiter((len(r.prompt_ids) + len(r.output_ids) for r in requests),
+                            np.int64, B)
         n0 = n_tok - d_cached
         npre = n_tok - t_cached
         if np.any(npre < 1):
@@ -461,11 +543,8 @@ class SpeculativeDecoder:
         # One walk over the token lists: the longer of the two suffixes, split
         # into the draft's catch-up tokens and the target's uncomputed ones.
         kmax = np.maximum(n0, npre)
-        if tails_of is None:
-            tails = np.fromiter(itertools.chain.from_iterable(_tails(requests, kmax)), np.int32,
-                                int(kmax.sum()))
-        else:
-            tails = tails_of(kmax)
+        tails = np.fromiter(itertools.chain.from_iterable(_tails(requests, kmax)), np.int32,
+                            int(kmax.sum()))
         tail_end = np.cumsum(kmax)
 
         # The draft's slots for the whole round (all-or-nothing).
@@ -557,10 +636,13 @@ class SpeculativeDecoder:
         plan.qv, plan.segv, plan.withinv = qv, segv, withinv
         plan.kv_draft = plan.kv_draft0 + sum(int(c.sum()) for c in ctx_j)
 
-    def _plan_verify(self, plan: _RoundPlan, target_cache: PagedKVCache) -> None:
+    def _plan_verify(self, plan: _RoundPlan, target_cache: PagedKVCache,
+                     chain: bool = False) -> None:
         """Phase B, run on the host while the draft passes execute: the target
         cache's slots (room checked in :meth:`_plan`) and the verify batch's
-        metadata, packed into a third blob."""
+        metadata, packed into a third blob.  With ``chain``, the draft cache
+        reserves blocks for every request's next round (n_tok + 2 gamma
+        tokens) and the blob carries what ``ms_spec_chain_plan`` reads."""
         G = self.gamma
         ids = plan.ids
         npre = plan.npre
@@ -575,9 +657,23 @@ class SpeculativeDecoder:
         ctxv = t_cached + npre + G
         rowsv = (qv[1:, None] - (G + 1) + np.arange(G + 1)[None, :]).reshape(-1)
         parts = [posv, tslots, qv, ctxv, npre + G, ttab, rowsv]
+        plan.target_cache = target_cache
+        plan.chain_reserved = chain and self.draft_cache.reserve_many(
+            ids, plan.n_tok + 2 * G, plan.drows)
+        if plan.chain_reserved:
+            dtab, _, dw = self.draft_cache.table_rows(ids, plan.drows)
+            last = plan.tails[plan.tail_end - 1] if plan.tails.size else self._last_tokens(plan)
+            parts.append(np.concatenate([plan.n_tok.astype(np.int32), last.astype(np.int32),
+                                         dtab.reshape(-1)]))
+            plan.chain_span, plan.chain_dw = len(parts) - 1, dw
         blob, spans = pack_int32([np.ascontiguousarray(p).astype(np.int32, copy=False) for p in parts])
         plan.blob_v, plan.spans_v, plan.tw = blob, spans, tw
         plan.ctxv, plan.kv_verify = int(ctxv.max()), int(ctxv.sum())
+
+    def _last_tokens(self, plan: _RoundPlan) -> np.ndarray:
+        """Every request's last token (a chained round keeps no tails)."""
+        return np.fromiter(((r.output_ids[-1] if r.output_ids else r.prompt_ids[-1])
+                            for r in plan.requests), np.int32, plan.B)
 
     def _launch_draft(self, plan: _RoundPlan) -> None:
         """Upload phase A, launch draft pass 0, plan the rest of the draft side
@@ -628,15 +724,17 @@ class SpeculativeDecoder:
         plan.dev_params, plan.dev_idsv = params, idsv
 
     def _launch_verify(self, plan: _RoundPlan, target_cache: PagedKVCache,
-                       ev: tuple[torch.cuda.Event, torch.cuda.Event] | None) -> None:
+                       ev: tuple[torch.cuda.Event, torch.cuda.Event] | None,
+                       chain: bool = False) -> None:
         """Plan the target side (its slots are taken here), then the verify pass
         and the fused accept kernel."""
         G, V = self.gamma, self.target.cfg.vocab_size
         B = plan.B
         buf = self._buf
         stream = _lib.stream_ptr(self.device)
-        self._plan_verify(plan, target_cache)
+        self._plan_verify(plan, target_cache, chain)
         vblob = self._staging_v.upload(plan.blob_v)
+        plan.dev_blob_v = vblob
         w = [vblob[o : o + n] for o, n in plan.spans_v]
         tw = plan.tw
         bv = PagedBatch(
@@ -684,7 +782,10 @@ class SpeculativeDecoder:
         keep = n_tok + nacc
         target_cache.truncate_many(ids, keep, plan.trows)
         d_len = plan.d_cached + plan.n0 + (G - 1)
-        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep), plan.drows)
+        # with a chained round in flight its draft passes write into the
+        # blocks reserved for it: keep them
+        self.draft_cache.truncate_many(ids, np.minimum(d_len, keep), plan.drows,
+                                       keep_blocks=plan.chain_reserved)
         rows = tokens.tolist()
         nacc_l = nacc.tolist()
         keep_l = keep.tolist()

@@ -295,6 +295,7 @@ class _Setup:
         ccfg = CacheConfig(16, blocks, "bfloat16")
         self.cache = PagedKVCache(tcfg, ccfg, DEV)
         self.dec = SpeculativeDecoder(self.target, self.draft, ccfg, gamma=gamma, device=DEV)
+        self.dec.lookahead = False  # the checks read this round's logits out of its buffers
         rng = np.random.default_rng(seed)
         self.reqs, self.gens, self.oreqs = [], {}, []
         for i, c in enumerate(ctx):

@@ -123,6 +123,7 @@ def test_sampled_rounds_match_oracle_draw_for_draw(golden, setting) -> None:
     o_t = OracleModel(tiny_dims(golden, "target"), tiny_state(golden, "target"))
     o_d = OracleModel(tiny_dims(golden, "draft"), tiny_state(golden, "draft"))
     dec = SpeculativeDecoder(target, draft, _cache_cfg(8, 64), gamma=gamma)
+    dec.lookahead = False  # the round's proposals are read back out of its buffers
     cache = PagedKVCache(target.cfg, _cache_cfg(8, 64), DEV)
     rng = np.random.default_rng(4)
     sc = SamplingConfig(temperature=t, top_k=k, top_p=p, max_new_tokens=64)

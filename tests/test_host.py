@@ -647,3 +647,28 @@ def test_chunked_prefill_charges_only_the_next_chunk() -> None:
     assert [r.request_id for r in plain.schedule(0.0).scheduled] == [0]
     with pytest.raises(ValueError):
         SchedulerConfig(prefill_chunk=0)
+
+
+def test_reserved_capacity_and_lazy_truncation() -> None:
+    """reserve_many gives blocks without tokens; appends inside the reserve
+    take no block and land on the reserved blocks; truncate with keep_blocks
+    keeps them; free returns everything."""
+    c = host_cache(block_size=4, num_blocks=32)
+    c.append_many([0, 1], [5, 2])
+    free0 = c.num_free_blocks
+    assert c.reserve_many([0, 1], [13, 3])  # 4 blocks for seq 0 (had 2), 1 for seq 1 (had 1)
+    assert c.num_free_blocks == free0 - 2 and c.num_tokens(0) == 5
+    table0 = list(c.tables[0].blocks)
+    slots = c.append_many([0], [6]).tolist()  # positions 5..10, inside the reserve
+    assert c.num_free_blocks == free0 - 2
+    assert slots == [table0[p // 4] * 4 + p % 4 for p in range(5, 11)]
+    c.truncate_many([0], [6], keep_blocks=True)
+    assert c.num_tokens(0) == 6 and list(c.tables[0].blocks) == table0
+    assert not c.reserve_many([1], [4 * 40])  # more than the pool: nothing changes
+    assert c.num_free_blocks == free0 - 2
+    with pytest.raises(ValueError):
+        c.truncate_many([0], [9], keep_blocks=True)
+    c.free(0)
+    c.free(1)
+    assert c.num_free_blocks == 32
+    c.allocator.check_invariants()
