@@ -127,7 +127,7 @@ class LLMEngine:
         self._param_upload = HostStaging(self.device)
         self._q_start = np.zeros(1, dtype=np.int32)  # the last built pass's row offsets
         self.lookahead = True  # let the decoder draft the next round ahead (same streams)
-        self._no_rows = torch.zeros(1, dtype=torch.int32, device=self.device)[:0]  # no logits
+        self._no_rows = torch.zeros(0, dtype=torch.int32, device=self.device)  # no logits
         self.spec = None
         if draft_model is not None and self.config.speculative.enabled:
             from .speculative import SpeculativeDecoder
@@ -246,7 +246,7 @@ class LLMEngine:
         done = [i for i, r in enumerate(batch) if r.num_uncomputed == 0]
         out: list[list[int]] = [[] for _ in batch]
         if not done:
-            self.model.forward_paged(meta, self.cache, logit_rows=self._no_rows)
+            self.model.forward_paged(meta, self.cache, logit_rows=self._no_rows)  # K/V only
             return out
         fin = [batch[i] for i in done]
         last_rows = (self._q_start[1:] - 1).astype(np.int32)[done]

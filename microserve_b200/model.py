@@ -294,10 +294,11 @@ class Transformer:
         return sum(t.numel() * t.element_size() for t in ts)
 
     # -- forward ---------------------------------------------------------------
-    def _no_rows(self) -> torch.Tensor:
+    def _placeholder(self) -> torch.Tensor:
+        """A 4-byte device buffer whose pointer stands for an empty argument."""
         if self._empty_rows is None:
             self._empty_rows = torch.zeros(1, dtype=torch.int32, device=self.device)
-        return self._empty_rows[:0]
+        return self._empty_rows
 
     def workspace(self, n_tokens: int, n_rows: int, attn_scratch: int = 0) -> torch.Tensor:
         """Grow-only device workspace: ms_forward's carve plus ``attn_scratch``
@@ -324,15 +325,16 @@ class Transformer:
         preallocated buffer whose rows are ``out_row_stride`` apart.
         """
         n_rows = batch.n_tokens if logit_rows is None else int(logit_rows.numel())
-        if logit_rows is not None and n_rows == 0:
-            # no logits wanted: a non-null row list of length 0 (a null list
-            # would mean "every row")
-            logit_rows = self._no_rows()
         if out is None:
-            # (at least one row, so the pointer is never null when no logits are wanted)
-            out = torch.empty((max(n_rows, 1), self.cfg.vocab_size), dtype=torch.float32,
-                              device=self.device)[:n_rows]
+            out = torch.empty((n_rows, self.cfg.vocab_size), dtype=torch.float32,
+                              device=self.device)
             out_row_stride = 0
+        rows_ptr, out_ptr = _lib.ptr(logit_rows), out.data_ptr()
+        if logit_rows is not None and n_rows == 0:
+            # No logits wanted.  An empty tensor's data pointer is null, and a
+            # null row list means "every row": pass a real (unused) row list
+            # and output of length 0 instead.
+            rows_ptr, out_ptr = self._placeholder().data_ptr(), self._placeholder().data_ptr()
         cb = batch.c_struct()
         cc = cache.c_struct()
         scratch = int(_lib.load().ms_attention_scratch_size(ctypes.byref(cc), self.cfg.n_heads,
@@ -340,7 +342,7 @@ class Transformer:
         ws = self.workspace(batch.n_tokens, n_rows, scratch)
         _lib.call(
             "ms_forward", ctypes.byref(self._c_model), ctypes.byref(cache.c_struct()),
-            ctypes.byref(cb), _lib.ptr(logit_rows), n_rows, out.data_ptr(), out_row_stride,
+            ctypes.byref(cb), rows_ptr, n_rows, out_ptr, out_row_stride,
             ws.data_ptr(), ws.numel(), _lib.stream_ptr(self.device),
         )
         return out
