@@ -276,6 +276,14 @@ def plan_waves(ctx: np.ndarray, per_req_blocks: np.ndarray, cap_blocks: int, max
     return waves
 
 
+# DRAM bytes per round of the GEMM class on the default 1.1B workload (256
+# requests, gamma 4, chained rounds): the per-launch traffic of an ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum of every GEMM shape,
+# profiles/gemm_tc_kernel_dram_traffic_llama1.1b.md) times each shape's
+# launches per round.
+GEMM_DRAM_BYTES_PER_ROUND_1B = 4.66e9
+
+
 def run_gpu(args: argparse.Namespace) -> None:
     import torch
 
@@ -439,6 +447,9 @@ def run_gpu(args: argparse.Namespace) -> None:
 
     peaks = _peaks()
     achieved = flops / (gemm_ms.value / 1e3) / 1e12 if gemm_ms.value > 0 else 0.0
+    default_workload = (not args.small and not reqset.strong and args.model == "1b"
+                        and args.requests == 256)
+    weight_bytes_round = target.weight_bytes() + GAMMA * draft.weight_bytes()
     rounds_timed = args.steps * len(waves)
     workload = WORKLOAD if not args.small else WORKLOAD + " [small: 2+1 layers]"
     if reqset.strong:
@@ -502,7 +513,9 @@ def run_gpu(args: argparse.Namespace) -> None:
             "unit": "TFLOP/s",
             "frac": achieved / peaks["bf16_sustained"],
             "peak_source": peaks["source"],
-            "traffic": None,
+            "traffic": (GEMM_DRAM_BYTES_PER_ROUND_1B if default_workload else None),
+            "traffic_unit": "bytes per round (all GEMM launches of a round, ncu capture)",
+            "weight_bytes_per_round": weight_bytes_round,
             "launches": int(gemm_n.value),
             "device_ms": gemm_ms.value,
             "measured_over": f"{args.steps} rounds of the same workload after the timed rounds, "
