@@ -92,6 +92,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--qlen", type=int, default=5, help="--micro attention: query tokens per sequence")
     ap.add_argument("--dh", type=int, default=64, choices=[64, 128], help="--micro attention: head size")
     ap.add_argument("--iters", type=int, default=20, help="--micro: timed launches")
+    ap.add_argument("--gemm-policy", type=int, default=0, choices=[0, 1, 2],
+                    help="tensor-core GEMM kernel: 0 by shape, 1 one CTA per tile, 2 CTA pairs")
     return ap.parse_args()
 
 
@@ -1113,6 +1115,10 @@ def use_8b(args: argparse.Namespace) -> None:
 
 def main() -> None:
     args = parse()
+    if args.gemm_policy:
+        from microserve_b200 import _lib
+
+        _lib.call("ms_gemm_set_policy", args.gemm_policy)
     if args.model == "8b":
         if args.impl == "reference" or args.micro:
             raise SystemExit("--model 8b runs the speculative rounds on the GPU only")

@@ -165,6 +165,7 @@ _SIGNATURES: dict[str, tuple[object, list[object]]] = {
                            c_void_p]),
     "ms_gemm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64, c_int,
                         c_int, c_int, c_void_p]),
+    "ms_gemm_set_policy": (c_int, [c_int]),
     "ms_attention_scratch_size": (c_size_t, [POINTER(MsKVCache), c_int, POINTER(MsBatch)]),
     "ms_paged_attention": (c_int, [c_void_p, POINTER(MsKVCache), c_int, POINTER(MsBatch), c_int,
                                    c_void_p, c_void_p]),

@@ -335,11 +335,13 @@ struct Schedule {
   int64_t it, it_end;  // stream-K: [it, it_end) over tiles * kiters
   int next_tile;       // round-robin
 
-  __device__ void init(int tiles_, int kiters_, bool sk) {
+  __device__ void init(int tiles_, int kiters_, bool sk) { init(tiles_, kiters_, sk, gridDim.x, blockIdx.x); }
+  // `grid_` workers, this one `cta_` (a CTA, or a CTA pair of the 2-SM kernel)
+  __device__ void init(int tiles_, int kiters_, bool sk, int grid_, int cta_) {
     tiles = tiles_;
     kiters = kiters_;
-    grid = gridDim.x;
-    cta = blockIdx.x;
+    grid = grid_;
+    cta = cta_;
     stream_k = sk;
     const int64_t total = (int64_t)tiles * kiters;
     it = total * cta / grid;
@@ -511,6 +513,237 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---- 2-SM variant (cta_group::2) ------------------------------------------------------
+// A cluster of two CTAs on two SMs computes 256 x 256 output tiles with
+// tcgen05.mma.cta_group::2 (M = 256): CTA r of the pair holds rows
+// [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the B
+// tile (the tile's output columns) in its shared memory, and its TMEM holds
+// output rows 128 r .. 128 r + 127 for all 256 columns.  Per k-step an SM
+// loads 32 KB (16 KB of A, 16 KB of B) for the work a 1-SM 128 x 256 tile
+// needs 48 KB for: the operand feed from L2, which bounds the 1-SM kernel at
+// K = 2048 (about 45 B per SM-cycle against the 88 B a k-step's MMAs would
+// take), carries two thirds of the bytes per FLOP.
+//   warp 0 lane 0, both CTAs: TMA loads of its own A and B halves
+//     (cp.async.bulk.tensor ... .cta_group::2, plain tile loads of this GPU's
+//     memory), completing on the leader CTA's "full" barrier, whose expected
+//     byte count (both halves of both CTAs) the leader posts;
+//   warp 1: both CTAs allocate 512 TMEM columns (two 256-column
+//     accumulators) with cta_group::2; lane 0 of the leader issues the MMAs
+//     and commits each stage to both CTAs' "empty" barriers and each finished
+//     accumulator to both CTAs' "tfull" barriers (a commit with the pair's
+//     CTA mask: a completion signal, not a data load);
+//   warps 2-5, both CTAs: the epilogue of their 128 rows, then an arrive on
+//     the leader's "tempty" barrier (8 arrivals free an accumulator).
+// Tiles (or stream-K pieces) are dealt to CTA pairs; both CTAs of a pair
+// walk the same schedule.  Waits are bounded as in the 1-SM kernel; the
+// pair meets at a cluster barrier before any cross-CTA signal and again
+// before TMEM is released and the CTAs exit.
+constexpr int kStages2 = 6;
+constexpr int kHalf2 = 128 * BK * 2;       // one CTA's A or B half of a k-step (16 KB)
+constexpr int kStage2 = 2 * kHalf2;        // per CTA and stage
+constexpr int kSmem2 = kStages2 * kStage2 + 1024 + 256;
+constexpr int kBN2 = 256;                  // tile columns (each CTA holds 128 rows of B)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of this CTA's shared variable `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map,
+                                                 uint32_t leader_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t id,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(id), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at shared offset `bar` in both CTAs of the pair once
+// the MMAs this thread issued so far have completed (a commit to the CTA
+// mask 0b11; no data moves).
+__device__ __forceinline__ void umma_pair_commit_both(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+
+template <int EPI, typename TC>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
+                    const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
+                    int* err) {
+  pdl_enter();
+  constexpr int S = kStages2;
+  constexpr int BN = kBN2;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  unsigned char* smem = smem_raw + pad;
+  const uint32_t sbase = raw + pad;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * kStage2);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * S;
+  const uint32_t tfull0 = full0 + 16 * S, tempty0 = tfull0 + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const int mt = (M + 2 * BM - 1) / (2 * BM);  // 256-row tiles
+  const int tiles = mt * (N / BN);
+  const int kiters = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull0 + 8 * a, 1);
+      mbar_init(tempty0 + 8 * a, 8);  // four epilogue warps in each CTA
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(2 * BN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any signal crosses
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  Schedule sched;
+  sched.init(tiles, kiters, stream_k != 0, gridDim.x / 2, blockIdx.x / 2);
+  int tile, k0, k1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs) ----
+      const uint32_t leader_full0 = cluster_addr(full0, 0);
+      uint32_t q = 0;
+      bool alive = true;
+      while (alive && sched.next(tile, k0, k1)) {
+        const int m0 = (tile % mt) * 2 * BM + (int)rank * BM;
+        const int n0 = (tile / mt) * BN + (int)rank * (BN / 2);
+        for (int k = k0; k < k1; ++k, ++q) {
+          const uint32_t s = q % S;
+          if (q >= (uint32_t)S &&
+              !mbar_wait(empty0 + 8 * s, ((q / S) - 1) & 1, abort_flag, err)) {
+            alive = false;
+            break;
+          }
+          const uint32_t dst = sbase + s * kStage2;
+          if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * kStage2);
+          tma_load_2d_pair(dst, &tmap_a, leader_full0 + 8 * s, k * BK, m0);
+          tma_load_2d_pair(dst + kHalf2, &tmap_b, leader_full0 + 8 * s, k * BK, n0);
+        }
+      }
+      if (*abort_flag && rank == 0) {  // every load of the pair completes on these barriers
+        const long long t0 = clock64();
+        for (uint32_t j = q > (uint32_t)S ? q - S : 0; j < q; ++j)
+          while (!mbar_try_wait(full0 + 8 * (j % S), (j / S) & 1) && clock64() - t0 < kWaitCycles) {
+          }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---- MMA issuer (leader CTA) ----
+      const uint32_t id = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                          ((uint32_t)((2 * BM) >> 4) << 24);
+      uint32_t q = 0, seg = 0;
+      bool alive = true;
+      while (alive && sched.next(tile, k0, k1)) {
+        const uint32_t a = seg & 1, u = seg >> 1;
+        if (u >= 1 && !mbar_wait(tempty0 + 8 * a, (u - 1) & 1, abort_flag, err)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t d = tmem + a * BN;
+        for (int k = k0; k < k1; ++k, ++q) {
+          const uint32_t s = q % S;
+          if (!mbar_wait(full0 + 8 * s, (q / S) & 1, abort_flag, err)) {
+            alive = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t a_addr = sbase + s * kStage2;
+          const uint32_t b_addr = a_addr + kHalf2;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk)
+            umma_pair(d, sdesc(a_addr + kk * 32), sdesc(b_addr + kk * 32), id,
+                      (k > k0) || (kk > 0));
+          umma_pair_commit_both(empty0 + 8 * s);
+        }
+        if (!alive) break;
+        umma_pair_commit_both(tfull0 + 8 * a);
+        ++seg;
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5 (both CTAs): rows 128 * rank + 32 * (warp % 4) + lane ----
+    const int row_group = warp & 3;
+    const bool reduce = EPI == kEpiResidual && stream_k;
+    const uint32_t leader_tempty0 = cluster_addr(tempty0, 0);
+    uint32_t seg = 0;
+    while (sched.next(tile, k0, k1)) {
+      const uint32_t a = seg & 1, u = seg >> 1;
+      if (!mbar_wait(tfull0 + 8 * a, u & 1, abort_flag, err)) break;
+      __syncwarp();
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int m = (tile % mt) * 2 * BM + (int)rank * BM + row_group * 32 + lane;
+      const int n0 = (tile / mt) * BN;
+      const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(base + c, v);
+        if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(leader_tempty0 + 8 * a);
+      ++seg;
+    }
+  }
+  __syncwarp();
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while the pair's MMAs or signals may reach it
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN));
+  }
+}
+
 // ---- host side ------------------------------------------------------------------------
 using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                               const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -607,6 +840,61 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
   return check_launch("gemm_tc_kernel");
 }
 
+template <int EPI, typename TC>
+int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
+               int64_t ldc, bool stream_k, cudaStream_t s) {
+  CUtensorMap ta, tb;
+  MS_TRY(tensor_map(A, M, K, BM, &ta));
+  MS_TRY(tensor_map(B, N, K, kBN2 / 2, &tb));
+  auto kern = gemm_tc2_kernel<EPI, TC>;
+  static uint64_t attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set & (1ull << (dev & 63)))) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
+    if (e != cudaSuccess) return fail(MS_ERR_CUDA, "gemm_tc2: smem attribute: %s", cudaGetErrorString(e));
+    attr_set |= 1ull << (dev & 63);
+  }
+  const int tiles = ((M + 2 * BM - 1) / (2 * BM)) * (N / kBN2);
+  const int kiters = (K + BK - 1) / BK;
+  // Pairs are placed within a GPC: as many as can be resident at once (at
+  // most one CTA per SM), so the persistent grid is a single wave.
+  static int max_pairs[64] = {};
+  if (max_pairs[dev & 63] == 0) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(kNumSMs);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmem2;
+    int n = 0;
+    const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = kNumSMs / 2;
+    }
+    max_pairs[dev & 63] = std::min(n, kNumSMs / 2);
+  }
+  const int pairs_max = max_pairs[dev & 63];
+  int pairs = stream_k ? (int)std::min<int64_t>((int64_t)tiles * kiters, pairs_max)
+                       : std::min(tiles, pairs_max);
+  if (pairs < 1) pairs = 1;
+  launch_pdl(kern, 2 * pairs, kThreads, kSmem2, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
+             stream_k ? 1 : 0, device_error_word());
+  return check_launch("gemm_tc2_kernel");
+}
+
+// Which tcgen05 kernel: 0 = by shape, 1 = one CTA per tile, 2 = CTA pairs
+// (ms_gemm_set_policy; for measurements and tests).
+int g_gemm_policy = 0;
+
+// CTA pairs (256 x 256 tiles) for GEMMs with at least 4 row tiles of 256 and
+// 256-wide column tiles.
+bool use_pairs(int M, int N, int epi) {
+  if (g_gemm_policy == 1 || epi == kEpiRopeKV || N % kBN2 != 0) return false;
+  if (g_gemm_policy == 2) return true;
+  return false;
+}
+
 // Tile width: 256 columns when N allows it and there are enough tiles to go
 // around, else 128.
 bool use_bn256(int M, int N, bool stream_k) {
@@ -653,6 +941,18 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
        reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
+  if (use_pairs(M, N, epi)) {
+    if (epi == kEpiSwiGLU) return launch_tc2<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+    if (epi == kEpiResidual) {
+      const bool in_place = static_cast<const void*>(R) == C;
+      const int tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * (N / kBN2);
+      const double ab_bytes = 2.0 * ((double)M + (double)N) * (double)K;
+      const bool stream_k = in_place && (tiles2 < kNumSMs / 2 || ab_bytes <= 64.0 * (1 << 20));
+      return launch_tc2<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s);
+    }
+    if (c_dtype == MS_DTYPE_F32) return launch_tc2<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
+    return launch_tc2<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+  }
   if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
   if (epi == kEpiResidual) {
     // In place (C += A B^T): stream-K with reductions into C, unless there is
@@ -672,3 +972,9 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
 }
 
 }  // namespace ms
+
+extern "C" int ms_gemm_set_policy(int policy) {
+  if (policy < 0 || policy > 2) return ms::fail(MS_ERR_INVALID, "ms_gemm_set_policy: %d", policy);
+  ms::g_gemm_policy = policy;
+  return MS_OK;
+}

@@ -23,8 +23,19 @@ def _ref(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     return A.float() @ B.float().T
 
 
+@pytest.fixture(params=[1, 2], ids=["one_cta_per_tile", "cta_pairs"], autouse=True)
+def policy(request):
+    """Every case on both tcgen05 kernels: one CTA per 128 x 256 tile, and CTA
+    pairs (cta_group::2, 256 x 256 tiles) wherever N allows."""
+    from microserve_b200 import _lib
+
+    _lib.call("ms_gemm_set_policy", request.param)
+    yield request.param
+    _lib.call("ms_gemm_set_policy", 0)
+
+
 SHAPES = [(1, 128, 64), (77, 256, 520), (128, 128, 2048), (300, 384, 200), (1280, 2560, 2048),
-          (256, 1024, 5632)]
+          (256, 1024, 5632), (600, 512, 192), (1280, 2048, 5632), (2048, 2048, 2048)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
