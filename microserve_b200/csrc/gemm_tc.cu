@@ -887,12 +887,15 @@ int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int
 // (ms_gemm_set_policy; for measurements and tests).
 int g_gemm_policy = 0;
 
-// CTA pairs (256 x 256 tiles) for GEMMs with at least 4 row tiles of 256 and
-// 256-wide column tiles.
+// CTA pairs by shape: the wide store GEMMs (the lm_head: 1280 x 32000 x 2048
+// 170 -> 151 us, 256 x 32000 x 2048 49 -> 45 us).  Elsewhere the pairs
+// measured no faster (1280 x 11264 x 2048 SwiGLU 51.6 us both) or slower
+// (stream-K residual, qkv, M = 256 projections): halving the bytes each SM
+// loads per k-step does not move GEMMs that run at the power-capped clock.
 bool use_pairs(int M, int N, int epi) {
   if (g_gemm_policy == 1 || epi == kEpiRopeKV || N % kBN2 != 0) return false;
   if (g_gemm_policy == 2) return true;
-  return false;
+  return epi == kEpiStore && N >= 16384 && M >= 2 * BM;
 }
 
 // Tile width: 256 columns when N allows it and there are enough tiles to go
