@@ -13,10 +13,12 @@ forward that computes logits only for each request's last row, then a draw
 that writes the proposal straight into the next pass's inputs and into the
 verify batch), one target verify pass over ``[uncached tokens] + proposals``
 with logits for the last gamma+1 rows of each request, and the fused
-accept/resample/bonus kernel.  All metadata for the round goes up in one
-pinned copy and the accepted tokens come back in one; the host then rolls
-both caches back with ``truncate`` as the reference does
-(speculative.py:213-226).
+accept/resample/bonus kernel.  The metadata goes up in at most three pinned
+copies, planned while earlier passes run, and the accepted tokens come back
+in one; the host then rolls both caches back with ``truncate`` as the
+reference does (speculative.py:213-226).  When the next round's requests are
+known to continue, its draft side is planned on the device and launched
+before the host reads the results (round chaining; see SpeculativeDecoder).
 
 Random draws use Philox uniforms keyed by the request generator's seed and
 ``Request.rng_step`` (see sampling.py), one step per round: draft draw j on
