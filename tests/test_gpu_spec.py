@@ -227,3 +227,86 @@ def test_lookahead_keeps_the_streams_and_gives_back_its_slots(golden) -> None:
     ahead, dec = serve(True)
     assert ahead == plain
     assert dec.lookahead_hits >= 4 and dec.lookahead_misses >= 2
+
+
+def test_chain_plan_kernel_matches_a_host_restatement() -> None:
+    """ms_spec_chain_plan through the C ABI against the next round's draft-side
+    metadata computed here on the host, request by request: after a round
+    with n accepted of gamma proposals, a request that had T tokens holds
+    T + n + 1; draft pass 0 takes its last two tokens (the first to a spare
+    reserved slot unless n == gamma), pass j its token at T + n + j, the
+    verify batch starts with the emitted token at T + n, and the sampling
+    step advances by one."""
+    from microserve_b200 import _lib
+    from microserve_b200.config import SamplingConfig
+    from microserve_b200.sampling import make_params, params_to_device
+
+    rng = np.random.default_rng(3)
+    B, G, bs, nb = 7, 4, 8, 200
+    T = rng.integers(1, 60, B)
+    nacc = rng.integers(0, G + 1, B)
+    nacc[0], nacc[1] = 0, G  # both ends
+    out_tok = rng.integers(0, 1000, (B, G + 1)).astype(np.int32)
+    last = rng.integers(0, 1000, B).astype(np.int32)
+    width = int(((T + 2 * G + bs - 1) // bs).max())
+    tables = rng.permutation(nb)[: B * width].reshape(B, width).astype(np.int32)
+    params = make_params([SamplingConfig(temperature=0.8)] * B, np.arange(B) + 11,
+                         np.arange(B) * 3 + 5)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a, dtype=np.int32)).to(DEV)  # noqa: E731
+    d_out, d_nacc, d_T, d_last, d_tab = dev(out_tok), dev(nacc), dev(T), dev(last), dev(tables)
+    p_in = params_to_device(params, torch.device(DEV))
+    p_out = torch.empty_like(p_in)
+    n = int(_lib.load().ms_spec_chain_size(B, G))
+    chain = torch.full((n,), -7, dtype=torch.int32, device=DEV)
+    _lib.call("ms_spec_chain_plan", d_out.data_ptr(), d_nacc.data_ptr(), d_T.data_ptr(),
+              d_last.data_ptr(), d_tab.data_ptr(), width, bs, nb, p_in.data_ptr(), B, G,
+              chain.data_ptr(), p_out.data_ptr(), _lib.stream_ptr())
+    torch.cuda.synchronize()
+    assert _lib.device_error() == 0
+    got = chain.cpu().numpy()
+    slot = lambda b, p: int(tables[b, p // bs]) * bs + p % bs  # noqa: E731
+    want = {k: [] for k in ("ids0", "pos0", "slots0", "pos", "slots", "ctx", "ctx0")}
+    idsv_first = []
+    pos_j = np.zeros((G - 1, B), np.int64)
+    slots_j = np.zeros((G - 1, B), np.int64)
+    ctx_j = np.zeros((G - 1, B), np.int64)
+    for b in range(B):
+        n_b, t = int(nacc[b]), int(T[b])
+        ntok = t + n_b + 1
+        tok_a = int(out_tok[b, n_b - 1]) if n_b >= 1 else int(last[b])
+        want["ids0"] += [tok_a, int(out_tok[b, n_b])]
+        want["pos0"] += [ntok - 2, ntok - 1]
+        want["slots0"] += [slot(b, ntok - 2 if n_b == G else t + 2 * G - 1), slot(b, ntok - 1)]
+        want["ctx0"].append(ntok)
+        idsv_first.append(int(out_tok[b, n_b]))
+        for j in range(1, G):
+            pos_j[j - 1, b] = ntok + j - 1
+            slots_j[j - 1, b] = slot(b, ntok + j - 1)
+            ctx_j[j - 1, b] = ntok + j
+    o = 0
+
+    def take(k: int) -> np.ndarray:
+        nonlocal o
+        v = got[o : o + k]
+        o += k
+        return v
+
+    assert take(2 * B).tolist() == want["ids0"]
+    assert take(2 * B).tolist() == want["pos0"]
+    assert take(2 * B).tolist() == want["slots0"]
+    assert take(B + 1).tolist() == [2 * b for b in range(B + 1)]
+    assert take(B).tolist() == want["ctx0"]
+    assert take(B).tolist() == [2] * B
+    assert take(B).tolist() == [2 * b + 1 for b in range(B)]
+    assert take((G - 1) * B).tolist() == pos_j.reshape(-1).tolist()
+    assert take((G - 1) * B).tolist() == slots_j.reshape(-1).tolist()
+    assert take((G - 1) * B).tolist() == ctx_j.reshape(-1).tolist()
+    assert take(B + 1).tolist() == list(range(B + 1))
+    assert take(B).tolist() == [1] * B
+    verify_ids = take((G + 1) * B).reshape(B, G + 1)
+    assert verify_ids[:, 0].tolist() == idsv_first
+    assert (verify_ids[:, 1:] == -7).all()  # left for the samplers' scatter
+    assert o == n
+    po = np.frombuffer(p_out.cpu().numpy().tobytes(), dtype=_lib.SAMPLING_PARAMS_DTYPE)
+    assert po["step"].tolist() == (params["step"] + 1).tolist()
+    assert po["seed"].tolist() == params["seed"].tolist()
