@@ -244,6 +244,17 @@ def config_fixtures() -> None:
                 out[f"cfg2/{tag}/g{gamma}/{j}"] = np.asarray(t)
             out[f"cfg2/{tag}/g{gamma}/counts"] = np.asarray(counts)
             print(f"config 2 amplify {amp} gamma {gamma}: counts {counts}")
+    # top-p with exact ties at the cut (sampling.py:34-51): which tied tokens
+    # survive follows torch.sort's order among equal values, which is not
+    # stable for long rows
+    from microserve.sampling import apply_top_p
+
+    x = torch.zeros(1, 40000)
+    x[0, ::3] = 1.0
+    out["ties/long_row_kept"] = torch.isfinite(apply_top_p(x.clone(), 0.3)[0]).nonzero().flatten().numpy()
+    x = torch.tensor([[2.0, 1.0, 1.0, 1.0, 1.0, 1.0, 0.0, 1.0]])
+    out["ties/short_row_kept"] = torch.isfinite(apply_top_p(x.clone(), 0.5)[0]).nonzero().flatten().numpy()
+
     # scheduler decisions under memory pressure (scheduler.py:173-258)
     from microserve.cache import PagedKVCache
     from microserve.config import SamplingConfig, SchedulerConfig
