@@ -195,8 +195,10 @@ def _ref_model(shape, state: dict[str, np.ndarray]):
 
 
 def _run_engine(target, draft, gamma: int, prompts, budgets, cache_blocks: int,
-                max_batch: int, max_tokens: int) -> tuple[list[list[int]], list[int]]:
-    """LLMEngine.run of the reference (engine.py:155-202) at temperature 0."""
+                max_batch: int, max_tokens: int,
+                preemptions: bool = False) -> tuple[list[list[int]], list[int]]:
+    """LLMEngine.run of the reference (engine.py:155-202) at temperature 0;
+    counts are [accepted, proposed, steps] (+ preemptions when asked)."""
     from microserve.config import (CacheConfig, EngineConfig, SamplingConfig, SchedulerConfig,
                                    SpeculativeConfig)
     from microserve.engine import LLMEngine
@@ -209,8 +211,10 @@ def _run_engine(target, draft, gamma: int, prompts, budgets, cache_blocks: int,
     reqs = [eng.add_request(p, SamplingConfig(temperature=0.0, max_new_tokens=int(b)))
             for p, b in zip(prompts, budgets, strict=True)]
     outs = {o.request_id: o.output_ids for o in eng.run()}
-    return ([outs[r.request_id] for r in reqs],
-            [eng.stats.num_draft_accepted, eng.stats.num_draft_proposed, eng.stats.num_steps])
+    counts = [eng.stats.num_draft_accepted, eng.stats.num_draft_proposed, eng.stats.num_steps]
+    if preemptions:
+        counts.append(eng.stats.num_preemptions)
+    return [outs[r.request_id] for r in reqs], counts
 
 
 def config_fixtures() -> None:
@@ -244,6 +248,20 @@ def config_fixtures() -> None:
                 out[f"cfg2/{tag}/g{gamma}/{j}"] = np.asarray(t)
             out[f"cfg2/{tag}/g{gamma}/counts"] = np.asarray(counts)
             print(f"config 2 amplify {amp} gamma {gamma}: counts {counts}")
+    # the same workload under memory pressure: 24 requests in 64 blocks of 16,
+    # so the scheduler preempts running requests between speculative rounds
+    # and recomputes them by prefill (scheduler.py:196-225, engine.py:163-166)
+    wp = wl.config2(24, seed=5)
+    for amp in (1.0, 20.0):
+        tag = f"a{int(amp)}"
+        target = _ref_model(wl.CHAR_TARGET, wl.init_state(wl.CHAR_TARGET, 0, amp))
+        draft = _ref_model(wl.CHAR_DRAFT, wl.init_state(wl.CHAR_DRAFT, 1, amp))
+        toks, counts = _run_engine(target, draft, 3, wp.prompts, wp.max_new_tokens, 64, 24, 4096,
+                                   preemptions=True)
+        for j, t in enumerate(toks):
+            out[f"cfg2p/{tag}/g3/{j}"] = np.asarray(t)
+        out[f"cfg2p/{tag}/g3/counts"] = np.asarray(counts)
+        print(f"config 2 amplify {amp} under memory pressure: counts {counts}")
     # top-p with exact ties at the cut (sampling.py:34-51): which tied tokens
     # survive follows torch.sort's order among equal values, which is not
     # stable for long rows

@@ -5,7 +5,9 @@
   unmodified reference engine's (``config_fixtures.npz``), and its sampled
   streams at temperature 0.8 against the oracle draw for draw;
 * config 2 (the same models, continuous batching): a 64-request subset of
-  the workload at gamma 1/2/3/5, greedy, against the reference engine;
+  the workload at gamma 1/2/3/5, greedy, against the reference engine, and
+  24 requests in a 64-block pool, where the reference preempts between
+  speculative rounds;
 * config 1 (acceptance microbenchmark): one ``ms_spec_accept`` launch at the
   full 4096 x gamma 5 x 32000, a fixed subset of 256 requests checked
   against the oracle;
@@ -180,6 +182,25 @@ def test_config2_engine_subset_matches_reference(cfgfix, gamma: int, amp: int) -
         assert toks == cfgfix[f"cfg2/a{amp}/g{gamma}/{j}"].tolist(), f"request {j}"
     assert counts == cfgfix[f"cfg2/a{amp}/g{gamma}/counts"].tolist()
     eng.cache.allocator.check_invariants()
+
+
+@pytest.mark.parametrize("amp", [1, 20])
+def test_config2_engine_under_memory_pressure_matches_reference(cfgfix, amp: int) -> None:
+    """24 requests of the continuous-batching workload in a pool of 64 blocks
+    of 16: running requests are preempted between speculative rounds and
+    recomputed by prefill.  Streams, acceptance counts, engine steps and the
+    number of preemptions equal the reference engine's."""
+    target, draft, _, _ = _char_models(float(amp))
+    w = _wl().config2(24, seed=5)
+    eng = _engine(target, draft, 3, 64, 24, 4096)
+    got, counts = _greedy_run(eng, w.prompts, w.max_new_tokens)
+    for j, toks in enumerate(got):
+        assert toks == cfgfix[f"cfg2p/a{amp}/g3/{j}"].tolist(), f"request {j}"
+    want = cfgfix[f"cfg2p/a{amp}/g3/counts"].tolist()
+    assert counts + [eng.stats.num_preemptions] == want
+    assert want[3] > 0
+    eng.cache.allocator.check_invariants()
+    assert eng.cache.num_free_blocks == eng.cache.allocator.num_blocks
 
 
 # -- config 1 ---------------------------------------------------------------------
