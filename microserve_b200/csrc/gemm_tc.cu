@@ -1,16 +1,19 @@
 // tcgen05 tensor-core GEMM for bf16 (sm_100a): C = A[M,K] * B[N,K]^T with
 // float32 accumulation in tensor memory.  Persistent and warp-specialised.
 //
-// Grid: one CTA per SM (at most), 192 threads:
+// Grid: one CTA per SM (at most), 320 threads:
 //   warp 0 lane 0  TMA producer: K-major 128B-swizzled A (128 x 64) and B
 //                  (BN x 64) tiles into a STAGES-deep shared-memory ring;
 //   warp 1         allocates 2 x BN TMEM columns (a double-buffered
 //                  accumulator); lane 0 issues tcgen05.mma.cta_group::1
 //                  .kind::f16 (M=128, N=BN, K=16), commits each stage back to
 //                  the producer and each finished accumulator to the epilogue;
-//   warps 2-5      epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
-//                  32*(w%4)..+31 = tile rows), fused store / SwiGLU / residual
-//                  reduction, while the MMA warp fills the other accumulator.
+//   warps 2-9      epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
+//                  32*(w%4)..+31 = tile rows; warps w and w+4 split the
+//                  columns), fused store / SwiGLU / residual reduction
+//                  through a shared-memory exchange that makes every global
+//                  access whole 128-byte row segments, while the MMA warp
+//                  fills the other accumulator.
 // Work: output tiles are dealt round-robin to the CTAs; for the in-place
 // residual GEMM (C += A B^T, R == C) the (tile, k-step) space is instead cut
 // into equal contiguous ranges (stream-K), and every piece is added into C
@@ -33,7 +36,11 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;  // warps 2..9: two per TMEM lane quarter
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kStageRowBytes = 128;  // epilogue exchange: 32 rows x 128 B per warp
+constexpr int kEpiBufBytes = 32 * kStageRowBytes;
+constexpr int kEpiSmem = kEpiWarps * kEpiBufBytes;
 constexpr int kNumSMs = 148;
 constexpr long long kWaitCycles = 1ll << 32;  // ~2.2 s at 1.965 GHz
 constexpr int kErrTimeout = 5;
@@ -43,7 +50,9 @@ template <int BN> struct TileCfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmem =
+      kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ + kEpiSmem;
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -147,83 +156,127 @@ __device__ __forceinline__ void red_add4(float* p, float a, float b, float c, fl
                : "memory");
 }
 
-// Epilogue for one thread's 32 consecutive columns [n, n+32) of row m.
-// kEpiResidual with `reduce`: C += acc by vector reductions (stream-K pieces
-// and whole tiles alike, C already holding the residual).
-template <int EPI, typename TC>
-__device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const float* R, int m,
-                                            int n, int N, int64_t ldc, bool reduce) {
-  if constexpr (EPI == kEpiSwiGLU) {
-    // columns [16g, 16g+8) gate, [16g+8, 16g+16) up -> outputs 8g..8g+7
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n / 2;
-    uint32_t w[8];
+// ---- epilogue stores through a per-warp shared-memory exchange --------------
+// tcgen05.ld 32x32b gives each thread one accumulator row, so stores made
+// straight from registers touch 32 rows (32 cache lines) per warp
+// instruction and the epilogue runs at the load/store unit's line rate (a
+// 128 x 256 f32 tile took ~5 us).  Instead each epilogue warp owns a 4 KB
+// buffer of 32 rows x 128 bytes: the thread holding row r writes its
+// 128-byte row segment, 16-byte chunk j at position j ^ (r & 7) (the eight
+// lanes of each 128-bit phase hit distinct banks, on both sides); read back
+// in 8 steps, step i gives lane l chunk (l & 7) of row 4 i + (l >> 3), so
+// every warp-wide global access covers four whole 128-byte row segments.
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t x, uint32_t y, uint32_t z,
+                                             uint32_t w) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(x), "r"(y), "r"(z),
+               "r"(w)
+               : "memory");
+}
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void stage_row(uint32_t buf, int lane, const uint32_t (&w)[32]) {
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
+  for (int j = 0; j < 8; ++j)
+    st_shared_v4(buf + lane * kStageRowBytes + ((j ^ (lane & 7)) << 4), w[4 * j], w[4 * j + 1],
+                 w[4 * j + 2], w[4 * j + 3]);
+}
+__device__ __forceinline__ uint4 staged_chunk(uint32_t buf, int r, int j) {
+  return ld_shared_v4(buf + r * kStageRowBytes + ((j ^ (r & 7)) << 4));
+}
+// SwiGLU of 32 accumulator columns laid out [16g, 16g+8) gate, [16g+8,
+// 16g+16) up (g = 0, 1): 16 bf16 outputs in 8 words.  silu(x) = x / (1 +
+// e^-x) with the fast exponential and division intrinsics (the result is
+// rounded to bf16).
+__device__ __forceinline__ void swiglu16(const float (&v)[32], uint32_t* w) {
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        const float g0 = v[16 * g + j], g1 = v[16 * g + j + 1];
-        const float u0 = v[16 * g + 8 + j], u1 = v[16 * g + 8 + j + 1];
-        const float s0 = g0 / (1.f + expf(-g0)) * u0;
-        const float s1 = g1 / (1.f + expf(-g1)) * u1;
-        w[g * 4 + j / 2] = pack_bf16(s0, s1);
+  for (int g = 0; g < 2; ++g) {
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const float g0 = v[16 * g + j], g1 = v[16 * g + j + 1];
+      const float u0 = v[16 * g + 8 + j], u1 = v[16 * g + 8 + j + 1];
+      const float s0 = __fdividef(g0, 1.f + __expf(-g0)) * u0;
+      const float s1 = __fdividef(g1, 1.f + __expf(-g1)) * u1;
+      w[4 * g + j / 2] = pack_bf16(s0, s1);
+    }
+  }
+}
+
+// One warp's share of a finished BN-column accumulator: rows row0 .. row0+31
+// (TMEM lanes at `base`), the 128-byte row segments u = half, half + 2, ...
+// of the tile.  A segment is 32 input columns for f32 outputs, 64 for bf16
+// and 128 for SwiGLU (64 bf16 outputs).  kEpiResidual with `reduce` adds
+// into C with vector reductions (C already holds the residual); without it
+// C = R + acc.
+template <int BN, int EPI, typename TC>
+__device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int lane, int half,
+                                              int row0, int M, int n0, int64_t ldc, TC* C,
+                                              const float* R, bool reduce) {
+  constexpr int U = EPI == kEpiSwiGLU ? 128 : (sizeof(TC) == 2 ? 64 : 32);
+  static_assert(BN % U == 0, "tile width");
+#pragma unroll 1
+  for (int u = half; u < BN / U; u += 2) {
+    uint32_t w[32];
+    if constexpr (EPI == kEpiSwiGLU) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        float v[32];
+        tmem_ld32(base + u * U + 32 * h, v);
+        swiglu16(v, w + 8 * h);
       }
-    }
-    if (n + 32 <= N) {
-      uint4* o = reinterpret_cast<uint4*>(out);
-      o[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      o[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
-  } else if constexpr (EPI == kEpiResidual) {
-    float* out = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
-    if (reduce) {
-      if (n + 32 <= N) {
+    } else if constexpr (sizeof(TC) == 2) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) red_add4(out + i, v[i], v[i + 1], v[i + 2], v[i + 3]);
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+        tmem_ld32(base + u * U + 32 * h, v);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) w[16 * h + k] = pack_bf16(v[2 * k], v[2 * k + 1]);
+      }
+    } else {
+      float v[32];
+      tmem_ld32(base + u * U, v);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) w[k] = __float_as_uint(v[k]);
+    }
+    stage_row(buf, lane, w);
+    __syncwarp();
+    const int j = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3);
+      const uint4 x = staged_chunk(buf, r, j);
+      const int m = row0 + r;
+      if (m >= M) continue;
+      if constexpr (EPI == kEpiSwiGLU) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc +
+                             (n0 + u * U) / 2 + 8 * j;
+        *reinterpret_cast<uint4*>(out) = x;
+      } else if constexpr (EPI == kEpiResidual) {
+        const int64_t off = (int64_t)m * ldc + n0 + u * U + 4 * j;
+        float* out = reinterpret_cast<float*>(C) + off;
+        const float4 a = make_float4(__uint_as_float(x.x), __uint_as_float(x.y),
+                                     __uint_as_float(x.z), __uint_as_float(x.w));
+        if (reduce) {
+          red_add4(out, a.x, a.y, a.z, a.w);
+        } else {
+          const float4 r4 = *reinterpret_cast<const float4*>(R + off);
+          *reinterpret_cast<float4*>(out) =
+              make_float4(r4.x + a.x, r4.y + a.y, r4.z + a.z, r4.w + a.w);
+        }
+      } else if constexpr (sizeof(TC) == 4) {
+        *reinterpret_cast<uint4*>(reinterpret_cast<float*>(C) + (int64_t)m * ldc + n0 + u * U +
+                                  4 * j) = x;
       } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (n + i < N) atomicAdd(out + i, v[i]);
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n0 +
+                                  u * U + 8 * j) = x;
       }
-      return;
     }
-    const float* res = R + (int64_t)m * ldc + n;
-    if (n + 32 <= N) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        const float4 r4 = *reinterpret_cast<const float4*>(res + i);
-        *reinterpret_cast<float4*>(out + i) =
-            make_float4(r4.x + v[i], r4.y + v[i + 1], r4.z + v[i + 2], r4.w + v[i + 3]);
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (n + i < N) out[i] = res[i] + v[i];
-    }
-  } else if constexpr (sizeof(TC) == 4) {
-    float* out = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
-    if (n + 32 <= N) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(out + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (n + i < N) out[i] = v[i];
-    }
-  } else {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
-    if (n + 32 <= N) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 8) {
-        *reinterpret_cast<uint4*>(out + i) =
-            make_uint4(pack_bf16(v[i], v[i + 1]), pack_bf16(v[i + 2], v[i + 3]),
-                       pack_bf16(v[i + 4], v[i + 5]), pack_bf16(v[i + 6], v[i + 7]));
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (n + i < N) out[i] = __float2bfloat16_rn(v[i]);
-    }
+    __syncwarp();
   }
 }
 
@@ -233,10 +286,12 @@ __device__ __forceinline__ void store_chunk(const float (&v)[32], TC* C, const f
 // together.  Values are rounded to bf16 first and the rotation is the same
 // arithmetic as rope_kv_write's, so q and the cache get the bits the
 // separate kernels would write.  k and v go to the cache at the row's slot
-// (pool layout (num_blocks, kv heads, block_size, dh)).
+// (pool layout (num_blocks, kv heads, block_size, dh)).  The two epilogue
+// warps of a TMEM lane quarter take alternate heads (`half_warps` 0 or 1).
 template <int BN>
-__device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0, const RopeKv& rk,
-                                            __nv_bfloat16* qkv, int64_t ldc, int* err) {
+__device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0, int half_warps,
+                                            const RopeKv& rk, __nv_bfloat16* qkv, int64_t ldc,
+                                            int* err) {
   const int dh = rk.dh, half = dh >> 1;
   const bool live = m < M;
   int pos = 0, slot = -1;
@@ -272,7 +327,7 @@ __device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0,
       }
     }
 #pragma unroll 1
-    for (int hc = 0; hc < BN; hc += dh) {
+    for (int hc = half_warps * dh; hc < BN; hc += 2 * dh) {
       const int head = (n0 + hc) / dh;
       float a[32], b[32];
       tmem_ld32(base + hc + j, a);
@@ -399,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 4);  // one arrive per epilogue warp
+      mbar_init(tempty0 + 8 * a, kEpiWarps);  // one arrive per epilogue warp
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -477,8 +532,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5 ----
+    // ---- epilogue warps 2..9: lane quarter warp % 4, column half (warp - 2) / 4 ----
     const int row_group = warp & 3;  // TMEM lanes 32*row_group .. +31
+    const int half = (warp - 2) >> 2;
+    const uint32_t buf = sbase + S * Cfg::kStageBytes + 256 + (warp - 2) * kEpiBufBytes;
     const bool reduce = EPI == kEpiResidual && stream_k;
     uint32_t seg = 0;
     while (sched.next(tile, k0, k1)) {
@@ -487,17 +544,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
-      const int m = m0 + row_group * 32 + lane;
+      const int row0 = m0 + row_group * 32;
       const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
       if constexpr (EPI == kEpiRopeKV) {
-        rope_kv_row<BN>(base, m, M, n0, rk, reinterpret_cast<__nv_bfloat16*>(C), ldc, err);
+        rope_kv_row<BN>(base, row0 + lane, M, n0, half, rk, reinterpret_cast<__nv_bfloat16*>(C),
+                        ldc, err);
       } else {
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-          float v[32];
-          tmem_ld32(base + c, v);
-          if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
-        }
+        epilogue_tile<BN, EPI, TC>(base, buf, lane, half, row0, M, n0, ldc, static_cast<TC*>(C), R,
+                                   reduce);
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
@@ -532,8 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 //     and commits each stage to both CTAs' "empty" barriers and each finished
 //     accumulator to both CTAs' "tfull" barriers (a commit with the pair's
 //     CTA mask: a completion signal, not a data load);
-//   warps 2-5, both CTAs: the epilogue of their 128 rows, then an arrive on
-//     the leader's "tempty" barrier (8 arrivals free an accumulator).
+//   warps 2-9, both CTAs: the epilogue of their 128 rows, then an arrive on
+//     the leader's "tempty" barrier (16 arrivals free an accumulator).
 // Tiles (or stream-K pieces) are dealt to CTA pairs; both CTAs of a pair
 // walk the same schedule.  Waits are bounded as in the 1-SM kernel; the
 // pair meets at a cluster barrier before any cross-CTA signal and again
@@ -541,7 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kStages2 = 6;
 constexpr int kHalf2 = 128 * BK * 2;       // one CTA's A or B half of a k-step (16 KB)
 constexpr int kStage2 = 2 * kHalf2;        // per CTA and stage
-constexpr int kSmem2 = kStages2 * kStage2 + 1024 + 256;
+constexpr int kSmem2 = kStages2 * kStage2 + 1024 + 256 + kEpiSmem;
+static_assert(kSmem2 <= 227 * 1024, "shared memory per CTA");
 constexpr int kBN2 = 256;                  // tile columns (each CTA holds 128 rows of B)
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -626,7 +681,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull0 + 8 * a, 1);
-      mbar_init(tempty0 + 8 * a, 8);  // four epilogue warps in each CTA
+      mbar_init(tempty0 + 8 * a, 2 * kEpiWarps);  // every epilogue warp of both CTAs
     }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -709,8 +764,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5 (both CTAs): rows 128 * rank + 32 * (warp % 4) + lane ----
+    // ---- epilogue warps 2..9 (both CTAs): rows 128 * rank + 32 * (warp % 4) + lane,
+    // column half (warp - 2) / 4 ----
     const int row_group = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t buf = sbase + S * kStage2 + 256 + (warp - 2) * kEpiBufBytes;
     const bool reduce = EPI == kEpiResidual && stream_k;
     const uint32_t leader_tempty0 = cluster_addr(tempty0, 0);
     uint32_t seg = 0;
@@ -719,15 +777,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (!mbar_wait(tfull0 + 8 * a, u & 1, abort_flag, err)) break;
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m = (tile % mt) * 2 * BM + (int)rank * BM + row_group * 32 + lane;
+      const int row0 = (tile % mt) * 2 * BM + (int)rank * BM + row_group * 32;
       const int n0 = (tile / mt) * BN;
       const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        float v[32];
-        tmem_ld32(base + c, v);
-        if (m < M) store_chunk<EPI, TC>(v, C, R, m, n0 + c, N, ldc, reduce);
-      }
+      epilogue_tile<BN, EPI, TC>(base, buf, lane, half, row0, M, n0, ldc, static_cast<TC*>(C), R,
+                                 reduce);
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(leader_tempty0 + 8 * a);
