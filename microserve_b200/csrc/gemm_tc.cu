@@ -146,6 +146,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -280,19 +293,23 @@ __device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int l
   }
 }
 
-// kEpiRopeKV: row m of a BN-column tile of the qkv projection.  Every head
-// lies inside one tile (dh divides BN and the tile start); the thread holds
-// the row, so the two halves of a head (columns j and j + dh/2) rotate
-// together.  Values are rounded to bf16 first and the rotation is the same
-// arithmetic as rope_kv_write's, so q and the cache get the bits the
-// separate kernels would write.  k and v go to the cache at the row's slot
-// (pool layout (num_blocks, kv heads, block_size, dh)).  The two epilogue
-// warps of a TMEM lane quarter take alternate heads (`half_warps` 0 or 1).
+// kEpiRopeKV: rows row0 .. row0+31 of a BN-column tile of the qkv
+// projection.  Every head lies inside one tile (dh divides BN and the tile
+// start); the thread holding row m rotates the two halves of a head
+// (columns j and j + dh/2) together.  Values are rounded to bf16 first and
+// the rotation is the same arithmetic as rope_kv_write's, so q and the cache
+// get the bits the separate kernels would write.  q goes to its row of the
+// qkv buffer, k and v to the cache at the row's slot (pool layout
+// (num_blocks, kv heads, block_size, dh)).  The two epilogue warps of a TMEM
+// lane quarter take alternate heads (`half_warps` 0 or 1).  Each head's
+// 32-column slice pair (128 bytes of bf16 per row) goes through the warp's
+// exchange buffer, so the stores cover whole row segments.
 template <int BN>
-__device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0, int half_warps,
-                                            const RopeKv& rk, __nv_bfloat16* qkv, int64_t ldc,
-                                            int* err) {
+__device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int lane, int row0,
+                                             int M, int n0, int half_warps, const RopeKv& rk,
+                                             __nv_bfloat16* qkv, int64_t ldc, int* err) {
   const int dh = rk.dh, half = dh >> 1;
+  const int m = row0 + lane;
   const bool live = m < M;
   int pos = 0, slot = -1;
   if (live) {
@@ -303,81 +320,82 @@ __device__ __forceinline__ void rope_kv_row(uint32_t base, int m, int M, int n0,
     }
     slot = rk.slots[m];
   }
-  const int blk = slot >= 0 ? slot / rk.bs : 0, off = slot - blk * rk.bs;
-  const bool slot_ok = slot >= 0 && blk < rk.num_blocks;
-  // Columns j .. j+31 of every head's halves share the row's cos/sin: load
-  // them once per j, then walk the tile's heads.
+  const bool slot_ok = slot >= 0 && slot / rk.bs < rk.num_blocks;
+  // cos/sin of the row's position, read as float4 (L1-resident) per head
+  const float* cos_row = rk.cos_t + (int64_t)pos * half;
+  const float* sin_row = rk.sin_t + (int64_t)pos * half;
 #pragma unroll 1
   for (int j = 0; j < half; j += 32) {
-    float cs[32], sn[32];
-    if (live) {
-      const float4* c4 = reinterpret_cast<const float4*>(rk.cos_t + (int64_t)pos * half + j);
-      const float4* s4 = reinterpret_cast<const float4*>(rk.sin_t + (int64_t)pos * half + j);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 cv = c4[i], sv = s4[i];
-        cs[4 * i] = cv.x;
-        cs[4 * i + 1] = cv.y;
-        cs[4 * i + 2] = cv.z;
-        cs[4 * i + 3] = cv.w;
-        sn[4 * i] = sv.x;
-        sn[4 * i + 1] = sv.y;
-        sn[4 * i + 2] = sv.z;
-        sn[4 * i + 3] = sv.w;
-      }
-    }
 #pragma unroll 1
     for (int hc = half_warps * dh; hc < BN; hc += 2 * dh) {
       const int head = (n0 + hc) / dh;
-      float a[32], b[32];
-      tmem_ld32(base + hc + j, a);
-      tmem_ld32(base + hc + half + j, b);
-      if (!live) continue;
-      uint32_t w1[16], w2[16];
-      __nv_bfloat16* dst;
-      if (head < rk.hq + rk.hkv) {
+      const bool rotate = head < rk.hq + rk.hkv;
+      uint32_t w[32];  // words 0-15: columns j.. of the first half, 16-31: of the second
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float r1[2], r2[2];
+      for (int sub = 0; sub < 2; ++sub) {  // 16 columns of each half at a time
+        float a[16], b[16];
+        tmem_ld16(base + hc + j + 16 * sub, a);
+        tmem_ld16(base + hc + half + j + 16 * sub, b);
+        if (rotate) {
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int k = 2 * i + e;
-            const float p = __bfloat162float(__float2bfloat16_rn(a[k]));
-            const float q = __bfloat162float(__float2bfloat16_rn(b[k]));
-            r1[e] = p * cs[k] - q * sn[k];
-            r2[e] = q * cs[k] + p * sn[k];
+          for (int i4 = 0; i4 < 4; ++i4) {
+            const int c = j + 16 * sub + 4 * i4;
+            float4 cv = make_float4(0.f, 0.f, 0.f, 0.f), sv = cv;
+            if (live) {
+              cv = *reinterpret_cast<const float4*>(cos_row + c);
+              sv = *reinterpret_cast<const float4*>(sin_row + c);
+            }
+            const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+            float r1[4], r2[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float p = __bfloat162float(__float2bfloat16_rn(a[4 * i4 + e]));
+              const float q = __bfloat162float(__float2bfloat16_rn(b[4 * i4 + e]));
+              r1[e] = p * cc[e] - q * ss[e];
+              r2[e] = q * cc[e] + p * ss[e];
+            }
+            const int wi = 8 * sub + 2 * i4;
+            w[wi] = pack_bf16(r1[0], r1[1]);
+            w[wi + 1] = pack_bf16(r1[2], r1[3]);
+            w[16 + wi] = pack_bf16(r2[0], r2[1]);
+            w[16 + wi + 1] = pack_bf16(r2[2], r2[3]);
           }
-          w1[i] = pack_bf16(r1[0], r1[1]);
-          w2[i] = pack_bf16(r2[0], r2[1]);
-        }
-        if (head < rk.hq) {
-          dst = qkv + (int64_t)m * ldc + n0 + hc + j;
         } else {
-          if (!slot_ok) {
-            raise_device_error(err, kErrSlot);
-            continue;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            w[8 * sub + i] = pack_bf16(a[2 * i], a[2 * i + 1]);
+            w[16 + 8 * sub + i] = pack_bf16(b[2 * i], b[2 * i + 1]);
           }
-          dst = rk.kpool + (((int64_t)blk * rk.hkv + (head - rk.hq)) * rk.bs + off) * dh + j;
         }
-      } else {
-        if (!slot_ok) {
-          raise_device_error(err, kErrSlot);
-          continue;
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          w1[i] = pack_bf16(a[2 * i], a[2 * i + 1]);
-          w2[i] = pack_bf16(b[2 * i], b[2 * i + 1]);
-        }
-        dst = rk.vpool + (((int64_t)blk * rk.hkv + (head - rk.hq - rk.hkv)) * rk.bs + off) * dh + j;
       }
-      uint4* d1 = reinterpret_cast<uint4*>(dst);
-      uint4* d2 = reinterpret_cast<uint4*>(dst + half);
+      if (live && head >= rk.hq && !slot_ok) raise_device_error(err, kErrSlot);
+      stage_row(buf, lane, w);
+      __syncwarp();
+      const int jj = lane & 7;
+      // chunks 0-3: columns j + 8 jj of the first half; 4-7: the second half
+      const int col = jj < 4 ? j + 8 * jj : half + j + 8 * (jj - 4);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        d1[i] = make_uint4(w1[4 * i], w1[4 * i + 1], w1[4 * i + 2], w1[4 * i + 3]);
-        d2[i] = make_uint4(w2[4 * i], w2[4 * i + 1], w2[4 * i + 2], w2[4 * i + 3]);
+      for (int i = 0; i < 8; ++i) {
+        const int r = 4 * i + (lane >> 3);
+        const uint4 x = staged_chunk(buf, r, jj);
+        const int slot_r = __shfl_sync(0xffffffffu, slot, r);
+        const int mr = row0 + r;
+        if (mr >= M) continue;
+        __nv_bfloat16* dst;
+        if (head < rk.hq) {
+          dst = qkv + (int64_t)mr * ldc + n0 + hc + col;
+        } else {
+          const int blk = slot_r >= 0 ? slot_r / rk.bs : 0;
+          if (slot_r < 0 || blk >= rk.num_blocks) continue;
+          const int off = slot_r - blk * rk.bs;
+          const bool is_k = head < rk.hq + rk.hkv;
+          const int kh = head - rk.hq - (is_k ? 0 : rk.hkv);
+          dst = (is_k ? rk.kpool : rk.vpool) +
+                (((int64_t)blk * rk.hkv + kh) * rk.bs + off) * dh + col;
+        }
+        *reinterpret_cast<uint4*>(dst) = x;
       }
+      __syncwarp();
     }
   }
 }
@@ -547,8 +565,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row0 = m0 + row_group * 32;
       const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
       if constexpr (EPI == kEpiRopeKV) {
-        rope_kv_row<BN>(base, row0 + lane, M, n0, half, rk, reinterpret_cast<__nv_bfloat16*>(C),
-                        ldc, err);
+        rope_kv_rows<BN>(base, buf, lane, row0, M, n0, half, rk,
+                         reinterpret_cast<__nv_bfloat16*>(C), ldc, err);
       } else {
         epilogue_tile<BN, EPI, TC>(base, buf, lane, half, row0, M, n0, ldc, static_cast<TC*>(C), R,
                                    reduce);
