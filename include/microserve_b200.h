@@ -318,16 +318,16 @@ MS_API int ms_gemm(const void* A, const void* B, void* C, const float* R, int M,
             int N, int K, int64_t ldc, int ab_dtype, int c_dtype,
             int epilogue, void* stream);
 
-/* Scratch bytes the tensor-core attention would use for split-KV partials on
- * this batch.  ms_forward uses workspace bytes past
- * ms_forward_workspace_size() for them; with fewer it runs one KV range per
- * tile (same results, less parallelism).  No reference counterpart. */
 /* Which tensor-core GEMM ms_gemm and ms_forward use: 0 = chosen by shape
  * (the default), 1 = one CTA per 128 x 256 tile, 2 = CTA pairs on two SMs
  * (tcgen05 cta_group::2, 256 x 256 tiles) wherever the shape allows.  No
  * reference counterpart: a switch for measurements and tests.  Process-wide. */
 MS_API int ms_gemm_set_policy(int policy);
 
+/* Scratch bytes the tensor-core attention would use for split-KV partials on
+ * this batch.  ms_forward uses workspace bytes past
+ * ms_forward_workspace_size() for them; with fewer it runs one KV range per
+ * tile (same results, less parallelism).  No reference counterpart. */
 MS_API size_t ms_attention_scratch_size(const ms_kv_cache* cache, int n_heads,
                                         const ms_batch* batch);
 

@@ -256,9 +256,22 @@ __device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int l
 #pragma unroll
       for (int k = 0; k < 32; ++k) w[k] = __float_as_uint(v[k]);
     }
+    const int j = lane & 7;
+    // the residual rows this lane adds, all loads issued before the exchange
+    float4 res[EPI == kEpiResidual ? 8 : 1];
+    if constexpr (EPI == kEpiResidual) {
+      if (!reduce) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int m = row0 + 4 * i + (lane >> 3);
+          res[i] = m < M ? *reinterpret_cast<const float4*>(R + (int64_t)m * ldc + n0 + u * U +
+                                                            4 * j)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
     stage_row(buf, lane, w);
     __syncwarp();
-    const int j = lane & 7;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int r = 4 * i + (lane >> 3);
@@ -277,7 +290,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int l
         if (reduce) {
           red_add4(out, a.x, a.y, a.z, a.w);
         } else {
-          const float4 r4 = *reinterpret_cast<const float4*>(R + off);
+          const float4 r4 = res[i];
           *reinterpret_cast<float4*>(out) =
               make_float4(r4.x + a.x, r4.y + a.y, r4.z + a.z, r4.w + a.w);
         }
