@@ -30,8 +30,11 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // (griddepcontrol.launch_dependents).  Launched with launch_pdl, a kernel's
 // CTAs are scheduled while its predecessor's last CTAs still run and start
 // the moment it completes, so back-to-back launches lose no launch latency.
-// Nothing is read or written before the wait, so ordering is the stream's.
-// Launched without the attribute, the wait returns at once.
+// Nothing the previous kernels write is read or written before the wait, so
+// ordering is the stream's.  (The tcgen05 GEMM calls it after its CTA-local
+// setup -- barriers, TMEM -- and, for constant weights, after issuing its
+// first weight tiles.)  Launched without the attribute, the wait returns at
+// once.
 __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");

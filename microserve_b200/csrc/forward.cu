@@ -120,10 +120,11 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
                       hkv, dh, c.block_size, c.num_blocks,
                       static_cast<__nv_bfloat16*>(c.k_pool[l]),
                       static_cast<__nv_bfloat16*>(c.v_pool[l])};
-      rc = gemm_qkv_rope(w.xn, m.w_qkv[l], w.qkv, T, qkv_w, d, rk, s);
+      rc = gemm_qkv_rope(w.xn, m.w_qkv[l], w.qkv, T, qkv_w, d, rk, s, true);
     }
     if (rc == MS_ERR_UNSUPPORTED) {
-      MS_TRY(gemm_dispatch(w.xn, m.w_qkv[l], w.qkv, nullptr, T, qkv_w, d, 0, dt, dt, kEpiStore, s));
+      MS_TRY(gemm_dispatch(w.xn, m.w_qkv[l], w.qkv, nullptr, T, qkv_w, d, 0, dt, dt, kEpiStore, s,
+                           true));
       MS_TRY(rope_kv_write(w.qkv, bt.positions, bt.slot_mapping, m.rope_cos, m.rope_sin,
                            m.max_seq_len, T, hq, hkv, dh, c, l, dt, s));
     } else {
@@ -133,12 +134,12 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
     MS_TRY(paged_attention(w.qkv, qkv_w, c, l, bt, hq, w.attn, attn_scratch, attn_scratch_bytes,
                            s, order));
     MS_TRY(gemm_dispatch(w.attn, m.w_o[l], w.x, w.x, T, d, hq * dh, 0, dt, MS_DTYPE_F32,
-                         kEpiResidual, s));
+                         kEpiResidual, s, true));
     MS_TRY(rmsnorm(w.x, m.ffn_norm[l], w.xn, nullptr, T, d, m.norm_eps, dt, s));
     MS_TRY(gemm_dispatch(w.xn, m.w_gate_up[l], w.h, nullptr, T, 2 * m.d_ff, d, 0, dt, dt,
-                         kEpiSwiGLU, s));
+                         kEpiSwiGLU, s, true));
     MS_TRY(gemm_dispatch(w.h, m.w_down[l], w.x, w.x, T, d, m.d_ff, 0, dt, MS_DTYPE_F32,
-                         kEpiResidual, s));
+                         kEpiResidual, s, true));
     if (l + 1 < m.n_layers)
       MS_TRY(rmsnorm(w.x, m.attn_norm[l + 1], w.xn, nullptr, T, d, m.norm_eps, dt, s));
   }
@@ -147,5 +148,5 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
   MS_REQUIRE(logits_row_stride == 0 || logits_row_stride >= m.vocab_size,
              "ms_forward: logits_row_stride < vocab");
   return gemm_dispatch(w.xl, m.embed, logits, nullptr, R, m.vocab_size, d, logits_row_stride, dt,
-                       MS_DTYPE_F32, kEpiStore, s);
+                       MS_DTYPE_F32, kEpiStore, s, true);
 }

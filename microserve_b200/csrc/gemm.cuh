@@ -24,18 +24,22 @@ struct RopeKv {
 // The qkv GEMM with RoPE and the cache write in its epilogue (bf16, d_head 64
 // or 128, tensor-core shapes): replaces gemm_dispatch(kEpiStore) followed by
 // rope_kv_write.  Returns MS_ERR_UNSUPPORTED when the shape does not apply.
+// weights_const: W is never written by the kernels before it (model weights),
+// so its first tiles may be loaded before the previous launch completes.
 int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, const RopeKv& rk,
-                  cudaStream_t s);
+                  cudaStream_t s, bool weights_const = false);
 
 // C = A[M,K] * B[N,K]^T; picks the tensor-core kernel when it applies.
 // C and R rows are ldc elements apart (ldc >= output columns).
+// weights_const as for gemm_qkv_rope, for B.
 int gemm_dispatch(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-                  int64_t ldc, int ab_dtype, int c_dtype, int epi, cudaStream_t s);
+                  int64_t ldc, int ab_dtype, int c_dtype, int epi, cudaStream_t s,
+                  bool weights_const = false);
 int gemm_simt(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
               int64_t ldc, int ab_dtype, int c_dtype, int epi, cudaStream_t s);
 // tcgen05 bf16 kernel (gemm_tc.cu).
 bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi);
 int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-            int64_t ldc, int c_dtype, int epi, cudaStream_t s);
+            int64_t ldc, int c_dtype, int epi, cudaStream_t s, bool weights_const = false);
 
 }  // namespace ms

@@ -111,7 +111,8 @@ int gemm_simt(const void* A, const void* B, void* C, const float* R, int M, int 
 }
 
 int gemm_dispatch(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-                  int64_t ldc, int ab_dtype, int c_dtype, int epi, cudaStream_t s) {
+                  int64_t ldc, int ab_dtype, int c_dtype, int epi, cudaStream_t s,
+                  bool weights_const) {
   if (M == 0 || N == 0) return MS_OK;
   if (epi == kEpiSwiGLU && (N % 16) != 0)
     return fail(MS_ERR_UNSUPPORTED, "gemm: SwiGLU needs N %% 16 == 0 (got %d)", N);
@@ -121,7 +122,7 @@ int gemm_dispatch(const void* A, const void* B, void* C, const float* R, int M, 
                                   (long long)out_cols);
   ProfScope prof(kClsGemm, s);
   if (ab_dtype == MS_DTYPE_BF16 && gemm_tc_supported(M, N, K, ldc, c_dtype, epi))
-    return gemm_tc(A, B, C, R, M, N, K, ldc, c_dtype, epi, s);
+    return gemm_tc(A, B, C, R, M, N, K, ldc, c_dtype, epi, s, weights_const);
   return gemm_simt(A, B, C, R, M, N, K, ldc, ab_dtype, c_dtype, epi, s);
 }
 

@@ -458,8 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
                    const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
-                   int* err, const RopeKv rk) {
-  pdl_enter();
+                   int* err, const RopeKv rk, int b_const) {
   using Cfg = TileCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -505,6 +504,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   sched.init(tiles, kiters, stream_k != 0);
   int tile, k0, k1;
 
+  // Everything above touches only this CTA's shared memory and TMEM, so it
+  // ran before the wait for the previous kernel (programmatic dependent
+  // launch).  When B is constant (model weights), the first stages' B tiles
+  // are loaded before the wait too: a CTA placed on an SM while the previous
+  // kernel's last CTAs still run elsewhere starts with its weights in flight.
+  uint32_t npre = 0;
+  if (b_const && warp == 0 && lane == 0) {
+    Schedule pre = sched;
+    int pt, pk0, pk1;
+    while (npre < (uint32_t)S && pre.next(pt, pk0, pk1)) {
+      const int pn0 = (pt / mt) * BN;
+      for (int k = pk0; k < pk1 && npre < (uint32_t)S; ++k, ++npre) {
+        const uint32_t dst = sbase + npre * Cfg::kStageBytes;
+        mbar_expect_tx(full0 + 8 * npre, Cfg::kStageBytes);
+        tma_load_2d(dst + Cfg::kABytes, &tmap_b, full0 + 8 * npre, k * BK, pn0);
+      }
+    }
+  }
+  pdl_enter();
+
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer ----
@@ -520,9 +539,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t a_dst = sbase + s * Cfg::kStageBytes;
-          mbar_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
+          if (q >= npre) {  // the first npre stages already hold their B tile
+            mbar_expect_tx(full0 + 8 * s, Cfg::kStageBytes);
+            tma_load_2d(a_dst + Cfg::kABytes, &tmap_b, full0 + 8 * s, k * BK, n0);
+          }
           tma_load_2d(a_dst, &tmap_a, full0 + 8 * s, k * BK, m0);
-          tma_load_2d(a_dst + Cfg::kABytes, &tmap_b, full0 + 8 * s, k * BK, n0);
         }
       }
       if (*abort_flag) {  // drain this thread's loads before leaving
@@ -899,7 +920,8 @@ int tensor_map(const void* ptr, int rows, int cols, int box_rows, CUtensorMap* o
 
 template <int BN, int EPI, typename TC>
 int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-              int64_t ldc, bool stream_k, cudaStream_t s, const RopeKv& rk = RopeKv{}) {
+              int64_t ldc, bool stream_k, cudaStream_t s, const RopeKv& rk = RopeKv{},
+              bool b_const = false) {
   CUtensorMap ta, tb;
   MS_TRY(tensor_map(A, M, K, BM, &ta));
   MS_TRY(tensor_map(B, N, K, BN, &tb));
@@ -921,7 +943,7 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
                       : std::min(tiles, kNumSMs);
   if (grid < 1) grid = 1;
   launch_pdl(kern, grid, kThreads, Cfg::kSmem, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-                                          stream_k ? 1 : 0, device_error_word(), rk);
+             stream_k ? 1 : 0, device_error_word(), rk, b_const ? 1 : 0);
   return check_launch("gemm_tc_kernel");
 }
 
@@ -997,15 +1019,16 @@ bool use_bn256(int M, int N, bool stream_k) {
 
 template <int EPI, typename TC>
 int launch_any(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-               int64_t ldc, bool stream_k, cudaStream_t s) {
-  if (use_bn256(M, N, stream_k)) return launch_tc<256, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s);
-  return launch_tc<128, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s);
+               int64_t ldc, bool stream_k, cudaStream_t s, bool b_const) {
+  if (use_bn256(M, N, stream_k))
+    return launch_tc<256, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s, RopeKv{}, b_const);
+  return launch_tc<128, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s, RopeKv{}, b_const);
 }
 
 }  // namespace
 
 int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, const RopeKv& rk,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool weights_const) {
   if ((rk.dh != 64 && rk.dh != 128) || N != (rk.hq + 2 * rk.hkv) * rk.dh ||
       !gemm_tc_supported(M, N, K, N, MS_DTYPE_BF16, kEpiStore) ||
       ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(W) |
@@ -1013,8 +1036,10 @@ int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, 
     return MS_ERR_UNSUPPORTED;
   ProfScope prof(kClsGemm, s);
   if (use_bn256(M, N, false))
-    return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk);
-  return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk);
+    return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk,
+                                                     weights_const);
+  return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk,
+                                                   weights_const);
 }
 
 bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi) {
@@ -1025,7 +1050,7 @@ bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi) {
 }
 
 int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K, int64_t ldc,
-            int c_dtype, int epi, cudaStream_t s) {
+            int c_dtype, int epi, cudaStream_t s, bool weights_const) {
   if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B) |
        reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
@@ -1041,7 +1066,8 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
     if (c_dtype == MS_DTYPE_F32) return launch_tc2<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
     return launch_tc2<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
   }
-  if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+  if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s,
+                                                          weights_const);
   if (epi == kEpiResidual) {
     // In place (C += A B^T): stream-K with reductions into C, unless there is
     // at least one 256-wide tile per SM and A + B overflow L2.  Stream-K
@@ -1053,10 +1079,12 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
     const double ab_bytes = 2.0 * ((double)M + (double)N) * (double)K;
     const bool stream_k =
         in_place && (N % 256 != 0 || tiles256 < kNumSMs || ab_bytes <= 64.0 * (1 << 20));
-    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s);
+    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s,
+                                           weights_const);
   }
-  if (c_dtype == MS_DTYPE_F32) return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
-  return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+  if (c_dtype == MS_DTYPE_F32)
+    return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
+  return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
 }
 
 }  // namespace ms
