@@ -705,8 +705,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
                     const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
-                    int* err) {
-  pdl_enter();
+                    int* err, int b_const) {
   constexpr int S = kStages2;
   constexpr int BN = kBN2;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -754,6 +753,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   sched.init(tiles, kiters, stream_k != 0, gridDim.x / 2, blockIdx.x / 2);
   int tile, k0, k1;
 
+  // As in the 1-SM kernel: the setup above ran before the wait for the
+  // previous kernel, and with constant weights so do the first stages' B
+  // loads (both CTAs walk the same schedule, so npre agrees; the leader
+  // posts each stage's byte count).
+  uint32_t npre = 0;
+  if (b_const && warp == 0 && lane == 0) {
+    const uint32_t leader_full0 = cluster_addr(full0, 0);
+    Schedule pre = sched;
+    int pt, pk0, pk1;
+    while (npre < (uint32_t)S && pre.next(pt, pk0, pk1)) {
+      const int pn0 = (pt / mt) * BN + (int)rank * (BN / 2);
+      for (int k = pk0; k < pk1 && npre < (uint32_t)S; ++k, ++npre) {
+        const uint32_t dst = sbase + npre * kStage2;
+        if (rank == 0) mbar_expect_tx(full0 + 8 * npre, 2 * kStage2);
+        tma_load_2d_pair(dst + kHalf2, &tmap_b, leader_full0 + 8 * npre, k * BK, pn0);
+      }
+    }
+  }
+  pdl_enter();
+
   if (warp == 0) {
     if (lane == 0) {
       // ---- TMA producer (both CTAs) ----
@@ -771,9 +790,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           const uint32_t dst = sbase + s * kStage2;
-          if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * kStage2);
+          if (q >= npre) {  // the first npre stages already hold their B halves
+            if (rank == 0) mbar_expect_tx(full0 + 8 * s, 2 * kStage2);
+            tma_load_2d_pair(dst + kHalf2, &tmap_b, leader_full0 + 8 * s, k * BK, n0);
+          }
           tma_load_2d_pair(dst, &tmap_a, leader_full0 + 8 * s, k * BK, m0);
-          tma_load_2d_pair(dst + kHalf2, &tmap_b, leader_full0 + 8 * s, k * BK, n0);
         }
       }
       if (*abort_flag && rank == 0) {  // every load of the pair completes on these barriers
@@ -949,7 +970,7 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
 
 template <int EPI, typename TC>
 int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-               int64_t ldc, bool stream_k, cudaStream_t s) {
+               int64_t ldc, bool stream_k, cudaStream_t s, bool b_const) {
   CUtensorMap ta, tb;
   MS_TRY(tensor_map(A, M, K, BM, &ta));
   MS_TRY(tensor_map(B, N, K, kBN2 / 2, &tb));
@@ -986,7 +1007,7 @@ int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int
                        : std::min(tiles, pairs_max);
   if (pairs < 1) pairs = 1;
   launch_pdl(kern, 2 * pairs, kThreads, kSmem2, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-             stream_k ? 1 : 0, device_error_word());
+             stream_k ? 1 : 0, device_error_word(), b_const ? 1 : 0);
   return check_launch("gemm_tc2_kernel");
 }
 
@@ -995,10 +1016,11 @@ int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int
 int g_gemm_policy = 0;
 
 // CTA pairs by shape: the wide store GEMMs (the lm_head: 1280 x 32000 x 2048
-// 170 -> 151 us, 256 x 32000 x 2048 49 -> 45 us).  Elsewhere the pairs
-// measured no faster (1280 x 11264 x 2048 SwiGLU 51.6 us both) or slower
-// (stream-K residual, qkv, M = 256 projections): halving the bytes each SM
-// loads per k-step does not move GEMMs that run at the power-capped clock.
+// 140 -> 128 us, 256 x 32000 x 2048 40 -> 37 us with the staged epilogue).
+// The verify-sized SwiGLU GEMM is 3% faster alone on pairs (1280 x 11264 x
+// 2048: 44.0 -> 42.6 us) but a round was not (6.29 against 6.27 ms);
+// elsewhere the pairs measured slower (stream-K residual pieces twice as
+// large on half as many workers, qkv, the M = 256 projections).
 bool use_pairs(int M, int N, int epi) {
   if (g_gemm_policy == 1 || epi == kEpiRopeKV || N % kBN2 != 0) return false;
   if (g_gemm_policy == 2) return true;
@@ -1055,16 +1077,20 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
        reinterpret_cast<uintptr_t>(C)) & 15)
     return fail(MS_ERR_INVALID, "gemm_tc: operands must be 16-byte aligned");
   if (use_pairs(M, N, epi)) {
-    if (epi == kEpiSwiGLU) return launch_tc2<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+    if (epi == kEpiSwiGLU)
+      return launch_tc2<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s,
+                                                   weights_const);
     if (epi == kEpiResidual) {
       const bool in_place = static_cast<const void*>(R) == C;
       const int tiles2 = ((M + 2 * BM - 1) / (2 * BM)) * (N / kBN2);
       const double ab_bytes = 2.0 * ((double)M + (double)N) * (double)K;
       const bool stream_k = in_place && (tiles2 < kNumSMs / 2 || ab_bytes <= 64.0 * (1 << 20));
-      return launch_tc2<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s);
+      return launch_tc2<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s,
+                                            weights_const);
     }
-    if (c_dtype == MS_DTYPE_F32) return launch_tc2<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s);
-    return launch_tc2<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s);
+    if (c_dtype == MS_DTYPE_F32)
+      return launch_tc2<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
+    return launch_tc2<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
   }
   if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s,
                                                           weights_const);
