@@ -222,7 +222,9 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
   const int split = blockIdx.x % a.n_splits, rt = blockIdx.x / a.n_splits;
   const int g = blockIdx.y, b = a.seq_order ? a.seq_order[blockIdx.z] : blockIdx.z;
   const int group = a.hq / a.hkv;
+  // independent loads issued together: the query range, the context length
   const int t0 = a.q_start[b], qlen = a.q_start[b + 1] - t0;
+  const int ctx_len = a.context_lens[b];
   const int nrows = qlen * group;
   const int r0 = rt * kRows;
   if (r0 >= nrows) return;
@@ -232,6 +234,18 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
     return;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The producer's first block-table slice, read while the row positions
+  // load (its start depends only on the split): no extra round trip later.
+  const int32_t* table = a.tables + (int64_t)b * a.max_blocks;
+  const int first_blk = (split * a.split_len) >> a.log2_bs;
+  int tbl_pre[kTblCap / 32];
+  if (warp == NW) {
+#pragma unroll
+    for (int j = 0; j < kTblCap / 32; ++j) {
+      const int i = first_blk + lane + 32 * j;
+      tbl_pre[j] = i < a.max_blocks ? table[i] : 0;
+    }
+  }
 
   for (int r = threadIdx.x; r < kRows; r += Cfg::kThreads)
     rowpos[r] = r < nr ? a.positions[t0 + (r0 + r) / group] : -1;
@@ -248,16 +262,6 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
   // values (their probabilities are 0, and 0 * NaN would poison O).
   for (int i = threadIdx.x; i < S * Cfg::kStageBytes / 16; i += Cfg::kThreads)
     reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
-  // Q tile (zero rows past nr).
-  for (int idx = threadIdx.x; idx < Cfg::kQRows * (DH / 8); idx += Cfg::kThreads) {
-    const int r = idx / (DH / 8), c = (idx % (DH / 8)) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nr) {
-      const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
-      v = *reinterpret_cast<const uint4*>(a.q + (int64_t)(t0 + t) * a.q_stride + h * DH + c);
-    }
-    *reinterpret_cast<uint4*>(Qs + r * LDQ + c) = v;
-  }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // zeros before TMA writes
   __syncthreads();
 
@@ -266,7 +270,7 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
     kmax = max(kmax, rowpos[r] + 1);
     minpos = min(minpos, rowpos[r]);
   }
-  kmax = min(kmax, a.context_lens[b]);
+  kmax = min(kmax, ctx_len);
   const int splits_here = max(1, (kmax + a.split_len - 1) / a.split_len);
   if (split >= splits_here) return;
   const int kbeg = split * a.split_len;
@@ -277,17 +281,18 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
 
   if (warp == NW) {
     // ---- producer: block-table slice staged in smem, one lane issues TMA ----
-    const int32_t* table = a.tables + (int64_t)b * a.max_blocks;
     const int bpc = CH >> a.log2_bs;  // blocks per chunk
-    const int first_blk = kbeg >> a.log2_bs;
     const int n_blk = (kend - kbeg + a.bs - 1) >> a.log2_bs;
     int issued = 0;
     bool stop = false;
     for (int base = 0; base < n_blk && !stop; base += kTblCap) {
       const int cnt = min(kTblCap, n_blk - base);
       __syncwarp();
-      for (int i = lane; i < cnt; i += 32) {
-        int blk = table[first_blk + base + i];
+#pragma unroll
+      for (int j = 0; j < kTblCap / 32; ++j) {
+        const int i = lane + 32 * j;
+        if (i >= cnt) break;
+        int blk = base == 0 ? tbl_pre[j] : table[first_blk + base + i];
         if (blk < 0 || blk >= a.num_blocks) {
           atomicCAS(a.err, 0, (int)kErrBlock);
           blk = 0;
@@ -338,6 +343,21 @@ __global__ void __launch_bounds__(TmaCfg<DH, KW, NWARPS, NSTAGES, CHK>::kThreads
   const int ra = wr + (lane >> 2), rb = ra + 8;
   const int pos_a = rowpos[ra], pos_b = rowpos[rb];
   const bool live = wr < nr;
+  // The Q rows of this warp's m-tile (zero past nr), loaded while the
+  // producer's first TMA loads are already in flight: only this warp reads
+  // them (warps that share an m-tile write the same bytes).
+  if (live) {
+    for (int idx = lane; idx < 16 * (DH / 8); idx += 32) {
+      const int r = wr + idx / (DH / 8), c = (idx % (DH / 8)) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < nr) {
+        const int rr = r0 + r, t = rr / group, h = g * group + rr % group;
+        v = *reinterpret_cast<const uint4*>(a.q + (int64_t)(t0 + t) * a.q_stride + h * DH + c);
+      }
+      *reinterpret_cast<uint4*>(Qs + r * LDQ + c) = v;
+    }
+    __syncwarp();
+  }
   float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
   float o[NT][4];
 #pragma unroll
