@@ -317,24 +317,56 @@ __device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int l
 // lane quarter take alternate heads (`half_warps` 0 or 1).  Each head's
 // 32-column slice pair (128 bytes of bf16 per row) goes through the warp's
 // exchange buffer, so the stores cover whole row segments.
+// What the epilogue of one row needs before its accumulator is ready: the
+// row's position and cache slot, and (d_head 64) its 32 cos/sin pairs, read
+// while the MMAs still run.  Loading the cos/sin per 16 columns after each
+// TMEM load made every step wait a full L2 round trip (a 1280 x 2560 verify
+// qkv epilogue took 7.7 us).
+struct RopeRow {
+  int pos, slot;
+  float cs[32], sn[32];
+};
+__device__ __forceinline__ void rope_row_load(const RopeKv& rk, int m, int M, int* err,
+                                              RopeRow& r) {
+  r.pos = 0;
+  r.slot = -1;
+  if (m < M) {
+    r.pos = rk.positions[m];
+    if (r.pos < 0 || r.pos >= rk.max_pos) {
+      raise_device_error(err, kErrPosition);
+      r.pos = 0;
+    }
+    r.slot = rk.slots[m];
+  }
+  if (rk.dh == 64) {
+    const float4* c4 = reinterpret_cast<const float4*>(rk.cos_t + (int64_t)r.pos * 32);
+    const float4* s4 = reinterpret_cast<const float4*>(rk.sin_t + (int64_t)r.pos * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 c = c4[i], sv = s4[i];
+      r.cs[4 * i] = c.x;
+      r.cs[4 * i + 1] = c.y;
+      r.cs[4 * i + 2] = c.z;
+      r.cs[4 * i + 3] = c.w;
+      r.sn[4 * i] = sv.x;
+      r.sn[4 * i + 1] = sv.y;
+      r.sn[4 * i + 2] = sv.z;
+      r.sn[4 * i + 3] = sv.w;
+    }
+  }
+}
+
 template <int BN>
 __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int lane, int row0,
                                              int M, int n0, int half_warps, const RopeKv& rk,
-                                             __nv_bfloat16* qkv, int64_t ldc, int* err) {
+                                             __nv_bfloat16* qkv, int64_t ldc, int* err,
+                                             const RopeRow& rr) {
   const int dh = rk.dh, half = dh >> 1;
   const int m = row0 + lane;
   const bool live = m < M;
-  int pos = 0, slot = -1;
-  if (live) {
-    pos = rk.positions[m];
-    if (pos < 0 || pos >= rk.max_pos) {
-      raise_device_error(err, kErrPosition);
-      pos = 0;
-    }
-    slot = rk.slots[m];
-  }
+  const int pos = rr.pos, slot = rr.slot;
   const bool slot_ok = slot >= 0 && slot / rk.bs < rk.num_blocks;
-  // cos/sin of the row's position, read as float4 (L1-resident) per head
+  // d_head 128: cos/sin of the row's position read as float4 per head
   const float* cos_row = rk.cos_t + (int64_t)pos * half;
   const float* sin_row = rk.sin_t + (int64_t)pos * half;
 #pragma unroll 1
@@ -343,9 +375,12 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
     for (int hc = half_warps * dh; hc < BN; hc += 2 * dh) {
       const int head = (n0 + hc) / dh;
       const bool rotate = head < rk.hq + rk.hkv;
-      uint32_t w[32];  // words 0-15: columns j.. of the first half, 16-31: of the second
 #pragma unroll
       for (int sub = 0; sub < 2; ++sub) {  // 16 columns of each half at a time
+        // words 0-7: columns j + 16 sub .. of the first half, 8-15: of the
+        // second; they go to the row's exchange chunks 2 sub, 2 sub + 1 and
+        // 4 + 2 sub, 5 + 2 sub
+        uint32_t w[16];
         float a[16], b[16];
         tmem_ld16(base + hc + j + 16 * sub, a);
         tmem_ld16(base + hc + half + j + 16 * sub, b);
@@ -353,10 +388,18 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
 #pragma unroll
           for (int i4 = 0; i4 < 4; ++i4) {
             const int c = j + 16 * sub + 4 * i4;
-            float4 cv = make_float4(0.f, 0.f, 0.f, 0.f), sv = cv;
-            if (live) {
-              cv = *reinterpret_cast<const float4*>(cos_row + c);
-              sv = *reinterpret_cast<const float4*>(sin_row + c);
+            float4 cv, sv;
+            if (half == 32) {  // preloaded (j is 0)
+              const int k = 16 * sub + 4 * i4;
+              cv = make_float4(rr.cs[k], rr.cs[k + 1], rr.cs[k + 2], rr.cs[k + 3]);
+              sv = make_float4(rr.sn[k], rr.sn[k + 1], rr.sn[k + 2], rr.sn[k + 3]);
+            } else {
+              cv = make_float4(0.f, 0.f, 0.f, 0.f);
+              sv = cv;
+              if (live) {
+                cv = *reinterpret_cast<const float4*>(cos_row + c);
+                sv = *reinterpret_cast<const float4*>(sin_row + c);
+              }
             }
             const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
             float r1[4], r2[4];
@@ -367,22 +410,27 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
               r1[e] = p * cc[e] - q * ss[e];
               r2[e] = q * cc[e] + p * ss[e];
             }
-            const int wi = 8 * sub + 2 * i4;
-            w[wi] = pack_bf16(r1[0], r1[1]);
-            w[wi + 1] = pack_bf16(r1[2], r1[3]);
-            w[16 + wi] = pack_bf16(r2[0], r2[1]);
-            w[16 + wi + 1] = pack_bf16(r2[2], r2[3]);
+            w[2 * i4] = pack_bf16(r1[0], r1[1]);
+            w[2 * i4 + 1] = pack_bf16(r1[2], r1[3]);
+            w[8 + 2 * i4] = pack_bf16(r2[0], r2[1]);
+            w[8 + 2 * i4 + 1] = pack_bf16(r2[2], r2[3]);
           }
         } else {
 #pragma unroll
           for (int i = 0; i < 8; ++i) {
-            w[8 * sub + i] = pack_bf16(a[2 * i], a[2 * i + 1]);
-            w[16 + 8 * sub + i] = pack_bf16(b[2 * i], b[2 * i + 1]);
+            w[i] = pack_bf16(a[2 * i], a[2 * i + 1]);
+            w[8 + i] = pack_bf16(b[2 * i], b[2 * i + 1]);
           }
+        }
+        const uint32_t rowb = buf + lane * kStageRowBytes;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (q < 2 ? 2 * sub : 2 + 2 * sub) + q;  // 2s, 2s+1, 4+2s, 5+2s
+          st_shared_v4(rowb + ((chunk ^ (lane & 7)) << 4), w[4 * q], w[4 * q + 1], w[4 * q + 2],
+                       w[4 * q + 3]);
         }
       }
       if (live && head >= rk.hq && !slot_ok) raise_device_error(err, kErrSlot);
-      stage_row(buf, lane, w);
       __syncwarp();
       const int jj = lane & 7;
       // chunks 0-3: columns j + 8 jj of the first half; 4-7: the second half
@@ -592,15 +640,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t seg = 0;
     while (sched.next(tile, k0, k1)) {
       const uint32_t a = seg & 1, u = seg >> 1;
+      const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
+      const int row0 = m0 + row_group * 32;
+      RopeRow rr;
+      if constexpr (EPI == kEpiRopeKV) rope_row_load(rk, row0 + lane, M, err, rr);
       if (!mbar_wait(tfull0 + 8 * a, u & 1, abort_flag, err)) break;
       __syncwarp();
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
-      const int row0 = m0 + row_group * 32;
       const uint32_t base = tmem + a * BN + ((uint32_t)(row_group * 32) << 16);
       if constexpr (EPI == kEpiRopeKV) {
         rope_kv_rows<BN>(base, buf, lane, row0, M, n0, half, rk,
-                         reinterpret_cast<__nv_bfloat16*>(C), ldc, err);
+                         reinterpret_cast<__nv_bfloat16*>(C), ldc, err, rr);
       } else {
         epilogue_tile<BN, EPI, TC>(base, buf, lane, half, row0, M, n0, ldc, static_cast<TC*>(C), R,
                                    reduce);
