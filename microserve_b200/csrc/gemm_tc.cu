@@ -130,8 +130,9 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
                    bar)
                : "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
+// tcgen05.ld of 32 (or 16) columns without the wait: the registers hold the
+// values only after tmem_wait_ld(), so several loads can share one wait.
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -142,12 +143,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
         "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
         "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  tmem_ld32_nowait(taddr, r);
+  tmem_wait_ld();
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// Two 32-column loads, one wait.
+__device__ __forceinline__ void tmem_ld32x2(uint32_t ta, float (&va)[32], uint32_t tb,
+                                            float (&vb)[32]) {
+  uint32_t ra[32], rb[32];
+  tmem_ld32_nowait(ta, ra);
+  tmem_ld32_nowait(tb, rb);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    va[i] = __uint_as_float(ra[i]);
+    vb[i] = __uint_as_float(rb[i]);
+  }
+}
+__device__ __forceinline__ void tmem_ld16_nowait(uint32_t taddr, uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
       "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -155,9 +175,19 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// Two 16-column loads, one wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t ta, float (&va)[16], uint32_t tb,
+                                            float (&vb)[16]) {
+  uint32_t ra[16], rb[16];
+  tmem_ld16_nowait(ta, ra);
+  tmem_ld16_nowait(tb, rb);
+  tmem_wait_ld();
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 16; ++i) {
+    va[i] = __uint_as_float(ra[i]);
+    vb[i] = __uint_as_float(rb[i]);
+  }
 }
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -237,18 +267,19 @@ __device__ __forceinline__ void epilogue_tile(uint32_t base, uint32_t buf, int l
     uint32_t w[32];
     if constexpr (EPI == kEpiSwiGLU) {
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        float v[32];
-        tmem_ld32(base + u * U + 32 * h, v);
-        swiglu16(v, w + 8 * h);
+      for (int h = 0; h < 4; h += 2) {  // two loads per wait
+        float v0[32], v1[32];
+        tmem_ld32x2(base + u * U + 32 * h, v0, base + u * U + 32 * (h + 1), v1);
+        swiglu16(v0, w + 8 * h);
+        swiglu16(v1, w + 8 * (h + 1));
       }
     } else if constexpr (sizeof(TC) == 2) {
+      float v0[32], v1[32];
+      tmem_ld32x2(base + u * U, v0, base + u * U + 32, v1);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float v[32];
-        tmem_ld32(base + u * U + 32 * h, v);
-#pragma unroll
-        for (int k = 0; k < 16; ++k) w[16 * h + k] = pack_bf16(v[2 * k], v[2 * k + 1]);
+      for (int k = 0; k < 16; ++k) {
+        w[k] = pack_bf16(v0[2 * k], v0[2 * k + 1]);
+        w[16 + k] = pack_bf16(v1[2 * k], v1[2 * k + 1]);
       }
     } else {
       float v[32];
@@ -382,8 +413,7 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
         // 4 + 2 sub, 5 + 2 sub
         uint32_t w[16];
         float a[16], b[16];
-        tmem_ld16(base + hc + j + 16 * sub, a);
-        tmem_ld16(base + hc + half + j + 16 * sub, b);
+        tmem_ld16x2(base + hc + j + 16 * sub, a, base + hc + half + j + 16 * sub, b);
         if (rotate) {
 #pragma unroll
           for (int i4 = 0; i4 < 4; ++i4) {
