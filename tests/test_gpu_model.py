@@ -358,3 +358,34 @@ def test_fused_qkv_rope_writes_the_cache(dh: int) -> None:
     from microserve_b200 import _lib
 
     assert _lib.device_error() == 0
+
+
+def test_forward_lm_head_on_cta_pairs_matches_single_ctas() -> None:
+    """With 256 or more logit rows and a vocabulary of 16384 or more, the
+    forward's tied lm_head runs on CTA pairs (tcgen05 cta_group::2) and loads
+    its first weight tiles before the previous launch completes; the logits
+    equal the one-CTA-per-tile kernel's (policy 1) to float32 rounding (the
+    stream-K residual GEMMs add their pieces in a hardware-chosen order, so
+    the two runs' residual streams may differ in the last bits)."""
+    from microserve_b200 import _lib
+    from microserve_b200.config import ModelConfig
+    from microserve_b200.model import Transformer
+
+    cfg = ModelConfig(vocab_size=32000, n_layers=1, d_model=256, n_heads=4, n_kv_heads=2,
+                      d_ff=512, max_seq_len=512, dtype="bfloat16")
+    m = Transformer(cfg, DEV, seed=21)
+    rng = np.random.default_rng(22)
+    prompts = [rng.integers(0, 32000, int(n)).tolist() for n in (150, 90, 70)]  # 310 rows
+    outs = {}
+    for policy in (0, 1):
+        _lib.call("ms_gemm_set_policy", policy)
+        try:
+            cache = new_cache(m, 16, 64)
+            outs[policy] = run(m, cache, [0, 1, 2], prompts, [0, 0, 0])
+        finally:
+            _lib.call("ms_gemm_set_policy", 0)
+    assert outs[0].shape == (310, 32000)
+    assert np.isfinite(outs[0]).all()
+    scale = float(np.abs(outs[1]).max())
+    np.testing.assert_allclose(outs[0], outs[1], rtol=1e-4, atol=1e-4 * scale)
+    assert _lib.device_error() == 0
