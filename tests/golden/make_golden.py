@@ -220,8 +220,11 @@ def _run_engine(target, draft, gamma: int, prompts, budgets, cache_blocks: int,
 def config_fixtures() -> None:
     """Token streams of the reference engine on the character-level configurations
     (config 0: 8 requests, gamma 3; config 2: a 64-request subset of the
-    continuous-batching workload at gamma 1/2/3/5), greedy, random-init weights
-    from ``workloads.init_state``, plus the reference ModelConfig's field names."""
+    continuous-batching workload at gamma 1/2/3/5, and 24 requests of it in a
+    64-block pool where the scheduler preempts between speculative rounds),
+    greedy, random-init weights from ``workloads.init_state``; the reference
+    ModelConfig's field names; top-p tie choices; the scheduler's decisions
+    under memory pressure."""
     import dataclasses
 
     from microserve.config import CacheConfig, ModelConfig
