@@ -20,6 +20,10 @@
 // with red.global.add, so small grids (o_proj/down at 1280 tokens: 80 tiles)
 // keep every SM busy.  Partial sums then land in C in a hardware-chosen
 // order, so those outputs can differ run to run by float rounding.
+// A CTA's setup (barriers, TMEM) and, when B is constant (the forward's
+// weights), its first stages' B loads run before the wait for the previous
+// launch, so a CTA placed while that launch's last CTAs still run starts
+// with its weights in flight.
 // Loads are plain TMA tile loads of this GPU's memory (no multicast).  Every
 // mbarrier wait is bounded (~2 s of SM clock); on expiry the CTA records
 // kErrTimeout in the device error word, drains its own copies, frees its
