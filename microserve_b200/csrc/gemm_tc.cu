@@ -497,27 +497,45 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
 
 // The sequence of (tile, k-begin, k-end) pieces one CTA works on.  Every role
 // of the CTA walks the same sequence.
-struct Schedule {
-  int tiles, kiters, grid, cta;
-  bool stream_k;
-  int64_t it, it_end;  // stream-K: [it, it_end) over tiles * kiters
-  int next_tile;       // round-robin
+// Work modes: kSchedTiles deals whole output tiles round-robin; kSchedStreamK
+// cuts the (tile, k-step) space into equal contiguous ranges; kSchedHybrid
+// deals whole tiles while every worker gets one (the largest multiple of
+// the worker count), then cuts the remaining tiles' k-steps stream-K.
+constexpr int kSchedTiles = 0, kSchedStreamK = 1, kSchedHybrid = 2;
 
-  __device__ void init(int tiles_, int kiters_, bool sk) { init(tiles_, kiters_, sk, gridDim.x, blockIdx.x); }
+struct Schedule {
+  int tiles, kiters, grid, cta, mode;
+  int dp_tiles;        // tiles dealt whole
+  int64_t it, it_end;  // stream-K range over the other tiles' (tile, k-step) space
+  int next_tile;       // round-robin over the whole tiles
+
+  __device__ void init(int tiles_, int kiters_, int mode_) {
+    init(tiles_, kiters_, mode_, gridDim.x, blockIdx.x);
+  }
   // `grid_` workers, this one `cta_` (a CTA, or a CTA pair of the 2-SM kernel)
-  __device__ void init(int tiles_, int kiters_, bool sk, int grid_, int cta_) {
+  __device__ void init(int tiles_, int kiters_, int mode_, int grid_, int cta_) {
     tiles = tiles_;
     kiters = kiters_;
     grid = grid_;
     cta = cta_;
-    stream_k = sk;
-    const int64_t total = (int64_t)tiles * kiters;
-    it = total * cta / grid;
-    it_end = total * (cta + 1) / grid;
+    mode = mode_;
+    dp_tiles = mode == kSchedTiles ? tiles
+                                   : (mode == kSchedHybrid ? (tiles / grid) * grid : 0);
+    const int64_t base = (int64_t)dp_tiles * kiters;
+    const int64_t total = (int64_t)(tiles - dp_tiles) * kiters;
+    it = base + total * cta / grid;
+    it_end = base + total * (cta + 1) / grid;
     next_tile = cta;
   }
   __device__ bool next(int& tile, int& k0, int& k1) {
-    if (stream_k) {
+    if (next_tile < dp_tiles) {
+      tile = next_tile;
+      k0 = 0;
+      k1 = kiters;
+      next_tile += grid;
+      return true;
+    }
+    {
       if (it >= it_end) return false;
       tile = (int)(it / kiters);
       k0 = (int)(it - (int64_t)tile * kiters);
@@ -526,12 +544,6 @@ struct Schedule {
       it = e;
       return true;
     }
-    if (next_tile >= tiles) return false;
-    tile = next_tile;
-    k0 = 0;
-    k1 = kiters;
-    next_tile += grid;
-    return true;
   }
 };
 
@@ -539,7 +551,7 @@ template <int BN, int EPI, typename TC>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                    const __grid_constant__ CUtensorMap tmap_b, TC* __restrict__ C,
-                   const float* __restrict__ R, int M, int N, int K, int64_t ldc, int stream_k,
+                   const float* __restrict__ R, int M, int N, int K, int64_t ldc, int sched_mode,
                    int* err, const RopeKv rk, int b_const) {
   using Cfg = TileCfg<BN>;
   constexpr int S = Cfg::kStages;
@@ -583,7 +595,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   Schedule sched;
-  sched.init(tiles, kiters, stream_k != 0);
+  sched.init(tiles, kiters, sched_mode);
   int tile, k0, k1;
 
   // Everything above touches only this CTA's shared memory and TMEM, so it
@@ -670,9 +682,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_group = warp & 3;  // TMEM lanes 32*row_group .. +31
     const int half = (warp - 2) >> 2;
     const uint32_t buf = sbase + S * Cfg::kStageBytes + 256 + (warp - 2) * kEpiBufBytes;
-    const bool reduce = EPI == kEpiResidual && stream_k;
     uint32_t seg = 0;
     while (sched.next(tile, k0, k1)) {
+      // a piece that is a whole tile has no co-contributor: C = R + acc
+      const bool reduce = EPI == kEpiResidual && (k0 > 0 || k1 < kiters);
       const uint32_t a = seg & 1, u = seg >> 1;
       const int m0 = (tile % mt) * BM, n0 = (tile / mt) * BN;
       const int row0 = m0 + row_group * 32;
@@ -834,7 +847,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
   Schedule sched;
-  sched.init(tiles, kiters, stream_k != 0, gridDim.x / 2, blockIdx.x / 2);
+  sched.init(tiles, kiters, stream_k, gridDim.x / 2, blockIdx.x / 2);
   int tile, k0, k1;
 
   // As in the 1-SM kernel: the setup above ran before the wait for the
@@ -1025,7 +1038,7 @@ int tensor_map(const void* ptr, int rows, int cols, int box_rows, CUtensorMap* o
 
 template <int BN, int EPI, typename TC>
 int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-              int64_t ldc, bool stream_k, cudaStream_t s, const RopeKv& rk = RopeKv{},
+              int64_t ldc, int mode, cudaStream_t s, const RopeKv& rk = RopeKv{},
               bool b_const = false) {
   CUtensorMap ta, tb;
   MS_TRY(tensor_map(A, M, K, BM, &ta));
@@ -1044,11 +1057,11 @@ int launch_tc(const void* A, const void* B, void* C, const float* R, int M, int 
   }
   const int tiles = ((M + BM - 1) / BM) * (N / BN);
   const int kiters = (K + BK - 1) / BK;
-  int grid = stream_k ? (int)std::min<int64_t>((int64_t)tiles * kiters, kNumSMs)
-                      : std::min(tiles, kNumSMs);
+  int grid = mode == kSchedStreamK ? (int)std::min<int64_t>((int64_t)tiles * kiters, kNumSMs)
+                                    : std::min(tiles, kNumSMs);
   if (grid < 1) grid = 1;
   launch_pdl(kern, grid, kThreads, Cfg::kSmem, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-             stream_k ? 1 : 0, device_error_word(), rk, b_const ? 1 : 0);
+             mode, device_error_word(), rk, b_const ? 1 : 0);
   return check_launch("gemm_tc_kernel");
 }
 
@@ -1091,7 +1104,7 @@ int launch_tc2(const void* A, const void* B, void* C, const float* R, int M, int
                        : std::min(tiles, pairs_max);
   if (pairs < 1) pairs = 1;
   launch_pdl(kern, 2 * pairs, kThreads, kSmem2, s, ta, tb, static_cast<TC*>(C), R, M, N, K, ldc,
-             stream_k ? 1 : 0, device_error_word(), b_const ? 1 : 0);
+             stream_k ? kSchedStreamK : kSchedTiles, device_error_word(), b_const ? 1 : 0);
   return check_launch("gemm_tc2_kernel");
 }
 
@@ -1125,10 +1138,10 @@ bool use_bn256(int M, int N, bool stream_k) {
 
 template <int EPI, typename TC>
 int launch_any(const void* A, const void* B, void* C, const float* R, int M, int N, int K,
-               int64_t ldc, bool stream_k, cudaStream_t s, bool b_const) {
-  if (use_bn256(M, N, stream_k))
-    return launch_tc<256, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s, RopeKv{}, b_const);
-  return launch_tc<128, EPI, TC>(A, B, C, R, M, N, K, ldc, stream_k, s, RopeKv{}, b_const);
+               int64_t ldc, int mode, cudaStream_t s, bool b_const) {
+  if (use_bn256(M, N, mode == kSchedStreamK))
+    return launch_tc<256, EPI, TC>(A, B, C, R, M, N, K, ldc, mode, s, RopeKv{}, b_const);
+  return launch_tc<128, EPI, TC>(A, B, C, R, M, N, K, ldc, mode, s, RopeKv{}, b_const);
 }
 
 }  // namespace
@@ -1142,10 +1155,10 @@ int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, 
     return MS_ERR_UNSUPPORTED;
   ProfScope prof(kClsGemm, s);
   if (use_bn256(M, N, false))
-    return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk,
-                                                     weights_const);
-  return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, false, s, rk,
-                                                   weights_const);
+    return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, kSchedTiles,
+                                                     s, rk, weights_const);
+  return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, kSchedTiles, s,
+                                                   rk, weights_const);
 }
 
 bool gemm_tc_supported(int M, int N, int K, int64_t ldc, int c_dtype, int epi) {
@@ -1176,25 +1189,33 @@ int gemm_tc(const void* A, const void* B, void* C, const float* R, int M, int N,
       return launch_tc2<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
     return launch_tc2<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
   }
-  if (epi == kEpiSwiGLU) return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s,
-                                                          weights_const);
+  if (epi == kEpiSwiGLU)
+    return launch_any<kEpiSwiGLU, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, kSchedTiles, s,
+                                                 weights_const);
   if (epi == kEpiResidual) {
-    // In place (C += A B^T): stream-K with reductions into C, unless there is
-    // at least one 256-wide tile per SM and A + B overflow L2.  Stream-K
-    // puts the CTAs at scattered k offsets, so the whole of A and B is live
-    // at once: at M 1536, K 14336 (160 MB) that re-read DRAM ~7 times, while
-    // whole tiles dealt round-robin keep the CTAs near the same k-step.
+    // In place (C += A B^T): stream-K with reductions into C when the tiles
+    // are fewer than the SMs or A + B fit in L2.  Otherwise whole tiles first
+    // (the CTAs stay near the same k-step: stream-K's scattered k offsets
+    // keep the whole of A and B live at once, and at M 1536, K 14336
+    // (160 MB) that re-read DRAM ~7 times), then stream-K over the tiles
+    // left after the last whole wave, whose A and B fit in L2 (8B down, 192
+    // tiles: 195 -> 144 us, the second wave no longer on 44 SMs alone).
     const bool in_place = static_cast<const void*>(R) == C;
     const int tiles256 = ((M + BM - 1) / BM) * (N / 256);
     const double ab_bytes = 2.0 * ((double)M + (double)N) * (double)K;
-    const bool stream_k =
-        in_place && (N % 256 != 0 || tiles256 < kNumSMs || ab_bytes <= 64.0 * (1 << 20));
-    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, stream_k, s,
-                                           weights_const);
+    int mode = kSchedTiles;
+    if (in_place) {
+      if (N % 256 != 0 || tiles256 < kNumSMs || ab_bytes <= 64.0 * (1 << 20))
+        mode = kSchedStreamK;
+      else if (tiles256 % kNumSMs != 0)
+        mode = kSchedHybrid;
+    }
+    return launch_any<kEpiResidual, float>(A, B, C, R, M, N, K, ldc, mode, s, weights_const);
   }
   if (c_dtype == MS_DTYPE_F32)
-    return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
-  return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, false, s, weights_const);
+    return launch_any<kEpiStore, float>(A, B, C, R, M, N, K, ldc, kSchedTiles, s, weights_const);
+  return launch_any<kEpiStore, __nv_bfloat16>(A, B, C, R, M, N, K, ldc, kSchedTiles, s,
+                                              weights_const);
 }
 
 }  // namespace ms

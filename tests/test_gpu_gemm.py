@@ -34,8 +34,12 @@ def policy(request):
     _lib.call("ms_gemm_set_policy", 0)
 
 
+# (1536, 4096, 8192) and (1500, 3328, 8192): more 256-wide tiles than SMs but not a
+# whole number of waves, and A + B over 64 MB, so the in-place residual runs whole
+# tiles, then stream-K over the rest
 SHAPES = [(1, 128, 64), (77, 256, 520), (128, 128, 2048), (300, 384, 200), (1280, 2560, 2048),
-          (256, 1024, 5632), (600, 512, 192), (1280, 2048, 5632), (2048, 2048, 2048)]
+          (256, 1024, 5632), (600, 512, 192), (1280, 2048, 5632), (2048, 2048, 2048),
+          (1536, 4096, 8192), (1500, 3328, 8192)]
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
