@@ -9,7 +9,9 @@ requests per GPU with contexts uniform in [512, 2048] (token ids uniform
 over the vocabulary, K/V pools filled with synthetic values), paged block
 16, gamma = 4, temperature 0.8, top-p 0.9.  One step = one speculative
 round over all requests (4 draft passes, one 5-token verify pass, fused
-accept/resample, rollback).
+accept/resample, rollback).  The K timed rounds run as several timed regions
+(``--repeats``, each after a fresh admission of the same contexts and a
+warm-up), so that at least 200 rounds are measured by default.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -66,6 +68,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--repeats", type=int, default=0,
+                    help="timed regions of --steps rounds per wave, each after a fresh "
+                         "admission and warm-up (0: enough for at least 200 timed rounds, at "
+                         "most 20; 1 with --total-requests)")
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--requests", type=int, default=256, help="requests per GPU (weak scaling)")
     ap.add_argument("--total-requests", type=int, default=0,
@@ -160,9 +166,13 @@ class ClockSampler:
             return False
 
     def start(self) -> None:
+        """Starts (or resumes) polling; samples accumulate over every
+        start/pause interval."""
         import threading
 
-        if not self._open():
+        if self._handle is None and not self._open():
+            return
+        if self._thread is not None and self._thread.is_alive():
             return
         nv, h = self._nvml, self._handle
         self._stop = threading.Event()
@@ -181,11 +191,15 @@ class ClockSampler:
         self._thread = threading.Thread(target=poll, daemon=True)
         self._thread.start()
 
+    def pause(self) -> None:
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+
     def stop(self) -> dict[str, object] | None:
         if self._thread is None:
             return None
-        self._stop.set()
-        self._thread.join(timeout=5)
+        self.pause()
         if not self.samples:
             return None
         nv = self._nvml
@@ -369,11 +383,16 @@ def run_gpu(args: argparse.Namespace) -> None:
     emitted = accepted = proposed = 0
     h2d = d2h = launches = 0
     dev_ms = e2e_ms = 0.0
+    # Several timed regions per wave (each after a fresh admission of the
+    # same contexts and its own warm-up), so the clock record covers a long
+    # stretch of rounds without the contexts growing past the workload's.
+    # The count depends on the arguments only, so every rank runs the same.
+    # Strong scaling already times every wave of its request set: once.
+    repeats = args.repeats or (1 if reqset.strong else
+                               max(1, min(20, -(-200 // max(1, args.steps)))))
     distributed.barrier()
     torch.cuda.synchronize(dev)
-    if clocks:
-        clocks.start()
-    for wave in waves:
+    for wave in [w for w in waves for _ in range(repeats)]:
         reqs, gens = admit(wave)
         for i in range(args.warmup):
             # A round's draft passes may be launched ahead by the round before
@@ -388,6 +407,8 @@ def run_gpu(args: argparse.Namespace) -> None:
             raise RuntimeError("the first timed round has no start event")
         launches0 = _lib.launch_count()
         torch.cuda.synchronize(dev)
+        if clocks:
+            clocks.start()
         start = torch.cuda.Event(enable_timing=True)
         end = torch.cuda.Event(enable_timing=True)
         start.record()
@@ -397,6 +418,8 @@ def run_gpu(args: argparse.Namespace) -> None:
             d2h += dec.last_d2h_bytes
         end.record()
         torch.cuda.synchronize(dev)
+        if clocks:
+            clocks.pause()
         launches += _lib.launch_count() - launches0
         e2e_ms += start.elapsed_time(end)
         dev_ms += sum(a.elapsed_time(b) for a, b in dec.round_events)
@@ -452,7 +475,7 @@ def run_gpu(args: argparse.Namespace) -> None:
     default_workload = (not args.small and not reqset.strong and args.model == "1b"
                         and args.requests == 256)
     weight_bytes_round = target.weight_bytes() + GAMMA * draft.weight_bytes()
-    rounds_timed = args.steps * len(waves)
+    rounds_timed = args.steps * len(waves) * repeats
     workload = WORKLOAD if not args.small else WORKLOAD + " [small: 2+1 layers]"
     if reqset.strong:
         workload = workload.replace(f"{args.requests} req/GPU",
@@ -464,6 +487,8 @@ def run_gpu(args: argparse.Namespace) -> None:
         "n_gpus": info.world_size,
         "steps": args.steps,
         "warmup": args.warmup,
+        "repeats": repeats,
+        "rounds_timed": rounds_timed,
         "ms_per_step": dev_ms_max * 1e3 / rounds_timed,
         "higher_is_better": True,
         "scaling": "strong" if reqset.strong else "weak",
