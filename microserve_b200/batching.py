@@ -51,6 +51,42 @@ class HostStaging:
         return self._dev[:n]
 
 
+    def upload_on(self, blob: np.ndarray, side: torch.cuda.Stream,
+                  after: torch.cuda.Event | None) -> torch.Tensor:
+        """Like :meth:`upload`, but the copy runs on ``side`` as soon as the
+        consuming (current) stream has passed ``after`` -- the point after
+        which nothing enqueued there reads the previous upload -- instead of
+        in the consuming stream's order.  The consuming stream waits for the
+        copy before its next work, so the copy overlaps the kernels enqueued
+        between ``after`` and now.  ``after=None``: the copy waits for
+        everything enqueued on the consuming stream so far."""
+        n = int(blob.size)
+        main = torch.cuda.current_stream(self.device)
+        if self._host is None or self._host.numel() < n:
+            # the buffers are replaced: nothing queued may still read the old ones
+            main.synchronize()
+            if self._copied is not None:
+                self._copied.synchronize()
+            cap = max(n, 1024, 2 * (0 if self._host is None else self._host.numel()))
+            self._host = torch.empty(cap, dtype=torch.int32, pin_memory=True)
+            self._dev = torch.empty(cap, dtype=torch.int32, device=self.device)
+        assert self._dev is not None
+        if self._copied is not None:
+            self._copied.synchronize()  # the previous copy out of the pinned buffer is done
+        self._host[:n].numpy()[:] = blob.reshape(-1)
+        if after is not None:
+            side.wait_event(after)
+        else:
+            side.wait_stream(main)
+        with torch.cuda.stream(side):
+            self._dev[:n].copy_(self._host[:n], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(side)
+        main.wait_event(done)
+        self._copied = done
+        return self._dev[:n]
+
+
 def pack_int32(parts: list[np.ndarray]) -> tuple[np.ndarray, list[tuple[int, int]]]:
     """Concatenate int32 arrays; return the blob and (offset, size) per part."""
     spans = []

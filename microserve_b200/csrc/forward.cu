@@ -135,16 +135,16 @@ extern "C" int ms_forward(const ms_model* model, const ms_kv_cache* cache, const
                            s, order));
     MS_TRY(gemm_dispatch(w.attn, m.w_o[l], w.x, w.x, T, d, hq * dh, 0, dt, MS_DTYPE_F32,
                          kEpiResidual, s, true));
-    MS_TRY(rmsnorm(w.x, m.ffn_norm[l], w.xn, nullptr, T, d, m.norm_eps, dt, s));
+    MS_TRY(rmsnorm(w.x, m.ffn_norm[l], w.xn, nullptr, T, d, m.norm_eps, dt, s, true));
     MS_TRY(gemm_dispatch(w.xn, m.w_gate_up[l], w.h, nullptr, T, 2 * m.d_ff, d, 0, dt, dt,
                          kEpiSwiGLU, s, true));
     MS_TRY(gemm_dispatch(w.h, m.w_down[l], w.x, w.x, T, d, m.d_ff, 0, dt, MS_DTYPE_F32,
                          kEpiResidual, s, true));
     if (l + 1 < m.n_layers)
-      MS_TRY(rmsnorm(w.x, m.attn_norm[l + 1], w.xn, nullptr, T, d, m.norm_eps, dt, s));
+      MS_TRY(rmsnorm(w.x, m.attn_norm[l + 1], w.xn, nullptr, T, d, m.norm_eps, dt, s, true));
   }
   if (R == 0) return MS_OK;
-  MS_TRY(rmsnorm(w.x, m.final_norm, w.xl, logit_rows, R, d, m.norm_eps, dt, s));
+  MS_TRY(rmsnorm(w.x, m.final_norm, w.xl, logit_rows, R, d, m.norm_eps, dt, s, true));
   MS_REQUIRE(logits_row_stride == 0 || logits_row_stride >= m.vocab_size,
              "ms_forward: logits_row_stride < vocab");
   return gemm_dispatch(w.xl, m.embed, logits, nullptr, R, m.vocab_size, d, logits_row_stride, dt,

@@ -40,13 +40,26 @@ constexpr int kVec = 8;  // float4 per thread -> dim up to 4096
 template <typename TY>
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_vec_kernel(const float* __restrict__ x, const float* __restrict__ w, TY* __restrict__ y,
-                       const int32_t* __restrict__ row_idx, int dim, float eps) {
-  pdl_enter();
+                       const int32_t* __restrict__ row_idx, int dim, float eps, int w_const) {
   __shared__ float red[kNormThreads / 32];
+  const int n4 = dim >> 2;
+  // Constant norm weights (a model's) are read while the kernel that writes
+  // x still runs, before the launch wait; other weights after it.
+  const float4* wr = reinterpret_cast<const float4*>(w);
+  float4 g[kVec];
+  auto load_w = [&]() {
+#pragma unroll
+    for (int k = 0; k < kVec; ++k) {
+      const int i = threadIdx.x + k * kNormThreads;
+      g[k] = i < n4 ? wr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (w_const) load_w();
+  pdl_enter();
+  if (!w_const) load_w();
   const int row = blockIdx.x;
   const int src = row_idx ? row_idx[row] : row;
   const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)src * dim);
-  const int n4 = dim >> 2;
   float4 v[kVec];
   float ss = 0.f;
 #pragma unroll
@@ -60,15 +73,13 @@ __global__ void __launch_bounds__(kNormThreads)
   __syncthreads();
   ss = red[0] + red[1] + red[2] + red[3];
   const float r = 1.f / sqrtf(ss / (float)dim + eps);
-  const float4* wr = reinterpret_cast<const float4*>(w);
   TY* yr = y + (int64_t)row * dim;
 #pragma unroll
   for (int k = 0; k < kVec; ++k) {
     const int i = threadIdx.x + k * kNormThreads;
     if (i >= n4) break;
-    const float4 g = wr[i];
-    const float a = v[k].x * r * g.x, b = v[k].y * r * g.y, c = v[k].z * r * g.z,
-                d = v[k].w * r * g.w;
+    const float a = v[k].x * r * g[k].x, b = v[k].y * r * g[k].y, c = v[k].z * r * g[k].z,
+                d = v[k].w * r * g[k].w;
     if constexpr (sizeof(TY) == 4) {
       reinterpret_cast<float4*>(yr)[i] = make_float4(a, b, c, d);
     } else {
@@ -368,7 +379,7 @@ __global__ void kv_gather_kernel(const int32_t* __restrict__ tables, int max_blo
 }  // namespace
 
 int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int n_rows, int dim,
-            float eps, int dtype, cudaStream_t s) {
+            float eps, int dtype, cudaStream_t s, bool w_const) {
   if (n_rows == 0) return MS_OK;
   ProfScope prof(kClsNorm, s);
   const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
@@ -376,10 +387,10 @@ int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int
   if (dim % 4 == 0 && dim <= 4 * kNormThreads * kVec && aligned) {
     if (dtype == MS_DTYPE_F32)
       launch_pdl(rmsnorm_vec_kernel<float>, n_rows, kNormThreads, 0, s, x, w, static_cast<float*>(y),
-                                                                row_idx, dim, eps);
+                 row_idx, dim, eps, w_const ? 1 : 0);
     else if (dtype == MS_DTYPE_BF16)
       launch_pdl(rmsnorm_vec_kernel<__nv_bfloat16>, n_rows, kNormThreads, 0, s,
-          x, w, static_cast<__nv_bfloat16*>(y), row_idx, dim, eps);
+          x, w, static_cast<__nv_bfloat16*>(y), row_idx, dim, eps, w_const ? 1 : 0);
     else
       return fail(MS_ERR_UNSUPPORTED, "rmsnorm: dtype %d", dtype);
     return check_launch("rmsnorm_vec_kernel");

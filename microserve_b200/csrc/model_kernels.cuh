@@ -4,8 +4,10 @@
 
 namespace ms {
 
+// w_const: w holds a model's weights, which no kernel on the stream writes
+// (the kernel reads it before waiting for its predecessor).
 int rmsnorm(const float* x, const float* w, void* y, const int32_t* row_idx, int n_rows, int dim,
-            float eps, int dtype, cudaStream_t s);
+            float eps, int dtype, cudaStream_t s, bool w_const = false);
 int embed_rmsnorm(const void* embed, const int32_t* ids, int n_tokens, int vocab, int dim,
                   const float* w, float eps, float* x, void* y, int dtype, cudaStream_t s);
 int rope_kv_write(void* qkv, const int32_t* positions, const int32_t* slots, const float* cos_t,

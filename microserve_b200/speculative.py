@@ -199,6 +199,7 @@ class _RoundPlan:
     chain_span: int = -1
     chain_dw: int = 0
     dev_blob_v: torch.Tensor | None = None
+    v_slot: int = 0  # which of the decoder's two verify-blob buffers holds it
     target_cache: PagedKVCache | None = None
 
 
@@ -268,7 +269,18 @@ class SpeculativeDecoder:
         self.num_accepted = 0
         self._staging = HostStaging(self.device)
         self._staging_d = HostStaging(self.device)  # later draft passes, verify ids, params
-        self._staging_v = HostStaging(self.device)  # the verify batch's blob (phase B)
+        # The verify batch's blob (phase B), in two buffers used alternately:
+        # a round's blob goes up on a copy stream while its draft passes run.
+        # Its readers are that round's verify and accept kernels and, when
+        # the next round is chained, the next round's chain plan and draft
+        # passes (whose block tables it holds); `_v_free[k]` is recorded on
+        # the current stream after the last of them was enqueued, and the
+        # next upload into buffer k waits for it.
+        self._staging_v = [HostStaging(self.device), HostStaging(self.device)]
+        self._v_slot = 0
+        self._v_free: list[torch.cuda.Event | None] = [None, None]
+        self._copy_stream = torch.cuda.Stream(self.device)
+        self._v_fence = torch.zeros(1, device=self.device)
         self._buf = _Buffers(self.device)
         self.last_round_launches = 0
         self._row_cache: tuple | None = None  # see _rows_for
@@ -395,6 +407,7 @@ class SpeculativeDecoder:
             _lib.call("ms_sample", out.data_ptr(), V, B, V, params.data_ptr(), None,
                       _lib.LANE_DRAFT + j, buf.proposals[j].data_ptr(), None,
                       buf.dstats[j].data_ptr(), idsv.data_ptr(), scat[j].data_ptr(), stream)
+        self._release_blob_v(plan)  # the draft passes read their block tables from it
         return _Lookahead(
             ids=tuple(plan.ids), requests=plan.requests, gens=plan.gens, configs=plan.configs,
             samplings=[r.sampling for r in plan.requests],
@@ -735,8 +748,15 @@ class SpeculativeDecoder:
         buf = self._buf
         stream = _lib.stream_ptr(self.device)
         self._plan_verify(plan, target_cache, chain)
-        vblob = self._staging_v.upload(plan.blob_v)
+        k = self._v_slot
+        self._v_slot ^= 1
+        vblob = self._staging_v[k].upload_on(plan.blob_v, self._copy_stream, self._v_free[k])
+        # A kernel launched without programmatic serialisation after the wait
+        # for the copy: the verify pass's first kernel then overlaps this
+        # one only, never the copy.
+        self._v_fence.zero_()
         plan.dev_blob_v = vblob
+        plan.v_slot = k
         w = [vblob[o : o + n] for o, n in plan.spans_v]
         tw = plan.tw
         bv = PagedBatch(
@@ -766,9 +786,16 @@ class SpeculativeDecoder:
             buf.dstats.data_ptr(), 0, buf.proposals.data_ptr(), plan.dev_params.data_ptr(), B,
             G, V, buf.out.data_ptr(), buf.out[B * (G + 1) :].data_ptr(), stream,
         )
+        self._release_blob_v(plan)
         if ev is not None and self.round_events is not None:
             ev[1].record()
             self.round_events.append(ev)
+
+    def _release_blob_v(self, plan: _RoundPlan) -> None:
+        """Every reader of the round's verify blob has been enqueued."""
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.device))
+        self._v_free[plan.v_slot] = done
 
     def _finish(
         self,
