@@ -98,6 +98,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--qlen", type=int, default=5, help="--micro attention: query tokens per sequence")
     ap.add_argument("--dh", type=int, default=64, choices=[64, 128], help="--micro attention: head size")
     ap.add_argument("--iters", type=int, default=20, help="--micro: timed launches")
+    ap.add_argument("--timeline", action="store_true",
+                    help="1 GPU: record every kernel of the run with torch.profiler (CUPTI) and "
+                         "print each timed round's live time per kernel as a second JSON line")
     ap.add_argument("--gemm-policy", type=int, default=0, choices=[0, 1, 2],
                     help="tensor-core GEMM kernel: 0 by shape, 1 one CTA per tile, 2 CTA pairs")
     return ap.parse_args()
@@ -1152,8 +1155,62 @@ def main() -> None:
         run_micro(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.timeline:
+        run_timeline(args)
     else:
         run_gpu(args)
+
+
+def run_timeline(args: argparse.Namespace) -> None:
+    """The GPU arm under torch.profiler's CUDA activity records: each timed
+    round's span, idle time and per-kernel live time.  With programmatic
+    dependent launch a kernel starts while its predecessor still runs, so a
+    kernel's live time is counted from the later of its start and the end
+    of every kernel before it (the sum over a round is its busy time).  A
+    round ends with its accept kernel.  The first timed round is left out:
+    it also holds the host synchronisation between the warm-up and the timed
+    rounds.  Timing under the profiler is not a bench value; the breakdown
+    is what this is for."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        raise SystemExit("--timeline runs on one GPU")
+    args.repeats = 1
+    with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
+        run_gpu(args)
+        torch.cuda.synchronize()
+    ev = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+                if e.device_type.name == "CUDA" and e.name
+                and "Memcpy" not in e.name and "Memset" not in e.name)
+    ends = [i for i, (_, _, n) in enumerate(ev) if "spec_accept" in n]
+
+    def short(n: str) -> str:
+        n = n.replace("(anonymous namespace)::", "").replace("void ", "").replace("ms::", "")
+        return n.split("(")[0][:60]
+
+    per: dict[str, list[float]] = {}
+    spans, idles = [], []
+    timed = range(args.warmup + 1, min(args.warmup + args.steps, len(ends)))
+    for r in timed:
+        seg = ev[ends[r - 1] + 1 : ends[r] + 1] if r else ev[: ends[0] + 1]
+        prev_end, idle = seg[0][0], 0.0
+        for s_, e_, n in seg:
+            idle += max(0.0, s_ - prev_end)
+            slot = per.setdefault(short(n), [0, 0.0])
+            slot[0] += 1
+            slot[1] += max(0.0, e_ - max(prev_end, s_))
+            prev_end = max(prev_end, e_)
+        spans.append(seg[-1][1] - seg[0][0])
+        idles.append(idle)
+    n = max(1, len(spans))
+    print(json.dumps({
+        "timeline": "live time per kernel and timed round (torch.profiler CUDA activities)",
+        "rounds": len(spans), "round_us": sum(spans) / n, "idle_us": sum(idles) / n,
+        "round_us_each": [round(x, 1) for x in spans], "idle_us_each": [round(x, 1) for x in idles],
+        "kernels": {k: {"launches": c / n, "us": t / n, "share": t / max(1e-9, sum(spans))}
+                    for k, (c, t) in sorted(per.items(), key=lambda x: -x[1][1])},
+    }), flush=True)
 
 
 if __name__ == "__main__":
