@@ -391,6 +391,43 @@ __device__ __forceinline__ void rope_row_load(const RopeKv& rk, int m, int M, in
   }
 }
 
+// Writes a head's staged 32-row slice (exchange chunks 0-3: columns j ..
+// j + 31 of the head's first half, 4-7: the same of its second half) to q's
+// rows of the qkv buffer or to the cache at each row's slot; every lane
+// stores whole 16-byte chunks, four rows per warp instruction.
+// `crow`: this lane's row in the cache pool for kv head 0, block * hkv * bs +
+// offset in block (-1: no valid slot).  q heads need no slot, so their
+// rows skip the shuffle (the branch is uniform over the warp).
+__device__ __forceinline__ void rope_store_rows(uint32_t buf, int lane, int row0, int M, int n0,
+                                                int hc, int head, int j, int crow,
+                                                const RopeKv& rk, __nv_bfloat16* qkv,
+                                                int64_t ldc) {
+  const int dh = rk.dh, half = dh >> 1;
+  const int jj = lane & 7;
+  const int col = jj < 4 ? j + 8 * jj : half + j + 8 * (jj - 4);
+  if (head < rk.hq) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3);
+      const uint4 x = staged_chunk(buf, r, jj);
+      const int mr = row0 + r;
+      if (mr < M) *reinterpret_cast<uint4*>(qkv + (int64_t)mr * ldc + n0 + hc + col) = x;
+    }
+    return;
+  }
+  const bool is_k = head < rk.hq + rk.hkv;
+  const int kh = head - rk.hq - (is_k ? 0 : rk.hkv);
+  __nv_bfloat16* pool = (is_k ? rk.kpool : rk.vpool) + (int64_t)kh * rk.bs * dh + col;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const uint4 x = staged_chunk(buf, r, jj);
+    const int crow_r = __shfl_sync(0xffffffffu, crow, r);
+    if (row0 + r >= M || crow_r < 0) continue;
+    *reinterpret_cast<uint4*>(pool + (int64_t)crow_r * dh) = x;
+  }
+}
+
 template <int BN>
 __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int lane, int row0,
                                              int M, int n0, int half_warps, const RopeKv& rk,
@@ -400,7 +437,10 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
   const int m = row0 + lane;
   const bool live = m < M;
   const int pos = rr.pos, slot = rr.slot;
-  const bool slot_ok = slot >= 0 && slot / rk.bs < rk.num_blocks;
+  const int blk = slot >= 0 ? slot / rk.bs : 0;
+  const bool slot_ok = slot >= 0 && blk < rk.num_blocks;
+  // the row's place in the pool (num_blocks, hkv, bs, dh) for kv head 0
+  const int crow = slot_ok ? blk * rk.hkv * rk.bs + (slot - blk * rk.bs) : -1;
   // d_head 128: cos/sin of the row's position read as float4 per head
   const float* cos_row = rk.cos_t + (int64_t)pos * half;
   const float* sin_row = rk.sin_t + (int64_t)pos * half;
@@ -466,30 +506,7 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
       }
       if (live && head >= rk.hq && !slot_ok) raise_device_error(err, kErrSlot);
       __syncwarp();
-      const int jj = lane & 7;
-      // chunks 0-3: columns j + 8 jj of the first half; 4-7: the second half
-      const int col = jj < 4 ? j + 8 * jj : half + j + 8 * (jj - 4);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int r = 4 * i + (lane >> 3);
-        const uint4 x = staged_chunk(buf, r, jj);
-        const int slot_r = __shfl_sync(0xffffffffu, slot, r);
-        const int mr = row0 + r;
-        if (mr >= M) continue;
-        __nv_bfloat16* dst;
-        if (head < rk.hq) {
-          dst = qkv + (int64_t)mr * ldc + n0 + hc + col;
-        } else {
-          const int blk = slot_r >= 0 ? slot_r / rk.bs : 0;
-          if (slot_r < 0 || blk >= rk.num_blocks) continue;
-          const int off = slot_r - blk * rk.bs;
-          const bool is_k = head < rk.hq + rk.hkv;
-          const int kh = head - rk.hq - (is_k ? 0 : rk.hkv);
-          dst = (is_k ? rk.kpool : rk.vpool) +
-                (((int64_t)blk * rk.hkv + kh) * rk.bs + off) * dh + col;
-        }
-        *reinterpret_cast<uint4*>(dst) = x;
-      }
+      rope_store_rows(buf, lane, row0, M, n0, hc, head, j, crow, rk, qkv, ldc);
       __syncwarp();
     }
   }
