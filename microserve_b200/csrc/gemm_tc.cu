@@ -476,11 +476,24 @@ __device__ __forceinline__ void rope_kv_rows(uint32_t base, uint32_t buf, int la
               }
             }
             const float cc[4] = {cv.x, cv.y, cv.z, cv.w}, ss[4] = {sv.x, sv.y, sv.z, sv.w};
+            // the accumulators rounded to bf16 two at a time (each element
+            // rounds to nearest on its own, as the one-value conversion does)
+            float pv[4], qv[4];
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+              const float2 pa = __bfloat1622float2(__floats2bfloat162_rn(a[4 * i4 + e],
+                                                                         a[4 * i4 + e + 1]));
+              const float2 qb = __bfloat1622float2(__floats2bfloat162_rn(b[4 * i4 + e],
+                                                                         b[4 * i4 + e + 1]));
+              pv[e] = pa.x;
+              pv[e + 1] = pa.y;
+              qv[e] = qb.x;
+              qv[e + 1] = qb.y;
+            }
             float r1[4], r2[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              const float p = __bfloat162float(__float2bfloat16_rn(a[4 * i4 + e]));
-              const float q = __bfloat162float(__float2bfloat16_rn(b[4 * i4 + e]));
+              const float p = pv[e], q = qv[e];
               r1[e] = p * cc[e] - q * ss[e];
               r2[e] = q * cc[e] + p * ss[e];
             }
