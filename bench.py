@@ -1180,37 +1180,47 @@ def run_timeline(args: argparse.Namespace) -> None:
     with profile(activities=[ProfilerActivity.CUDA], acc_events=True) as prof:
         run_gpu(args)
         torch.cuda.synchronize()
-    ev = sorted((e.time_range.start, e.time_range.end, e.name) for e in prof.events()
-                if e.device_type.name == "CUDA" and e.name
-                and "Memcpy" not in e.name and "Memset" not in e.name)
+    ev = [(e.time_range.start, e.time_range.end, e.name) for e in prof.events()
+          if e.device_type.name == "CUDA" and e.name
+          and "Memcpy" not in e.name and "Memset" not in e.name]
+    print(json.dumps(timeline_summary(ev, args.warmup + 1, args.warmup + args.steps)),
+          flush=True)
+
+
+def _short_kernel_name(n: str) -> str:
+    n = n.replace("(anonymous namespace)::", "").replace("void ", "").replace("ms::", "")
+    return n.split("(")[0][:60]
+
+
+def timeline_summary(events: list[tuple[float, float, str]], first: int, stop: int) -> dict:
+    """Rounds ``first`` .. ``stop - 1`` (0-based, a round ending with its
+    accept kernel) of a kernel list ``(start, end, name)`` in microseconds:
+    each round's span and idle time, and each kernel's live time, counted
+    from the later of its own start and the end of every kernel before it
+    (kernels that start early and wait for their predecessor overlap it)."""
+    ev = sorted(events)
     ends = [i for i, (_, _, n) in enumerate(ev) if "spec_accept" in n]
-
-    def short(n: str) -> str:
-        n = n.replace("(anonymous namespace)::", "").replace("void ", "").replace("ms::", "")
-        return n.split("(")[0][:60]
-
     per: dict[str, list[float]] = {}
     spans, idles = [], []
-    timed = range(args.warmup + 1, min(args.warmup + args.steps, len(ends)))
-    for r in timed:
+    for r in range(first, min(stop, len(ends))):
         seg = ev[ends[r - 1] + 1 : ends[r] + 1] if r else ev[: ends[0] + 1]
         prev_end, idle = seg[0][0], 0.0
         for s_, e_, n in seg:
             idle += max(0.0, s_ - prev_end)
-            slot = per.setdefault(short(n), [0, 0.0])
+            slot = per.setdefault(_short_kernel_name(n), [0, 0.0])
             slot[0] += 1
             slot[1] += max(0.0, e_ - max(prev_end, s_))
             prev_end = max(prev_end, e_)
         spans.append(seg[-1][1] - seg[0][0])
         idles.append(idle)
     n = max(1, len(spans))
-    print(json.dumps({
+    return {
         "timeline": "live time per kernel and timed round (torch.profiler CUDA activities)",
         "rounds": len(spans), "round_us": sum(spans) / n, "idle_us": sum(idles) / n,
         "round_us_each": [round(x, 1) for x in spans], "idle_us_each": [round(x, 1) for x in idles],
         "kernels": {k: {"launches": c / n, "us": t / n, "share": t / max(1e-9, sum(spans))}
                     for k, (c, t) in sorted(per.items(), key=lambda x: -x[1][1])},
-    }), flush=True)
+    }
 
 
 if __name__ == "__main__":
