@@ -50,7 +50,7 @@ constexpr long long kWaitCycles = 1ll << 32;  // ~2.2 s at 1.965 GHz
 constexpr int kErrTimeout = 5;
 
 template <int BN> struct TileCfg {
-  static constexpr int kStages = BN == 128 ? 6 : 4;
+  static constexpr int kStages = BN == 64 ? 8 : (BN == 128 ? 6 : 4);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -1187,6 +1187,13 @@ int gemm_qkv_rope(const void* A, const void* W, void* qkv, int M, int N, int K, 
   if (use_bn256(M, N, false))
     return launch_tc<256, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, kSchedTiles,
                                                      s, rk, weights_const);
+  // Few rows (a draft pass: M 256 gives 40 tiles of 128 columns, each CTA
+  // streaming 1 MB of operands through a feed-bound k-loop): one head of 64
+  // columns per tile while that still fits in one wave, so twice the CTAs
+  // share the operand feed.
+  if (rk.dh == 64 && ((M + BM - 1) / BM) * (N / 64) <= kNumSMs)
+    return launch_tc<64, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, kSchedTiles,
+                                                    s, rk, weights_const);
   return launch_tc<128, kEpiRopeKV, __nv_bfloat16>(A, W, qkv, nullptr, M, N, K, N, kSchedTiles, s,
                                                    rk, weights_const);
 }
