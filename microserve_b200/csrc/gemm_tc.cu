@@ -3,23 +3,27 @@
 //
 // Grid: one CTA per SM (at most), 320 threads:
 //   warp 0 lane 0  TMA producer: K-major 128B-swizzled A (128 x 64) and B
-//                  (BN x 64) tiles into a STAGES-deep shared-memory ring;
+//                  (BN x 64, BN 64, 128 or 256) tiles into a 4-8 deep
+//                  shared-memory ring;
 //   warp 1         allocates 2 x BN TMEM columns (a double-buffered
 //                  accumulator); lane 0 issues tcgen05.mma.cta_group::1
 //                  .kind::f16 (M=128, N=BN, K=16), commits each stage back to
 //                  the producer and each finished accumulator to the epilogue;
 //   warps 2-9      epilogue: tcgen05.ld 32x32b (warp w reads TMEM lanes
 //                  32*(w%4)..+31 = tile rows; warps w and w+4 split the
-//                  columns), fused store / SwiGLU / residual reduction
-//                  through a shared-memory exchange that makes every global
-//                  access whole 128-byte row segments, while the MMA warp
-//                  fills the other accumulator.
+//                  columns), fused store / SwiGLU / residual / RoPE with
+//                  the k, v cache write, through a shared-memory exchange
+//                  that makes every global access whole 128-byte row
+//                  segments, while the MMA warp fills the other accumulator.
 // Work: output tiles are dealt round-robin to the CTAs; for the in-place
 // residual GEMM (C += A B^T, R == C) the (tile, k-step) space is instead cut
-// into equal contiguous ranges (stream-K), and every piece is added into C
-// with red.global.add, so small grids (o_proj/down at 1280 tokens: 80 tiles)
-// keep every SM busy.  Partial sums then land in C in a hardware-chosen
-// order, so those outputs can differ run to run by float rounding.
+// into equal contiguous ranges (stream-K) when the tiles are fewer than the
+// SMs or A + B fit in L2, or whole tiles go first and only the tiles after
+// the last full wave are cut (hybrid).  A piece that is a whole tile writes
+// R + acc; a partial one is added into C with red.global.add, so small grids
+// (o_proj/down at 1280 tokens: 80 tiles) keep every SM busy.  Partial sums
+// then land in C in a hardware-chosen order, so those outputs can differ run
+// to run by float rounding.
 // A CTA's setup (barriers, TMEM) and, when B is constant (the forward's
 // weights), its first stages' B loads run before the wait for the previous
 // launch, so a CTA placed while that launch's last CTAs still run starts
